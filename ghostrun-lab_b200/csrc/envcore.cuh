@@ -1,0 +1,662 @@
+// Decision semantics on the device: controller (moves, sticky repeats, dropout schedule), reward10, episode ends and
+// restarts, and the kernels that run them. Behaviour follows rl/csrc/rlenv_core.cuh:138-414 (phases),
+// rl/csrc/controller.cuh:41-187 (controller) and rl/csrc/reward10.cuh:546-632 (RewardTracker.update).
+//
+// Kernels of one decision (per game slice, one stream):
+//   k_frames<B>(decision)  thread per env: 4 x (pad byte, one emulated frame into presentation slot f)
+//   k_render<B>            warp per (env, frame): the 4 observations
+//   k_finish               thread per env: reward, outputs, episode end -> restart from a snapshot record,
+//                          restarting envs appended to a list; masks/timeline for the others
+//   k_frames<B>(restart)   grid-stride over the list: idle frames + 4 neutral frames, first tracker update, controls
+//   k_render<B>(list)      the restarted envs' first observation
+// The reward arithmetic is double in Python's order; the library is built with -fmad=false (no fused a*b+c).
+#pragma once
+#include "render.cuh"
+
+namespace gr {
+
+// ------------------------------------------------------------------------------------------------ controller
+
+__device__ __forceinline__ u32 dpad_bits(u32 d) {
+    // 0 none, 1 Up, 2 Up-Right, 3 Right, 4 Down-Right, 5 Down, 6 Down-Left, 7 Left, 8 Up-Left
+    // pad bits: 4 Up, 5 Down, 6 Left, 7 Right
+    switch (d) {
+        case 1: return 0x10u; case 2: return 0x90u; case 3: return 0x80u; case 4: return 0xA0u;
+        case 5: return 0x20u; case 6: return 0x60u; case 7: return 0x40u; case 8: return 0x50u;
+        default: return 0u;
+    }
+}
+__device__ __forceinline__ u32 dpad_from_bits(u32 b) {
+    for (u32 d = 0; d < 9; ++d) if (dpad_bits(d) == b) return d;
+    return 0;
+}
+struct Move { u32 dpad, a, b, start, select; };
+__device__ __forceinline__ Move unpack_move(int id) {
+    Move m;
+    m.dpad = id % 9; id /= 9;
+    m.a = id % 3; id /= 3;
+    m.b = id % 3; id /= 3;
+    m.start = id % 2; id /= 2;
+    m.select = id % 2;
+    return m;
+}
+__device__ __forceinline__ int pack_move(Move m) {
+    return static_cast<int>(m.dpad + 9 * (m.a + 3 * (m.b + 3 * (m.start + 2 * m.select))));
+}
+__device__ __forceinline__ u32 pad_byte(Move m, u64 frame) {
+    const bool even = (frame & 1u) == 0;
+    u32 p = dpad_bits(m.dpad);
+    if (m.a == 1 || (m.a == 2 && even)) p |= 1u;
+    if (m.b == 1 || (m.b == 2 && even)) p |= 2u;
+    if (m.start) p |= 8u;
+    if (m.select) p |= 4u;
+    return p;
+}
+__device__ __forceinline__ Move restrict_move(Move m, int dropped, bool start_ok, bool select_ok) {
+    u32 bits = dpad_bits(m.dpad);
+    if (dropped >= 0 && dropped < 4) bits &= ~(0x10u << dropped);
+    m.dpad = dpad_from_bits(bits);
+    if ((dropped == 4 && m.a == 1) || (dropped == 6 && m.a == 2)) m.a = 0;
+    if ((dropped == 5 && m.b == 1) || (dropped == 7 && m.b == 2)) m.b = 0;
+    if (!start_ok) m.start = 0;
+    if (!select_ok) m.select = 0;
+    return m;
+}
+__device__ __forceinline__ u64 splitmix64(u64 x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+__device__ __forceinline__ u32 rand_u32(u64 seed, u64& ctr) { return static_cast<u32>(splitmix64(seed ^ splitmix64(ctr++)) >> 32); }
+__device__ __forceinline__ u32 rand_below(u64 seed, u64& ctr, u32 n) {
+    return static_cast<u32>((static_cast<u64>(rand_u32(seed, ctr)) * n) >> 32);
+}
+constexpr u32 kGapP32 = 122713351u, kSticky32 = 0x40000000u;
+
+__device__ __forceinline__ i32 draw_gap(Dropout& s) { i32 k = 1; while (rand_u32(s.seed, s.counter) >= kGapP32) ++k; return k; }
+__device__ __forceinline__ int next_column(Dropout& s) {
+    if (s.drop_left > 0) {
+        const int out = s.drop_input;
+        if (--s.drop_left == 0) s.gap_left = draw_gap(s);
+        return out;
+    }
+    if (--s.gap_left == 0) {
+        s.drop_input = static_cast<i32>(rand_below(s.seed, s.counter, kDropInputs));
+        s.drop_left = 8 + static_cast<i32>(rand_below(s.seed, s.counter, 15));
+    }
+    return -1;
+}
+static __device__ void dropout_reset(Dropout& s, u64 seed, bool enabled) {
+    s.seed = seed; s.counter = 0; s.drop_left = 0; s.drop_input = -1; s.head = 0;
+    s.gap_left = enabled ? draw_gap(s) : 0x7FFFFFFF;
+    for (int j = 0; j < kRing; ++j) s.ring[j] = -1;
+    for (int j = 0; j < kTimeline; ++j) s.ring[j] = static_cast<int8_t>(enabled ? next_column(s) : -1);
+}
+__device__ __forceinline__ int dropped_now(const Dropout& s) { return s.ring[s.head % kRing]; }
+static __device__ void dropout_advance(Dropout& s, bool enabled) {
+    s.ring[s.head % kRing] = -1;
+    ++s.head;
+    s.ring[(s.head + kTimeline - 1) % kRing] = static_cast<int8_t>(enabled ? next_column(s) : -1);
+}
+
+// ------------------------------------------------------------------------------------------------ reward10
+
+struct Sig {
+    bool in_play, progress_valid, dying, has_lives, has_health, has_score, game_over, won;
+    int level, lives;
+    double progress, health;
+    long long score;
+};
+
+// The synthetic template's RAM -> Signals ($10-$11 progress, $12 level, $13 lives, $14-$16 BCD score, $17 mode).
+static __device__ Sig observe_synth(const StateView& S, u32 e) {
+    const u8* r8 = reinterpret_cast<const u8*>(S.ram);
+    auto rb = [&](u32 a) -> u32 { return r8[((static_cast<u64>(a >> 2) * S.Np + e) << 2) | (a & 3u)]; };
+    const u32 w10 = S.ram[static_cast<u64>(0x10 >> 2) * S.Np + e];   // $10-$13
+    const u32 w14 = S.ram[static_cast<u64>(0x14 >> 2) * S.Np + e];   // $14-$17
+    (void)rb;
+    Sig s;
+    const u32 mode = w14 >> 24;
+    s.in_play = mode == 1;
+    s.level = static_cast<int>((w10 >> 16) & 0xFFu);
+    s.progress = static_cast<double>(w10 & 0xFFFFu);
+    s.progress_valid = mode == 1;
+    s.dying = false;
+    s.has_lives = true; s.lives = static_cast<int>(w10 >> 24);
+    s.has_health = false; s.health = 0.0;
+    s.has_score = true;
+    long long v = 0;
+    for (int k = 0; k < 3; ++k) { const u32 b = (w14 >> (8 * k)) & 0xFFu; v = v * 100 + (b >> 4) * 10 + (b & 15u); }
+    s.score = v;
+    s.game_over = mode == 2;
+    s.won = false;
+    return s;
+}
+
+struct Upd { double reward; bool done; u32 events; int event_level; double part[kParts]; };
+enum : u32 { kEvSkip = 1, kEvLevel = 2, kEvDeath = 4, kEvWon = 8, kEvGameOver = 16, kEvStall = 32, kEvRollback = 64 };
+
+static __device__ Upd reward_update(const Spec& G, const Sig& s, int frames, Tracker& e) {
+    const bool has_p = e.has_prev != 0;
+    Sig p;
+    p.in_play = e.prev_in_play; p.progress_valid = e.prev_progress_valid; p.dying = e.prev_dying;
+    p.has_lives = e.prev_has_lives; p.has_health = e.prev_has_health; p.has_score = e.prev_has_score;
+    p.game_over = e.prev_game_over; p.won = e.prev_won; p.level = e.prev_level; p.lives = e.prev_lives;
+    p.progress = e.prev_progress; p.health = e.prev_health; p.score = e.prev_score;
+    e.has_prev = 1;
+    e.prev_in_play = s.in_play; e.prev_progress_valid = s.progress_valid; e.prev_dying = s.dying;
+    e.prev_has_lives = s.has_lives; e.prev_has_health = s.has_health; e.prev_has_score = s.has_score;
+    e.prev_game_over = s.game_over; e.prev_won = s.won; e.prev_level = s.level; e.prev_lives = s.lives;
+    e.prev_progress = s.progress; e.prev_health = s.health; e.prev_score = s.score;
+    Upd out;
+    out.reward = 0.0; out.done = true; out.events = 0; out.event_level = 0;
+    for (int k = 0; k < kParts; ++k) out.part[k] = 0.0;
+    if (e.done) return out;
+    double r = 0.0, pt[kParts] = {0, 0, 0, 0, 0, 0, 0};
+    u32 ev = 0;
+    int ev_level = 0;
+    bool fresh = false;
+    if (s.in_play) {
+        if (!e.has_best_level) {
+            e.has_best_level = 1; e.best_level = s.level; e.has_best_progress = 0; e.score_used = 0.0;
+        } else if (s.level > e.best_level + 1) {
+            ev |= kEvSkip; ev_level = s.level; e.done = 1; e.end_reason = 3;
+        } else if (s.level > e.best_level) {
+            r = __dadd_rn(r, G.w_level); pt[1] = __dadd_rn(pt[1], G.w_level);
+            ev |= kEvLevel; ev_level = s.level;
+            e.best_level = s.level; e.has_best_progress = 0; e.score_used = 0.0;
+            fresh = true;
+        }
+        if (s.level == e.best_level && s.progress_valid) {
+            if (!e.has_best_progress) {
+                e.has_best_progress = 1; e.best_progress = s.progress;
+            } else if (s.progress > e.best_progress) {
+                const double rp = __ddiv_rn(__dmul_rn(G.w_progress, __dsub_rn(s.progress, e.best_progress)), G.progress_unit);
+                r = __dadd_rn(r, rp); pt[0] = __dadd_rn(pt[0], rp);
+                e.best_progress = s.progress;
+                fresh = true;
+            }
+        }
+    }
+    bool death = false;
+    if (has_p) {
+        if (G.death_from_lives == 0.0) death = s.dying && !p.dying;
+        else death = s.has_lives && p.has_lives && s.lives < p.lives;
+        if (death && (s.in_play || p.in_play)) {
+            r = __dadd_rn(r, G.w_death); pt[2] = __dadd_rn(pt[2], G.w_death);
+            e.deaths += 1;
+            ev |= kEvDeath;
+            fresh = true;
+        }
+        if (s.in_play && p.in_play && s.has_health && p.has_health && s.health < p.health) {
+            const double rd = __dmul_rn(G.w_damage, __dsub_rn(p.health, s.health));
+            r = __dadd_rn(r, rd); pt[3] = __dadd_rn(pt[3], rd);
+        }
+        if (s.in_play && p.in_play && s.has_score && p.has_score && s.score > p.score) {
+            double sr = __ddiv_rn(__dmul_rn(G.w_score, static_cast<double>(s.score - p.score)), G.score_unit);
+            if (G.score_cap < sr) sr = G.score_cap;
+            const double left = __dsub_rn(G.score_level_budget, e.score_used);
+            if (left < sr) sr = left;
+            if (sr > 0) { r = __dadd_rn(r, sr); pt[4] = __dadd_rn(pt[4], sr); e.score_used = __dadd_rn(e.score_used, sr); }
+        }
+    }
+    if (has_p && !e.done && !death && !s.dying && !p.dying && !s.won && !s.game_over && s.in_play && p.in_play &&
+        s.progress_valid && p.progress_valid && s.level == p.level && s.level == e.best_level &&
+        __dsub_rn(p.progress, s.progress) >= __dmul_rn(G.rollback_drop, G.progress_unit)) {
+        r = __dadd_rn(r, G.w_rollback); pt[6] = __dadd_rn(pt[6], G.w_rollback);
+        ev |= kEvRollback;
+    }
+    if (!fresh && !e.done && has_p && s.in_play && p.in_play && s.progress_valid && p.progress_valid &&
+        s.progress <= p.progress) {
+        const double ci = __dmul_rn(G.idle_per_frame, static_cast<double>(frames));
+        r = __dadd_rn(r, ci); pt[6] = __dadd_rn(pt[6], ci);
+    }
+    e.idle_frames = (fresh || !has_p) ? 0 : e.idle_frames + frames;
+    if (s.won) {
+        r = __dadd_rn(r, G.w_win); pt[5] = __dadd_rn(pt[5], G.w_win);
+        ev |= kEvWon; e.done = 1; e.end_reason = 2;
+    } else if (s.game_over) {
+        ev |= kEvGameOver; e.done = 1; e.end_reason = 1;
+    } else if (!e.done && G.stall_frames >= 0.0 && static_cast<double>(e.idle_frames) >= G.stall_frames) {
+        r = __dadd_rn(r, G.w_stall); pt[6] = __dadd_rn(pt[6], G.w_stall);
+        ev |= kEvStall; e.done = 1; e.end_reason = 4;
+    }
+    out.reward = r; out.done = e.done != 0; out.events = ev; out.event_level = ev_level;
+    for (int k = 0; k < kParts; ++k) out.part[k] = pt[k];
+    return out;
+}
+
+// ------------------------------------------------------------------------------------------------ env arrays
+
+struct GameArgs {   // one game slice
+    CartView cart;
+    Spec spec;
+    u32 e0, n;                 // global env range
+    const u8* recs;            // snapshot records: [1 + idle_tmpl][kRecBytes] (boot first)
+    u32 idle_tmpl;
+    u64 tmpl_target;
+    u32 start_ok, select_ok;
+};
+
+struct EnvArgs {
+    StateView st;
+    // per env (global index)
+    Tracker* trk;
+    Dropout* drop;
+    u64* target;
+    u32* ep_frame;
+    int16_t* prev_applied;
+    u64* sticky_seed;
+    u64* sticky_ctr;
+    u32* episode;
+    float* ep_ret;
+    i32* ep_len;
+    i32* ep_maxlvl;
+    i32* ep_idle;
+    u32* fault;
+    u8* resetting;
+    // restart list
+    u32* list;
+    u32* list_count;
+    // caller buffers
+    const int16_t* actions;
+    u8* obs; u8* emph; float* reward; u8* done; u8* masks; u8* timeline; u8* pads; u32* events; float* info;
+    float* parts;
+    u64 run_seed;
+    i32 sticky, idle_max, dropout, no_render, episode_level_end;
+};
+
+// ------------------------------------------------------------------------------------------------ records
+
+// env slot <- record (whole console state; the record's frozen frame goes to presentation slot 0)
+static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, bool chr_ram) {
+    const u32* rr = reinterpret_cast<const u32*>(rec + kRecRegs);
+    for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = rr[w];
+    S.regs[static_cast<u64>(R_FSLOT) * S.Np + e] = 0;
+    const u32* ram = reinterpret_cast<const u32*>(rec + kRecRam);
+    for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * S.Np + e] = ram[i];
+    const u32* pr = reinterpret_cast<const u32*>(rec + kRecPrgRam);
+    for (u32 i = 0; i < kPrgRamWords; ++i) S.prg_ram[static_cast<u64>(i) * S.Np + e] = pr[i];
+    auto cp = [](u8* d, const u8* s, u32 n) {
+        uint4* dv = reinterpret_cast<uint4*>(d);
+        const uint4* sv = reinterpret_cast<const uint4*>(s);
+        for (u32 i = 0; i < n / 16; ++i) dv[i] = sv[i];
+    };
+    cp(S.oam + static_cast<u64>(e) * kOamBytes, rec + kRecOam, kOamBytes);
+    cp(S.nt + static_cast<u64>(e) * kNtBytes, rec + kRecNt, kNtBytes);
+    cp(S.pal + static_cast<u64>(e) * kPalBytes, rec + kRecPal, kPalBytes);
+    if (chr_ram) cp(S.chr_ram + static_cast<u64>(e) * kChrRamBytes, rec + kRecChrRam, kChrRamBytes);
+    cp(reinterpret_cast<u8*>(S.log + static_cast<u64>(e) * kLogBanks * kLogBankWords), rec + kRecLog, kLogBanks * kLogBankWords * 4);
+    const u64 sl = static_cast<u64>(e) * 4;
+    cp(S.snap_nt + sl * kNtBytes, rec + kRecSnapNt, kNtBytes);
+    cp(S.snap_oam + sl * kOamBytes, rec + kRecSnapOam, kOamBytes);
+    if (chr_ram && S.snap_chr) cp(S.snap_chr + sl * kChrRamBytes, rec + kRecChrRam, kChrRamBytes);
+    S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
+}
+
+// record <- env slot
+static __device__ void gather_record(const StateView& S, u32 e, u8* rec, bool chr_ram) {
+    u32* rr = reinterpret_cast<u32*>(rec + kRecRegs);
+    for (int w = 0; w < 64; ++w) rr[w] = w < kRegWords ? S.regs[static_cast<u64>(w) * S.Np + e] : 0u;
+    u32* ram = reinterpret_cast<u32*>(rec + kRecRam);
+    for (u32 i = 0; i < kRamWords; ++i) ram[i] = S.ram[static_cast<u64>(i) * S.Np + e];
+    u32* pr = reinterpret_cast<u32*>(rec + kRecPrgRam);
+    for (u32 i = 0; i < kPrgRamWords; ++i) pr[i] = S.prg_ram[static_cast<u64>(i) * S.Np + e];
+    auto cp = [](u8* d, const u8* s, u32 n) {
+        uint4* dv = reinterpret_cast<uint4*>(d);
+        const uint4* sv = reinterpret_cast<const uint4*>(s);
+        for (u32 i = 0; i < n / 16; ++i) dv[i] = sv[i];
+    };
+    cp(rec + kRecOam, S.oam + static_cast<u64>(e) * kOamBytes, kOamBytes);
+    cp(rec + kRecNt, S.nt + static_cast<u64>(e) * kNtBytes, kNtBytes);
+    cp(rec + kRecPal, S.pal + static_cast<u64>(e) * kPalBytes, kPalBytes);
+    if (chr_ram) cp(rec + kRecChrRam, S.chr_ram + static_cast<u64>(e) * kChrRamBytes, kChrRamBytes);
+    else for (u32 i = 0; i < kChrRamBytes / 4; ++i) reinterpret_cast<u32*>(rec + kRecChrRam)[i] = 0;
+    cp(rec + kRecLog, reinterpret_cast<const u8*>(S.log + static_cast<u64>(e) * kLogBanks * kLogBankWords), kLogBanks * kLogBankWords * 4);
+    const u32 fs = S.regs[static_cast<u64>(R_FSLOT) * S.Np + e];
+    const u64 sl = static_cast<u64>(e) * 4 + fs;
+    cp(rec + kRecSnapNt, S.snap_nt + sl * kNtBytes, kNtBytes);
+    cp(rec + kRecSnapOam, S.snap_oam + sl * kOamBytes, kOamBytes);
+}
+
+// ------------------------------------------------------------------------------------------------ phases
+
+static __device__ void write_controls(const GameArgs& g, const EnvArgs& A, u32 ge) {
+    const Dropout& d = A.drop[ge];
+    const int dr = dropped_now(d);
+    u32 dp = 0x1FF, ma = 7, mb = 7, ms = g.start_ok ? 3u : 1u, msel = g.select_ok ? 3u : 1u;
+    if (dr >= 0 && dr < 4) for (u32 k = 0; k < 9; ++k) if (dpad_bits(k) & (0x10u << dr)) dp &= ~(1u << k);
+    if (dr == 4) ma &= ~2u;
+    if (dr == 6) ma &= ~4u;
+    if (dr == 5) mb &= ~2u;
+    if (dr == 7) mb &= ~4u;
+    u8 m[20];
+    for (int i = 0; i < 9; ++i) m[i] = (dp >> i) & 1u;
+    for (int i = 0; i < 3; ++i) m[9 + i] = (ma >> i) & 1u;
+    for (int i = 0; i < 3; ++i) m[12 + i] = (mb >> i) & 1u;
+    for (int i = 0; i < 2; ++i) m[15 + i] = (ms >> i) & 1u;
+    for (int i = 0; i < 2; ++i) m[17 + i] = (msel >> i) & 1u;
+    u8* mo = A.masks + static_cast<u64>(ge) * kMaskBytes;
+    for (int i = 0; i < kMaskBytes; ++i) mo[i] = m[i];
+    u8* tl = A.timeline + static_cast<u64>(ge) * kTimelineBytes;
+    // 360 bytes = 90 words: zero, then the dropped inputs
+    u8 row[kTimelineBytes];
+    for (int i = 0; i < kTimelineBytes; ++i) row[i] = 0;
+    for (int j = 0; j < kTimeline; ++j) {
+        const int b = d.ring[(d.head + j) % kRing];
+        if (b >= 0) row[b * kTimeline + j] = 1;
+    }
+    if ((reinterpret_cast<uintptr_t>(tl) & 3u) == 0) {
+        for (int i = 0; i < kTimelineBytes / 4; ++i) {
+            reinterpret_cast<u32*>(tl)[i] = row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) | (static_cast<u32>(row[4 * i + 3]) << 24);
+        }
+    } else {
+        for (int i = 0; i < kTimelineBytes; ++i) tl[i] = row[i];
+    }
+}
+
+// rl/csrc/rlenv_core.cuh:208-263 (power-on / idle-snapshot restart)
+static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) {
+    const u32 ep = ++A.episode[ge];
+    const u64 seed = splitmix64(splitmix64(A.run_seed ^ 0xD20F0D20F0ull) ^ (static_cast<u64>(ge) << 40) ^ static_cast<u64>(ep));
+    const u64 ss = splitmix64(seed ^ 0x5717C4A55EEDull);
+    u64 ctr = 0;
+    int idle = 0;
+    if (A.idle_max > 0) idle = static_cast<int>(rand_below(ss, ctr, static_cast<u32>(A.idle_max + 1)));
+    A.sticky_seed[ge] = ss;
+    A.sticky_ctr[ge] = ctr;
+    const int k = idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
+    scatter_record(A.st, ge, g.recs + static_cast<u64>(k) * kRecBytes, g.cart.chr == nullptr);
+    A.target[ge] = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
+    A.ep_frame[ge] = static_cast<u32>(k);
+    Tracker t;
+    memset(&t, 0, sizeof t);
+    A.trk[ge] = t;
+    A.fault[ge] = 0;
+    Dropout d;
+    dropout_reset(d, seed, A.dropout != 0);
+    A.drop[ge] = d;
+    A.prev_applied[ge] = 0;
+    A.ep_idle[ge] = idle;
+    A.resetting[ge] = 1;
+}
+
+// ------------------------------------------------------------------------------------------------ kernels
+
+// Emulation: `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for listed envs.
+template <u32 BOARD>
+__global__ void __launch_bounds__(128) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
+    __shared__ u32 dtab[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) dtab[i] = kDecode.t[i];
+    __syncthreads();
+    u32 total = g.n;
+    if (restart) total = *A.list_count;
+    for (u32 k = blockIdx.x * blockDim.x + threadIdx.x; k < total; k += gridDim.x * blockDim.x) {
+        const u32 ge = restart ? A.list[k] : g.e0 + k;
+        if (restart && (ge < g.e0 || ge >= g.e0 + g.n)) continue;
+        Emu<BOARD> m(A.st, g.cart, ge, dtab);
+        m.load();
+        if (!restart) {
+            const int dr = dropped_now(A.drop[ge]);
+            u64 sctr = A.sticky_ctr[ge];
+            const u64 sseed = A.sticky_seed[ge];
+            int prev = A.prev_applied[ge];
+            const int act = A.actions[ge];
+            u32 pads4 = 0;
+            for (int f = 0; f < kFramesPerDecision; ++f) {
+                Move mv = unpack_move(act);
+                if (A.sticky && rand_u32(sseed, sctr) < kSticky32)
+                    mv = restrict_move(unpack_move(prev), dr, g.start_ok != 0, g.select_ok != 0);
+                prev = pack_move(mv);
+                const u32 pad = pad_byte(mv, A.ep_frame[ge]);
+                pads4 |= pad << (8 * f);
+                m.pad = pad;
+                m.slot = static_cast<u32>(f);
+                if (A.fault[ge] == 0) {
+                    const u32 fl = m.step_until(A.target[ge]);
+                    if (fl) A.fault[ge] = fl;
+                }
+                m.finish_slot();
+                A.target[ge] += kFrameDots;
+                A.ep_frame[ge] += 1;
+            }
+            A.sticky_ctr[ge] = sctr;
+            A.prev_applied[ge] = static_cast<int16_t>(prev);
+            reinterpret_cast<u32*>(A.pads)[ge] = pads4;
+        } else {
+            // ph_reset_idle: frames beyond the copied snapshot, then 4 neutral frames (rl/csrc/rlenv_core.cuh:311-328)
+            const int idle = A.ep_idle[ge];
+            const int have = idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
+            for (int i = have; i < idle; ++i) {
+                m.pad = 0;
+                m.slot = 0;
+                if (A.fault[ge] == 0) { const u32 fl = m.step_until(A.target[ge]); if (fl) A.fault[ge] = fl; }
+                m.finish_slot();
+                A.target[ge] += kFrameDots;
+                A.ep_frame[ge] += 1;
+            }
+            for (int f = 0; f < kFramesPerDecision; ++f) {
+                m.pad = 0;
+                m.slot = static_cast<u32>(f);
+                if (A.fault[ge] == 0) { const u32 fl = m.step_until(A.target[ge]); if (fl) A.fault[ge] = fl; }
+                m.finish_slot();
+                A.target[ge] += kFrameDots;
+                A.ep_frame[ge] += 1;
+            }
+        }
+        m.store();
+        if (restart) {
+            // ph_reset_finish_controls: first tracker update (no reward), counters, controls
+            Tracker t = A.trk[ge];
+            (void)reward_update(g.spec, observe_synth(A.st, ge), A.ep_idle[ge] + kFramesPerDecision, t);
+            A.trk[ge] = t;
+            A.ep_ret[ge] = 0.0f;
+            A.ep_len[ge] = 0;
+            A.ep_maxlvl[ge] = 0;
+            A.resetting[ge] = 0;
+            write_controls(g, A, ge);
+        }
+    }
+}
+
+// After a decision's frames: reward, outputs, episode end (rl/csrc/rlenv_core.cuh:266-309).
+static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int start) {
+    const u32 k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= g.n) return;
+    const u32 ge = g.e0 + k;
+    bool done;
+    if (start) {
+        done = true;
+    } else {
+        Tracker t = A.trk[ge];
+        const Upd u = reward_update(g.spec, observe_synth(A.st, ge), kFramesPerDecision, t);
+        A.trk[ge] = t;
+        const bool faulted = A.fault[ge] != 0;
+        const bool level_clear = !u.done && !faulted && A.episode_level_end >= 0 && (u.events & kEvLevel) &&
+                                 u.event_level == A.episode_level_end + 1;
+        const bool frame_limit = !u.done && !faulted && !level_clear && g.spec.frame_limit > 0.0 &&
+                                 static_cast<double>(A.ep_frame[ge]) >= g.spec.frame_limit;
+        done = u.done || faulted || level_clear || frame_limit;
+        const float r = faulted ? 0.0f : __double2float_rn(u.reward);
+        A.reward[ge] = r;
+        if (A.parts)
+            for (int q = 0; q < kParts; ++q) A.parts[static_cast<u64>(ge) * kParts + q] = faulted ? 0.0f : __double2float_rn(u.part[q]);
+        A.done[ge] = done ? 1 : 0;
+        A.events[ge] = u.events;
+        const float ret = __fadd_rn(A.ep_ret[ge], r);
+        A.ep_ret[ge] = ret;
+        const i32 len = A.ep_len[ge] + 1;
+        A.ep_len[ge] = len;
+        if (u.event_level > A.ep_maxlvl[ge]) A.ep_maxlvl[ge] = u.event_level;
+        Dropout d = A.drop[ge];
+        dropout_advance(d, A.dropout != 0);
+        A.drop[ge] = d;
+        if (done) {
+            float* inf = A.info + static_cast<u64>(ge) * kInfo;
+            inf[0] = ret;
+            inf[1] = static_cast<float>(len);
+            inf[2] = static_cast<float>(faulted ? 5 : level_clear ? 6 : frame_limit ? 7 : t.end_reason);
+            inf[3] = static_cast<float>(t.deaths);
+            inf[4] = static_cast<float>(A.ep_maxlvl[ge]);
+            inf[5] = t.overflow ? 1.0f : 0.0f;
+            inf[6] = static_cast<float>(A.ep_idle[ge]);
+            inf[7] = static_cast<float>(A.episode[ge]);
+        }
+    }
+    if (done) {
+        reset_state(g, A, ge);
+        const u32 slot = atomicAdd(A.list_count, 1u);
+        A.list[slot] = ge;
+    } else {
+        write_controls(g, A, ge);
+    }
+}
+
+// Warp per (env, frame). Grid-stride over the work items of this game slice (or the restart list).
+template <u32 BOARD>
+__global__ void __launch_bounds__(256) k_render(const __grid_constant__ RenderArgs R) {
+    extern __shared__ __align__(16) u8 smem[];
+    u32* spread = reinterpret_cast<u32*>(smem);                 // 1 KB
+    u32* chrx = spread + 256;                                   // 16 KB when staged
+    RWarp* warps = reinterpret_cast<RWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
+    for (u32 i = threadIdx.x; i < 256; i += blockDim.x) spread[i] = spread8(i);
+    if (R.chrx_smem) for (u32 i = threadIdx.x; i < 4096; i += blockDim.x) chrx[i] = R.cart.chrx[i];
+    __syncthreads();
+    const u32 lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    Renderer<BOARD> rd(R, lane, R.chrx_smem ? chrx : R.cart.chrx, spread, warps[wid]);
+    const u32 items = (R.list ? *R.list_count : R.count) * R.frames;
+    const u32 wpb = blockDim.x >> 5;
+    for (u32 it = blockIdx.x * wpb + wid; it < items; it += gridDim.x * wpb) {
+        const u32 k = it / R.frames, f = it % R.frames;
+        const u32 ge = R.list ? R.list[k] : R.e0 + k;
+        if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
+        rd.draw(ge, f, R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels, R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ set-up kernels
+
+// Power-on of env slot `e` (NeSLE cold reset, restated; RAM 0xFF as rl/csrc/rlenv_build.hpp:86).
+template <u32 BOARD>
+__global__ void k_power_on(const __grid_constant__ GameArgs g, StateView S, u32 e) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = 0;
+    for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * S.Np + e] = 0xFFFFFFFFu;
+    for (u32 i = 0; i < kPrgRamWords; ++i) S.prg_ram[static_cast<u64>(i) * S.Np + e] = 0;
+    for (u32 i = 0; i < kOamBytes; ++i) S.oam[static_cast<u64>(e) * kOamBytes + i] = 0;
+    for (u32 i = 0; i < kNtBytes; ++i) S.nt[static_cast<u64>(e) * kNtBytes + i] = 0;
+    for (u32 i = 0; i < kPalBytes; ++i) S.pal[static_cast<u64>(e) * kPalBytes + i] = 0;
+    if (S.chr_ram) for (u32 i = 0; i < kChrRamBytes; ++i) S.chr_ram[static_cast<u64>(e) * kChrRamBytes + i] = 0;
+    for (u32 i = 0; i < kLogBanks * kLogBankWords; ++i) S.log[static_cast<u64>(e) * kLogBanks * kLogBankWords + i] = 0;
+    __shared__ u32 dt[256];
+    for (int i = 0; i < 256; ++i) dt[i] = kDecode.t[i];
+    Emu<BOARD> m(S, g.cart, e, dt);
+    auto W = [&](int w, u32 v) { S.regs[static_cast<u64>(w) * S.Np + e] = v; };
+    // board power-on (patch:3057-3085)
+    // paged boards keep a run-time page map (the others mirror by the header and have none)
+    const u32 hmap = g.cart.arrangement == 1 ? kPageHorizontal : kPageVertical;
+    W(R_PPU2, (BOARD == kMmc1 || BOARD == kMmc3) ? (hmap << 24) : 0u);
+    if constexpr (BOARD == kMmc1) { m.set_mreg(0, 0x0C); m.mmc1_sync(); }
+    if constexpr (BOARD == kMmc3) {
+        m.set_mreg(1, 2); m.set_mreg(2, 4); m.set_mreg(3, 5); m.set_mreg(4, 6); m.set_mreg(5, 7); m.set_mreg(7, 1);
+        m.set_mreg(9, g.cart.arrangement == 1 ? 1 : 0);
+        m.mmc3_sync();
+    }
+    // CPU
+    m.prg_bank = 0;
+    const u32 lo = m.prg_rd(0xFFFCu), hi = m.prg_rd(0xFFFDu);
+    W(R_PC_SP_P, (lo | (hi << 8)) | (0xFDu << 16) | (0x24u << 24));
+    W(R_CYC_LO, 7);
+    // DMC power-on: byte_end = now + 1 + 7 * 428, idle
+    const u64 be = 7ull + 1ull + 7ull * 428ull;
+    W(R_DMC_END, static_cast<u32>(be)); W(R_DMC_END + 1, 0);
+    W(R_DMC_EV, 0xFFFFFFFFu); W(R_DMC_EV + 1, 0xFFFFFFFFu);
+    // both log banks 0 and 1 start from the reset state (frame_log_reset, patch:1133-1150); bank 0 shown
+    m.load();
+    m.fill_header(m.log_bank(0));
+    m.fill_header(m.log_bank(1));
+    // presentation slot 0 = the reset state
+    for (u32 i = 0; i < kNtBytes; ++i) S.snap_nt[static_cast<u64>(e) * 4 * kNtBytes + i] = 0;
+    for (u32 i = 0; i < kOamBytes; ++i) S.snap_oam[static_cast<u64>(e) * 4 * kOamBytes + i] = 0;
+    S.slot_bank[static_cast<u64>(e) * 4] = 0;
+}
+
+// Boot: run `frames` frames on env slot `e` with the given pads; after the boot and after each extra idle frame the
+// state is written as a snapshot record. Single thread.
+template <u32 BOARD>
+__global__ void k_boot(const __grid_constant__ GameArgs g, StateView S, u32 e, const u8* boot_pads, u32 boot_n,
+                       u32 idle_n, u8* recs, u32* fault_out) {
+    __shared__ u32 dt[256];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) dt[i] = kDecode.t[i];
+    __syncthreads();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    Emu<BOARD> m(S, g.cart, e, dt);
+    m.load();
+    u64 target = kVblankDot;
+    u32 fault = 0;
+    if (boot_n == 0) {
+        m.store();
+        gather_record(S, e, recs, g.cart.chr == nullptr);
+        m.load();
+    }
+    for (u32 k = 0; k < boot_n + idle_n; ++k) {
+        m.pad = k < boot_n ? boot_pads[k] : 0u;
+        m.slot = k & 3u;
+        const u32 f = m.step_until(target);
+        m.finish_slot();
+        target += kFrameDots;
+        if (f && !fault) fault = f;
+        if (k + 1 >= boot_n) {
+            m.store();
+            gather_record(S, e, recs + static_cast<u64>(k + 1 - boot_n) * kRecBytes, g.cart.chr == nullptr);
+            m.load();
+        }
+    }
+    m.store();
+    fault_out[0] = fault;
+    fault_out[1] = static_cast<u32>(target);
+    fault_out[2] = static_cast<u32>(target >> 32);
+}
+
+// Canonical dump of env slot e (same bytes as the CPU oracle's oracle_dump_env).
+static __global__ void k_dump(StateView S, u32 e, u32 chr_ram_cart, u8* o) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (u32 i = 0; i < kDumpBytes; ++i) o[i] = 0;
+    auto R = [&](int w) { return S.regs[static_cast<u64>(w) * S.Np + e]; };
+    auto p16 = [&](u32 off, u32 v) { o[off] = v & 0xFF; o[off + 1] = (v >> 8) & 0xFF; };
+    auto p32 = [&](u32 off, u32 v) { for (int i = 0; i < 4; ++i) o[off + i] = (v >> (8 * i)) & 0xFF; };
+    const u32 w0 = R(R_PC_SP_P), w1 = R(R_AXY_PAD);
+    p16(0, w0 & 0xFFFF); o[2] = w1 & 0xFF; o[3] = (w1 >> 8) & 0xFF; o[4] = (w1 >> 16) & 0xFF; o[5] = (w0 >> 16) & 0xFF;
+    o[6] = w0 >> 24; o[7] = w1 >> 24;
+    p32(8, R(R_CYC_LO)); p32(12, R(R_CYC_HI));
+    const u32 q0 = R(R_PPU0), q1 = R(R_PPU1), q2 = R(R_PPU2), io = R(R_IO);
+    o[16] = q0 & 0xFF; o[17] = (q0 >> 8) & 0xFF; o[18] = (q0 >> 16) & 0xFF; o[19] = q0 >> 24;
+    o[20] = q1 & 0xFF; o[21] = (q1 >> 8) & 0xFF; o[22] = (q1 >> 16) & 0xFF; o[23] = q1 >> 24;
+    o[24] = q2 & 0xFF; o[25] = ((q2 >> 8) & 0xFF) >> 2; o[26] = io >> 24; o[27] = (q2 >> 16) & 0xFF; o[28] = q2 >> 24;
+    o[29] = (io >> 16) & 0xFF; o[30] = (io >> 8) & 0xFF; o[31] = io & 0xFF;
+    p32(32, R(R_FDOT)); p32(36, R(R_VT));
+    p32(40, R(R_FRAME_LO)); p32(44, R(R_FRAME_HI));
+    p32(48, R(R_S0)); p16(52, R(R_LOGN) & 0xFFFF);
+    const u8* r8 = reinterpret_cast<const u8*>(S.ram);
+    for (u32 a = 0; a < 2048; ++a) o[64 + a] = r8[((static_cast<u64>(a >> 2) * S.Np + e) << 2) | (a & 3u)];
+    for (u32 a = 0; a < 2048; ++a) o[2112 + a] = S.nt[static_cast<u64>(e) * kNtBytes + a];
+    for (u32 a = 0; a < 32; ++a) o[4160 + a] = S.pal[static_cast<u64>(e) * kPalBytes + a];
+    for (u32 a = 0; a < 256; ++a) o[4192 + a] = S.oam[static_cast<u64>(e) * kOamBytes + a];
+    for (u32 i = 0; i < 4; ++i) p32(4448 + 4 * i, R(R_MREG + i));
+    for (u32 i = 0; i < 4; ++i) p32(4464 + 4 * i, R(R_PRGPG + i));
+    for (u32 i = 0; i < 8; ++i) p32(4480 + 4 * i, R(R_CHRPG + i));
+    p32(4512, R(R_DMC_END)); p32(4516, R(R_DMC_END + 1));
+    const u32 da = R(R_DMC_A), db = R(R_DMC_B);
+    p16(4520, da & 0xFFFF); o[4522] = (da >> 16) & 0xFF; o[4523] = da >> 24; o[4524] = db & 0xFF; o[4525] = (db >> 8) & 0xFF;
+    p32(4528, R(R_DMC_EV)); p32(4532, R(R_DMC_EV + 1));
+    const u32 shown = (q2 >> 8) & kLcBank;
+    const u32* h = S.log + (static_cast<u64>(e) * kLogBanks + shown) * kLogBankWords;
+    const u32 cnt = min(h[0] & ~kLogOverflow, kLogEv);
+    for (u32 i = 0; i < kLogHdr + 2 * cnt; ++i) p32(4544 + 4 * i, h[i]);
+    const u8* pr8 = reinterpret_cast<const u8*>(S.prg_ram);
+    for (u32 a = 0; a < 8192; ++a) o[6656 + a] = pr8[((static_cast<u64>(a >> 2) * S.Np + e) << 2) | (a & 3u)];
+    if (chr_ram_cart && S.chr_ram) for (u32 a = 0; a < 8192; ++a) o[14848 + a] = S.chr_ram[static_cast<u64>(e) * kChrRamBytes + a];
+}
+
+}  // namespace gr

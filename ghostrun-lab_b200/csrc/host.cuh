@@ -1,0 +1,187 @@
+// Host-side runtime shared by the library's translation units: device memory, cartridge parsing, the per-game
+// launch sequence and the boot run. The board-specialised templates (launch_game / boot_game) are instantiated
+// once per board in board_*.cu, so the four emulator specialisations compile in parallel.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "envcore.cuh"
+
+namespace gr {
+
+inline void ck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct DevMem {
+    std::vector<void*> blocks;
+    std::vector<std::pair<void*, std::size_t>> state;   // (ptr, bytes) saved by rlenv_save, in order
+    void* alloc(std::size_t n, bool saved = false) {
+        void* p = nullptr;
+        ck(cudaMalloc(&p, n ? n : 16), "cudaMalloc");
+        ck(cudaMemset(p, 0, n ? n : 16), "cudaMemset");
+        blocks.push_back(p);
+        if (saved) state.emplace_back(p, n);
+        return p;
+    }
+    template <class T> T* allocn(std::size_t count, bool saved = false) { return static_cast<T*>(alloc(sizeof(T) * count, saved)); }
+    ~DevMem() { for (void* p : blocks) cudaFree(p); }
+};
+
+// iNES 1.0 header -> board description (the product's own parser; rl/csrc/rlenv_build.hpp:36-84 uses NeSLE's).
+struct HostCart {
+    std::vector<u8> prg, chr;
+    u32 board = kNrom, arrangement = 0, bank_mask = 0, fixed_base = 0, prg_page_mask = 0, chr_page_mask = 0;
+};
+
+inline HostCart parse_rom(const u8* rom, std::size_t n) {
+    if (n < 16 || std::memcmp(rom, "NES\x1a", 4) != 0) throw std::runtime_error("not an iNES image");
+    const std::size_t prg_bytes = static_cast<std::size_t>(rom[4]) * 16384, chr_bytes = static_cast<std::size_t>(rom[5]) * 8192;
+    const u32 mapper = (rom[6] >> 4) | (rom[7] & 0xF0u);
+    const std::size_t base = 16 + ((rom[6] & 4) ? 512 : 0);
+    if (prg_bytes == 0 || base + prg_bytes + chr_bytes > n) throw std::runtime_error("truncated iNES image");
+    HostCart c;
+    std::size_t padded = 1;
+    while (padded < prg_bytes) padded <<= 1;
+    c.prg.assign(padded, 0);
+    std::memcpy(c.prg.data(), rom + base, prg_bytes);
+    c.chr.assign(rom + base + prg_bytes, rom + base + prg_bytes + chr_bytes);
+    c.arrangement = (rom[6] & 8) ? 2u : (rom[6] & 1) ? 0u : 1u;
+    const bool pow2 = (prg_bytes & (prg_bytes - 1)) == 0;
+    if (mapper == 0) {
+        if ((prg_bytes != 16384 && prg_bytes != 32768) || chr_bytes == 0) throw std::runtime_error("NROM needs 16/32 KB PRG and CHR ROM");
+        c.board = kNrom;
+    } else if (mapper == 2) {
+        if (prg_bytes < 32768 || !pow2) throw std::runtime_error("UxROM PRG must be a power of two >= 32 KB");
+        c.board = kUxrom;
+        c.bank_mask = static_cast<u32>(prg_bytes / 16384 - 1);
+        c.fixed_base = static_cast<u32>(prg_bytes - 16384);
+    } else if (mapper == 1 || mapper == 4) {
+        const std::size_t cb = chr_bytes ? chr_bytes : 8192;
+        if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || (cb & (cb - 1)))
+            throw std::runtime_error("unsupported MMC1/MMC3 image size");
+        c.board = mapper == 1 ? kMmc1 : kMmc3;
+        c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
+        c.chr_page_mask = static_cast<u32>(cb / 1024 - 1);
+    } else {
+        throw std::runtime_error("unsupported mapper " + std::to_string(mapper) + " (supported: 0 NROM, 1 MMC1, 2 UxROM, 4 MMC3)");
+    }
+    return c;
+}
+
+// CHR ROM as 4-bit-per-pixel rows (render.cuh): chrx[row * 512 + tile], first 8 KB.
+inline std::vector<u32> expand_chr(const std::vector<u8>& chr) {
+    std::vector<u32> out(4096, 0);
+    auto spread = [](u32 b) { u32 r = 0; for (int k = 0; k < 8; ++k) r |= ((b >> (7 - k)) & 1u) << (4 * k); return r; };
+    for (u32 tile = 0; tile < 512; ++tile)
+        for (u32 row = 0; row < 8; ++row) {
+            const u32 lo = chr[(tile * 16 + row) % chr.size()], hi = chr[(tile * 16 + row + 8) % chr.size()];
+            out[row * 512 + tile] = spread(lo) | (spread(hi) << 1);
+        }
+    return out;
+}
+
+struct Game {
+    int game_id = 0;
+    GameArgs g{};
+    bool chrx_smem = false;
+};
+
+struct Env {
+    DevMem mem;
+    int device = 0;
+    int total = 0;
+    u32 Np = 0;
+    std::vector<Game> games;
+    EnvArgs A{};
+    bool chr_ram_any = false;
+    cudaEvent_t ev = nullptr;
+    ~Env() { if (ev) cudaEventDestroy(ev); }
+};
+
+inline void check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <u32 B>
+void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s) {
+    const GameArgs& g = gm.g;
+    const EnvArgs& A = env.A;
+    const u32 n = g.n;
+    if (n == 0) return;
+    const u32 tb = 128;
+    RenderArgs R{};
+    R.cart = g.cart;
+    R.st = A.st;
+    R.obs = A.obs;
+    R.emph = A.emph;
+    R.e0 = g.e0;
+    R.count = n;
+    R.frames = kFramesPerDecision;
+    R.chrx_smem = gm.chrx_smem ? 1u : 0u;
+    const std::size_t smem = 1024 + (gm.chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp);
+    if (!start) {
+        k_frames<B><<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, 0);
+        check_launch("k_frames");
+        if (!A.no_render) {
+            R.list = nullptr;
+            const u32 items = n * kFramesPerDecision;
+            const u32 blocks = std::min<u32>((items + 7) / 8, 148u * 16u);
+            k_render<B><<<blocks, 256, smem, s>>>(R);
+            check_launch("k_render");
+        }
+    }
+    k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
+    check_launch("k_finish");
+    const u32 rb = start ? (n + tb - 1) / tb : std::min<u32>((n + tb - 1) / tb, 148u);
+    k_frames<B><<<rb, tb, 0, s>>>(g, A, 1);
+    check_launch("k_frames restart");
+    if (!A.no_render) {
+        R.list = A.list;
+        R.list_count = A.list_count;
+        const u32 blocks = start ? std::min<u32>((n * kFramesPerDecision + 7) / 8, 148u * 16u) : 148u;
+        k_render<B><<<blocks, 256, smem, s>>>(R);
+        check_launch("k_render restart");
+    }
+}
+
+template <u32 B>
+void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_max, u32 slot) {
+    u8* dpads = env.mem.allocn<u8>(npads + 1);
+    if (npads) ck(cudaMemcpy(dpads, pads, npads, cudaMemcpyHostToDevice), "boot pads");
+    u32* fault = env.mem.allocn<u32>(4);
+    const u32 idle = idle_max > 0 ? static_cast<u32>(idle_max) : 0u;
+    u8* recs = env.mem.allocn<u8>(static_cast<std::size_t>(idle + 1) * kRecBytes);
+    k_power_on<B><<<1, 32>>>(gm.g, env.A.st, slot);
+    check_launch("k_power_on");
+    k_boot<B><<<1, 32>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
+    check_launch("k_boot");
+    u32 hf[4] = {0, 0, 0, 0};
+    ck(cudaMemcpy(hf, fault, 16, cudaMemcpyDeviceToHost), "boot");
+    if (hf[0]) {
+        char buf[96];
+        std::snprintf(buf, sizeof buf, "emulator fault during boot of game %d (pc<<8|op = 0x%06x)", gm.game_id, hf[0]);
+        throw std::runtime_error(buf);
+    }
+    gm.g.recs = recs;
+    gm.g.idle_tmpl = idle;
+    gm.g.tmpl_target = static_cast<u64>(kVblankDot) + static_cast<u64>(npads) * kFrameDots;
+}
+
+
+#define GR_BOARD_TEMPLATES(EXT, B)                                                                   \
+    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t);                    \
+    EXT template void boot_game<B>(Env&, Game&, const u8*, std::size_t, int, u32);
+GR_BOARD_TEMPLATES(extern, kNrom)
+GR_BOARD_TEMPLATES(extern, kUxrom)
+GR_BOARD_TEMPLATES(extern, kMmc1)
+GR_BOARD_TEMPLATES(extern, kMmc3)
+
+}  // namespace gr

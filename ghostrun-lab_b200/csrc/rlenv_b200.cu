@@ -1,0 +1,289 @@
+// librlenv_b200.so: the batched NES environment for B200 behind the reference environment's C-ABI
+// (rl/csrc/rlenv_api.h:8-47 and the GPU-build extras of rl/csrc/rlenv.cu:247-421). The declarations, with the
+// reference interface each one replaces, are in include/rlenv_api.h.
+//
+// Host side: owns device memory, builds each game's cartridge view and boot / idle-frame snapshot records on the
+// device, and launches the per-decision kernel sequence (envcore.cuh) on the caller's stream. Errors: int 0 ok /
+// 1 failed, rlenv_create returns NULL, message in a thread-local string (rlenv_error); no C++ exception crosses
+// the ABI. There is no CPU path: without a CUDA device every entry point fails with a message.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "host.cuh"
+
+using namespace gr;
+
+namespace {
+
+thread_local std::string g_error;
+std::mutex g_specs_mu;
+std::map<int, Spec> g_specs;   // rl10 game id -> reward parameters (rl10_register_game)
+
+int fail(const std::exception& ex) { g_error = ex.what(); return 1; }
+
+void launch_all(Env& env, bool start, cudaStream_t s) {
+    ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
+    for (const Game& gm : env.games) {
+        switch (gm.g.cart.board) {
+            case kNrom: launch_game<kNrom>(env, gm, start, s); break;
+            case kUxrom: launch_game<kUxrom>(env, gm, start, s); break;
+            case kMmc1: launch_game<kMmc1>(env, gm, start, s); break;
+            default: launch_game<kMmc3>(env, gm, start, s); break;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int rl10_register_game(int game_id, const double* spec, int n) {
+    if (n != kSpecFields || game_id < 0) { g_error = "rl10_register_game: expected 20 fields"; return 1; }
+    Spec s;
+    std::memcpy(&s, spec, sizeof s);
+    std::lock_guard<std::mutex> lock(g_specs_mu);
+    g_specs[game_id] = s;
+    return 0;
+}
+
+void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* roms, const std::size_t* rom_sizes,
+                   const std::uint8_t* const* boot_pads, const std::size_t* boot_sizes, const int* n_envs,
+                   std::uint64_t run_seed, int sticky, int idle_max, int dropout, int device) {
+    Env* env = nullptr;
+    try {
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+            throw std::runtime_error("no CUDA device: librlenv_b200 runs on the GPU only");
+        ck(cudaSetDevice(device), "cudaSetDevice");
+        env = new Env();
+        env->device = device;
+        int total = 0;
+        for (int i = 0; i < ngames; ++i) total += n_envs[i];
+        env->total = total;
+        const u32 Np = static_cast<u32>((total + 1 + 31) / 32 * 32);   // + 1: boot slot
+        env->Np = Np;
+        std::vector<HostCart> carts;
+        for (int i = 0; i < ngames; ++i) {
+            carts.push_back(parse_rom(roms[i], rom_sizes[i]));
+            if (carts.back().chr.empty()) env->chr_ram_any = true;
+        }
+        DevMem& M = env->mem;
+        StateView& S = env->A.st;
+        S.Np = Np;
+        S.regs = M.allocn<u32>(static_cast<std::size_t>(kRegWords) * Np, true);
+        S.ram = M.allocn<u32>(static_cast<std::size_t>(kRamWords) * Np, true);
+        S.prg_ram = M.allocn<u32>(static_cast<std::size_t>(kPrgRamWords) * Np, true);
+        S.oam = M.allocn<u8>(static_cast<std::size_t>(kOamBytes) * Np, true);
+        S.nt = M.allocn<u8>(static_cast<std::size_t>(kNtBytes) * Np, true);
+        S.pal = M.allocn<u8>(static_cast<std::size_t>(kPalBytes) * Np, true);
+        S.chr_ram = env->chr_ram_any ? M.allocn<u8>(static_cast<std::size_t>(kChrRamBytes) * Np, true) : nullptr;
+        S.log = M.allocn<u32>(static_cast<std::size_t>(kLogBanks) * kLogBankWords * Np, true);
+        S.snap_nt = M.allocn<u8>(static_cast<std::size_t>(4) * kNtBytes * Np, true);
+        S.snap_oam = M.allocn<u8>(static_cast<std::size_t>(4) * kOamBytes * Np, true);
+        S.snap_chr = env->chr_ram_any ? M.allocn<u8>(static_cast<std::size_t>(4) * kChrRamBytes * Np, true) : nullptr;
+        S.slot_bank = M.allocn<u8>(static_cast<std::size_t>(4) * Np, true);
+        EnvArgs& A = env->A;
+        const std::size_t N = static_cast<std::size_t>(total) + 1;
+        A.trk = M.allocn<Tracker>(N, true);
+        A.drop = M.allocn<Dropout>(N, true);
+        A.target = M.allocn<u64>(N, true);
+        A.ep_frame = M.allocn<u32>(N, true);
+        A.prev_applied = M.allocn<int16_t>(N, true);
+        A.sticky_seed = M.allocn<u64>(N, true);
+        A.sticky_ctr = M.allocn<u64>(N, true);
+        A.episode = M.allocn<u32>(N, true);
+        A.ep_ret = M.allocn<float>(N, true);
+        A.ep_len = M.allocn<i32>(N, true);
+        A.ep_maxlvl = M.allocn<i32>(N, true);
+        A.ep_idle = M.allocn<i32>(N, true);
+        A.fault = M.allocn<u32>(N, true);
+        A.resetting = M.allocn<u8>(N);
+        A.list = M.allocn<u32>(N);
+        A.list_count = M.allocn<u32>(1);
+        {
+            std::vector<u32> init(N, 0xFFFFFFFFu);
+            ck(cudaMemcpy(A.episode, init.data(), N * 4, cudaMemcpyHostToDevice), "episode init");
+        }
+        A.run_seed = run_seed;
+        A.sticky = sticky;
+        A.idle_max = idle_max;
+        A.dropout = dropout;
+        A.no_render = 0;
+        A.episode_level_end = -1;
+        int offset = 0;
+        for (int i = 0; i < ngames; ++i) {
+            Game gm;
+            gm.game_id = game_ids[i];
+            {
+                std::lock_guard<std::mutex> lock(g_specs_mu);
+                auto it = g_specs.find(game_ids[i]);
+                if (it == g_specs.end())
+                    throw std::runtime_error("game id " + std::to_string(game_ids[i]) + " has no reward spec (rl10_register_game)");
+                if (it->second.reader != 1.0)
+                    throw std::runtime_error("game id " + std::to_string(game_ids[i]) + ": only the synthetic RAM reader is built");
+                gm.g.spec = it->second;
+            }
+            const HostCart& hc = carts[i];
+            CartView& C = gm.g.cart;
+            u8* prg = M.allocn<u8>(hc.prg.size());
+            ck(cudaMemcpy(prg, hc.prg.data(), hc.prg.size(), cudaMemcpyHostToDevice), "prg");
+            C.prg = prg;
+            C.prg_mask = static_cast<u32>(hc.prg.size() - 1);
+            if (!hc.chr.empty()) {
+                u8* chr = M.allocn<u8>(hc.chr.size());
+                ck(cudaMemcpy(chr, hc.chr.data(), hc.chr.size(), cudaMemcpyHostToDevice), "chr");
+                C.chr = chr;
+                C.chr_size = static_cast<u32>(hc.chr.size());
+                const std::vector<u32> x = expand_chr(hc.chr);
+                u32* cx = M.allocn<u32>(x.size());
+                ck(cudaMemcpy(cx, x.data(), x.size() * 4, cudaMemcpyHostToDevice), "chrx");
+                C.chrx = cx;
+                C.chr_tiles = 512;
+                gm.chrx_smem = hc.board == kNrom || hc.board == kUxrom;
+            } else {
+                C.chr = nullptr;
+                C.chr_size = 0;
+                C.chrx = nullptr;
+            }
+            C.board = hc.board;
+            C.arrangement = hc.arrangement;
+            C.bank_mask = hc.bank_mask;
+            C.fixed_base = hc.fixed_base;
+            C.prg_page_mask = hc.prg_page_mask;
+            C.chr_page_mask = hc.chr_page_mask;
+            gm.g.e0 = static_cast<u32>(offset);
+            gm.g.n = static_cast<u32>(n_envs[i]);
+            gm.g.start_ok = gm.g.spec.start_ok != 0.0;
+            gm.g.select_ok = gm.g.spec.select_ok != 0.0;
+            offset += n_envs[i];
+            const u32 boot_slot = static_cast<u32>(total);
+            switch (hc.board) {
+                case kNrom: boot_game<kNrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+                case kUxrom: boot_game<kUxrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+                case kMmc1: boot_game<kMmc1>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+                default: boot_game<kMmc3>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+            }
+            env->games.push_back(gm);
+        }
+        for (auto& gm : env->games) {
+            const std::size_t smem = 1024 + (gm.chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp);
+            if (smem > 48 * 1024) throw std::logic_error("render shared memory exceeds the default limit");
+        }
+        ck(cudaEventCreateWithFlags(&env->ev, cudaEventDisableTiming), "event");
+        ck(cudaDeviceSynchronize(), "create");
+        return env;
+    } catch (const std::exception& ex) {
+        g_error = ex.what();
+        delete env;
+        return nullptr;
+    }
+}
+
+int rlenv_num_envs(void* h) { return static_cast<Env*>(h)->total; }
+int rlenv_num_games(void* h) { return static_cast<int>(static_cast<Env*>(h)->games.size()); }
+void rlenv_set_episode_level_end(void* h, int level) { static_cast<Env*>(h)->A.episode_level_end = level; }
+void rlenv_set_no_render(void* h, int v) { static_cast<Env*>(h)->A.no_render = v; }
+
+void rlenv_bind(void* h, const std::int16_t* actions, std::uint8_t* obs, std::uint8_t* emph, float* reward,
+                std::uint8_t* done, std::uint8_t* masks, std::uint8_t* timeline, std::uint8_t* pads,
+                std::uint32_t* events, float* info) {
+    EnvArgs& A = static_cast<Env*>(h)->A;
+    A.actions = actions; A.obs = obs; A.emph = emph; A.reward = reward; A.done = done; A.masks = masks;
+    A.timeline = timeline; A.pads = pads; A.events = events; A.info = info;
+}
+void rlenv_bind_parts(void* h, float* parts) { static_cast<Env*>(h)->A.parts = parts; }
+void rlenv_bind_obs(void* h, std::uint8_t* obs, std::uint8_t* emph) {
+    EnvArgs& A = static_cast<Env*>(h)->A;
+    A.obs = obs;
+    A.emph = emph;
+}
+
+int rlenv_start(void* h, void* stream) {
+    try {
+        launch_all(*static_cast<Env*>(h), true, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rlenv_step(void* h, void* stream) {
+    try {
+        launch_all(*static_cast<Env*>(h), false, static_cast<cudaStream_t>(stream));
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+std::size_t rlenv_state_bytes(void* h) {
+    std::size_t n = 0;
+    for (const auto& pb : static_cast<Env*>(h)->mem.state) n += pb.second;
+    return n;
+}
+int rlenv_save(void* h, std::uint8_t* out, void* stream) {
+    try {
+        auto s = static_cast<cudaStream_t>(stream);
+        for (const auto& pb : static_cast<Env*>(h)->mem.state) {
+            ck(cudaMemcpyAsync(out, pb.first, pb.second, cudaMemcpyDeviceToHost, s), "save");
+            out += pb.second;
+        }
+        ck(cudaStreamSynchronize(s), "save");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rlenv_load(void* h, const std::uint8_t* in, void* stream) {
+    try {
+        auto s = static_cast<cudaStream_t>(stream);
+        for (const auto& pb : static_cast<Env*>(h)->mem.state) {
+            ck(cudaMemcpyAsync(pb.first, in, pb.second, cudaMemcpyHostToDevice, s), "load");
+            in += pb.second;
+        }
+        ck(cudaStreamSynchronize(s), "load");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+const char* rlenv_error() { return g_error.c_str(); }
+void rlenv_destroy(void* h) { delete static_cast<Env*>(h); }
+
+// Canonical machine state of global env `ge` into host memory (layout: include/rlenv_api.h).
+std::size_t rlenv_dump_bytes() { return kDumpBytes; }
+int rlenv_dump_env(void* h, int ge, std::uint8_t* host_out, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (ge < 0 || ge >= env.total) throw std::runtime_error("dump: bad env index");
+        auto s = static_cast<cudaStream_t>(stream);
+        u8* d = nullptr;
+        ck(cudaMallocAsync(reinterpret_cast<void**>(&d), kDumpBytes, s), "dump alloc");
+        k_dump<<<1, 32, 0, s>>>(env.A.st, static_cast<u32>(ge), env.chr_ram_any ? 1u : 0u, d);
+        check_launch("k_dump");
+        ck(cudaMemcpyAsync(host_out, d, kDumpBytes, cudaMemcpyDeviceToHost, s), "dump copy");
+        ck(cudaFreeAsync(d, s), "dump free");
+        ck(cudaStreamSynchronize(s), "dump");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// Per-env RL scalars of global env ge: target, ep_frame, episode, fault, sticky_ctr (host memory, synchronous).
+int rlenv_env_scalars(void* h, int ge, std::uint64_t* out, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        auto s = static_cast<cudaStream_t>(stream);
+        u64 t = 0, sc = 0;
+        u32 f = 0, ep = 0, fl = 0;
+        ck(cudaMemcpyAsync(&t, env.A.target + ge, 8, cudaMemcpyDeviceToHost, s), "scalars");
+        ck(cudaMemcpyAsync(&f, env.A.ep_frame + ge, 4, cudaMemcpyDeviceToHost, s), "scalars");
+        ck(cudaMemcpyAsync(&ep, env.A.episode + ge, 4, cudaMemcpyDeviceToHost, s), "scalars");
+        ck(cudaMemcpyAsync(&fl, env.A.fault + ge, 4, cudaMemcpyDeviceToHost, s), "scalars");
+        ck(cudaMemcpyAsync(&sc, env.A.sticky_ctr + ge, 8, cudaMemcpyDeviceToHost, s), "scalars");
+        ck(cudaStreamSynchronize(s), "scalars");
+        out[0] = t; out[1] = f; out[2] = ep; out[3] = fl; out[4] = sc;
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+}  // extern "C"

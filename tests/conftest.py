@@ -1,0 +1,50 @@
+"""Test set-up: the `gpu` marker (tests that need a B200), library paths, and the oracle / reference loaders."""
+from __future__ import annotations
+
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / 'ghostrun-lab_b200'
+ORACLE = ROOT / 'oracle'
+sys.path.insert(0, str(PKG))
+sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line('markers', 'gpu: needs a CUDA device (B200)')
+
+
+def oracle_lib() -> Path:
+    """The CPU oracle (test infrastructure), built from oracle/ on first use."""
+    lib = ORACLE / 'liboracle_rlenv.so'
+    srcs = [ORACLE / n for n in ('oracle_api.cpp', 'env.hpp', 'nes.hpp')]
+    if not lib.exists() or any(s.stat().st_mtime > lib.stat().st_mtime for s in srcs):
+        subprocess.run(['make', '-C', str(ORACLE), 'all'], check=True, capture_output=True)
+    return lib
+
+
+def reference_host_lib():
+    """The reference's own controller / reward10 host library (oracle/_ref, compiled from /root/reference), or None."""
+    lib = ORACLE / '_ref' / 'librl_host.so'
+    if not lib.exists() and Path('/root/reference/rl/csrc/host_api.cpp').exists():
+        subprocess.run(['make', '-C', str(ORACLE), 'ref'], check=True, capture_output=True)
+    return lib if lib.exists() else None
+
+
+@pytest.fixture(scope='session')
+def oracle_path():
+    return oracle_lib()
+
+
+@pytest.fixture(scope='session')
+def gpu_lib_path():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip('no CUDA device')
+    sys.path.insert(0, str(PKG))
+    import build
+    return build.build()
