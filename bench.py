@@ -1,0 +1,391 @@
+"""Benchmark of the batched NES environment step on B200 (the BASELINE metric: decisions/s and NES frames/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--envs E]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one process per GPU, NCCL)
+
+Workload (per GPU): E = 8192 envs of the seeded synthetic NROM cart 'synth00', 4 frames per
+decision, sticky moves, dropout and 0..30 idle frames at episode starts on, pictures packed to 6 bits by the
+renderer. Weak scaling: every GPU steps its own 8192 envs (seed * 7919 + rank); the per-rollout episode counters
+are all-reduced with NCCL every 128 decisions.
+  value   decisions/s with everything resident in HBM (env step only, CUDA events on the env's stream).
+  e2e     the same through the public API with host buffers: each decision copies its actions host->device from
+          pinned memory, steps, and copies the packed pictures (+ emphasis, reward, done, masks) device->host into a
+          pinned rollout ring; copies overlap the next decision's step on a copy stream.
+  roofline  the render kernel (the dominant one): algorithmic bytes per launch / its CUDA-event time vs the
+          measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the CPU oracle (restated reference CPU build, OpenMP over envs) on this host's cores, rank 0, N=1.
+Prints ONE JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / 'ghostrun-lab_b200'
+sys.path.insert(0, str(PKG))
+
+METRIC = 'decisions/s (4 NES frames each)'
+UNIT = 'decisions/s'
+GAME = 'synth00'
+PACKED_ROW = 4 * 224 * 240 // 4 * 3   # 161,280 bytes of packed pictures per decision
+EMPH_ROW = 4 * 224
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=100)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--envs', type=int, default=8192)
+    ap.add_argument('--seed', type=int, default=1)
+    ap.add_argument('--ring', type=int, default=4, help='pinned host rollout slots (decisions) for e2e')
+    ap.add_argument('--cpu-leg', action='store_true', help=argparse.SUPPRESS)
+    ap.add_argument('--cpu-seconds', type=float, default=15.0)
+    ap.add_argument('--no-cpu', action='store_true')
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------ CPU leg
+
+def cpu_leg(args):
+    """Runs in its own process (OMP_NUM_THREADS fixed before the oracle's OpenMP starts). Prints a JSON dict."""
+    import torch
+    from rlenv import RlEnv
+    from actions import random_legal
+    oracle = ROOT / 'oracle' / 'liboracle_rlenv.so'
+    if not oracle.exists():
+        subprocess.run(['make', '-C', str(ROOT / 'oracle'), 'all'], check=True, capture_output=True)
+    env = RlEnv({GAME: args.envs}, device='cpu', seed=args.seed * 7919, sticky=True, idle_max=30, dropout=True,
+                lib_path=oracle)
+    env.start()
+    gen = torch.Generator().manual_seed(args.seed)
+    for _ in range(max(1, min(args.warmup, 2))):
+        env.actions.copy_(random_legal(env.masks, gen)); env.step()
+    t0 = time.perf_counter()
+    env.actions.copy_(random_legal(env.masks, gen)); env.step()
+    one = time.perf_counter() - t0
+    steps = int(max(2, min(200, args.cpu_seconds / max(one, 1e-6))))
+    acts = [random_legal(env.masks, gen) for _ in range(1)]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        env.actions.copy_(acts[0]); env.step()
+    dt = time.perf_counter() - t0
+    cores = int(os.environ.get('OMP_NUM_THREADS', os.cpu_count()))
+    print(json.dumps(dict(value=steps * args.envs / dt, steps=steps, seconds=dt, cores=cores)))
+
+
+def run_cpu_leg(args, seconds):
+    cmd = [sys.executable, __file__, '--cpu-leg', '--envs', str(args.envs), '--seed', str(args.seed),
+           '--warmup', str(args.warmup), '--cpu-seconds', str(seconds)]
+    envv = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()), CUDA_VISIBLE_DEVICES='')
+    out = subprocess.run(cmd, capture_output=True, text=True, env=envv, timeout=900)
+    if out.returncode != 0:
+        raise RuntimeError(out.stderr[-2000:])
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+def cpu_model():
+    try:
+        for line in Path('/proc/cpuinfo').read_text().splitlines():
+            if line.startswith('model name'):
+                return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.Q}', '--format=csv,noheader,nounits',
+                                          '-i', str(self.index), '-lms', '200'], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(n)
+        if not sm:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=[], samples=0)
+        return dict(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), reasons=sorted(reasons), samples=len(sm))
+
+
+# ------------------------------------------------------------------------------------------------ GPU arm
+
+def measured_peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+def render_traffic_per_env_frame():
+    """DRAM bytes per rendered (env, frame) from the committed ncu summary of the render kernel, if any."""
+    p = ROOT / 'profiles' / 'k_render_synth00.md'
+    if p.exists():
+        m = re.search(r'traffic_bytes_per_env_frame:\s*([0-9.]+)', p.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+def gpu_arm(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from rlenv import RlEnv, default_lib
+    import build as gbuild
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if not default_lib().exists():
+        gbuild.build()
+    E = args.envs
+    env = RlEnv({GAME: E}, device=dev, seed=args.seed * 7919 + rank, sticky=True, idle_max=30, dropout=True)
+    packed = [torch.empty(E * PACKED_ROW, dtype=torch.uint8, device=dev) for _ in range(2)]
+    env.bind_obs_pack6(packed[0])
+    env.start()
+    # actions: uniform over the moves without Start/Select, drawn on the device up front (the env checks nothing)
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    K, W = args.steps, args.warmup
+    acts_dev = torch.randint(0, 81, (K + W, E), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+    counters = torch.zeros(4, dtype=torch.float64, device=dev)   # finished episodes, deaths, return sum, clears
+
+    def account():
+        d = env.done.bool()
+        counters[0] += d.sum()
+        counters[1] += torch.where(d, env.info[:, 3], 0).sum()
+        counters[2] += torch.where(d, env.info[:, 0], 0).sum()
+        counters[3] += (env.events & 2).ne(0).sum()
+
+    stream = torch.cuda.current_stream(dev)
+    for t in range(W):
+        env.actions.copy_(acts_dev[t]); env.step(); account()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+
+    # ---- value: device-resident
+    env.set_timing(True)
+    env.timing(reset=True)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    with clk:
+        ev0.record(stream)
+        for t in range(K):
+            env.actions.copy_(acts_dev[W + t])
+            env.step()
+            account()
+            if world > 1 and (t + 1) % 128 == 0:
+                dist.all_reduce(counters)
+        if world > 1:
+            dist.all_reduce(counters)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    tm = env.timing(reset=True)
+    env.set_timing(False)
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = K * E * world / (ms_max / 1e3)
+
+    # ---- e2e: public API with host buffers (pinned), copies overlapped on a copy stream
+    R = max(2, args.ring)
+    host_acts = torch.randint(0, 81, (K, E), dtype=torch.int16).pin_memory()
+    ring = torch.empty((R, E * (PACKED_ROW + EMPH_ROW)), dtype=torch.uint8).pin_memory()
+    small = torch.empty((R, E * (4 + 1 + 19)), dtype=torch.uint8).pin_memory()
+    copy = torch.cuda.Stream(dev)
+    done_ev = [torch.cuda.Event() for _ in range(2)]
+    emph_buf = [torch.empty(E * EMPH_ROW, dtype=torch.uint8, device=dev) for _ in range(2)]
+    env_obs_emph_keep = env.emph
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d = d2h = 0
+    e0.record(stream)
+    for t in range(K):
+        b = t & 1
+        stream.wait_event(done_ev[b]) if t >= 2 else None   # the copy of this buffer two steps ago finished
+        env.bind_obs_pack6(packed[b])
+        env.bind_obs(env.obs, emph_buf[b].view(E, 4, 224))
+        env.actions.copy_(host_acts[t], non_blocking=True)
+        h2d += E * 2
+        env.step()
+        account()
+        if world > 1 and (t + 1) % 128 == 0:
+            dist.all_reduce(counters)
+        # small per-env results on the env's stream (the next step overwrites them), pictures on the copy stream
+        sm = small[t % R]
+        sm[:E * 4].copy_(env.reward.view(torch.uint8), non_blocking=True)
+        sm[E * 4:E * 5].copy_(env.done, non_blocking=True)
+        sm[E * 5:].copy_(env.masks.view(-1), non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        copy.wait_event(ready)
+        with torch.cuda.stream(copy):
+            slot = ring[t % R]
+            slot[:E * PACKED_ROW].copy_(packed[b], non_blocking=True)
+            slot[E * PACKED_ROW:].copy_(emph_buf[b], non_blocking=True)
+        d2h += E * (PACKED_ROW + EMPH_ROW + 4 + 1 + 19)
+        done_ev[b].record(copy)
+    if world > 1:
+        dist.all_reduce(counters)
+    stream.wait_stream(copy)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    env.bind_obs(env.obs, env_obs_emph_keep)
+    e2e_ms = e0.elapsed_time(e1)
+    ems = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+    e2e_value = K * E * world / (float(ems.item()) / 1e3)
+
+    # host link reference: one pinned D2H copy of a step's bytes
+    link = None
+    if rank == 0:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ring[0][:packed[0].numel()].copy_(packed[0], non_blocking=True)
+        t0.record(stream)
+        for _ in range(3):
+            ring[0][:packed[0].numel()].copy_(packed[0], non_blocking=True)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        link = 3 * packed[0].numel() / (t0.elapsed_time(t1) / 1e3) / 1e9
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        launches_r = max(1, tm['launches']['render'])
+        render_ms = tm['ms']['render'] / launches_r
+        env_frames = E * 4
+        alg_bytes = env_frames * (PACKED_ROW // 4 + 224 + 2048 + 256 + 64)   # per launch: packed out, emph, NT, OAM, log header
+        achieved = alg_bytes / (render_ms / 1e3) / 1e9
+        tr = render_traffic_per_env_frame()
+        result = dict(
+            metric=METRIC, value=round(value, 1), unit=UNIT, n_gpus=world, steps=K, warmup=W,
+            ms_per_step=round(ms_max / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
+            data='synthetic (seeded NROM cart synth00, random moves)',
+            config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on', envs_per_gpu=E,
+                        frames_per_decision=4, parallelism=f'dp{world} (env shards, NCCL all-reduce of counters)',
+                        inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)'),
+            frames_per_s=round(4 * value, 1),
+            e2e=dict(value=round(e2e_value, 1), unit=UNIT, h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=d2h // K,
+                     pinned_ring_slots=R, host_link_gbs=round(link, 1) if link else None,
+                     note='packed 6-bit pictures + emphasis + reward/done/masks to a pinned host ring every decision'),
+            roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
+                          traffic=round(tr * env_frames) if tr else None, kernel='k_render',
+                          peak_source=f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured' else 'fallback',
+                          algorithmic_bytes_per_launch=alg_bytes, avg_launch_ms=round(render_ms, 4)),
+            kernel_ms_per_step={k: round(v / K, 4) for k, v in tm['ms'].items()},
+            gpu_launches=tm['total_launches'],
+            clocks=clk.summary(),
+            episodes=dict(finished=float(counters[0].item()), deaths=float(counters[1].item()),
+                          return_sum=float(counters[2].item()), level_events=float(counters[3].item())),
+        )
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def main():
+    args = parse()
+    if args.cpu_leg:
+        cpu_leg(args)
+        return
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    if args.impl == 'reference':
+        # the reference's CPU implementation of the path: the oracle port (the real CPU build needs NeSLE, which
+        # is not vendored), all host threads, a bounded sample of config 2
+        if rank != 0:
+            return
+        r = run_cpu_leg(args, seconds=30.0)
+        line = dict(impl='reference', metric=METRIC, value=round(r['value'], 1), unit=UNIT, n_gpus=world,
+                    steps=r['steps'], warmup=min(args.warmup, 2), ms_per_step=round(1e3 * r['seconds'] / r['steps'], 3),
+                    higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8', data='synthetic',
+                    config=dict(workload='config 2: synthetic NROM, 8192 envs, 4 frames/decision', envs=args.envs),
+                    cpu_baseline=dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
+                                      sample=f"{r['steps']} decisions x {args.envs} envs", cpu=cpu_model()),
+                    e2e=dict(value=round(r['value'], 1), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
+        return
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            r = run_cpu_leg(args, seconds=args.cpu_seconds)
+            cpu = dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
+                       sample=f"{r['steps']} decisions x {args.envs} envs (config 2 workload)", cpu=cpu_model())
+        except Exception as ex:   # reported, never silent
+            cpu = dict(value=None, unit=UNIT, cores=os.cpu_count(), kind='port', sample=f'failed: {ex}'[:200])
+    res = gpu_arm(args)
+    if res is not None:
+        res['cpu_baseline'] = cpu
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == '__main__':
+    main()

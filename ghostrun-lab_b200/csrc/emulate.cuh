@@ -141,12 +141,21 @@ __device__ __forceinline__ u32 v_inc_y(u32 v) {
 
 struct Hit0 { u32 dot; bool hit; };
 
+// Shared-memory staging of one warp's 32 consoles: register words, CPU RAM and OAM, each lane a column (word w of
+// lane l at [w][l]), so every lane touches its own bank whatever addresses the lanes use.
+struct EmuShared {
+    u32 regs[kRegWords][32];
+    u32 ram[kRamWords][32];
+    u32 oam[64][32];
+};
+
 template <u32 BOARD>
 struct Emu {
     const StateView& S;
     const CartView& C;
-    const u32 e;
-    const u32 Np;
+    const u32 e;          // global env slot
+    const u32 lane;       // column in the shared staging
+    EmuShared& sh;
     const u32* __restrict__ dtab;   // decode table (shared memory)
     // hot state (registers for the whole frame loop)
     u32 pc, a, x, y, sp, p, pad;
@@ -160,19 +169,39 @@ struct Emu {
     u32 slot;     // presentation slot of the frame being emulated
     u32 prg_bank; // UxROM
 
-    __device__ Emu(const StateView& s, const CartView& c, u32 env, const u32* dt)
-        : S(s), C(c), e(env), Np(s.Np), dtab(dt) {}
+    __device__ Emu(const StateView& s, const CartView& c, u32 env, u32 ln, EmuShared& shm, const u32* dt)
+        : S(s), C(c), e(env), lane(ln), sh(shm), dtab(dt) {}
 
-    // -------- register-word access (env-minor)
-    __device__ __forceinline__ u32 rw(int w) const { return S.regs[static_cast<u64>(w) * Np + e]; }
-    __device__ __forceinline__ void ww(int w, u32 v) const { S.regs[static_cast<u64>(w) * Np + e] = v; }
+    // -------- staging: global env-minor / env-major arrays <-> this lane's shared column
+    __device__ __forceinline__ void stage_in() const {
+        const u64 Np = S.Np;
+        for (int w = 0; w < kRegWords; ++w) sh.regs[w][lane] = S.regs[static_cast<u64>(w) * Np + e];
+        for (u32 i = 0; i < kRamWords; ++i) sh.ram[i][lane] = S.ram[static_cast<u64>(i) * Np + e];
+        const uint4* o = reinterpret_cast<const uint4*>(S.oam + static_cast<u64>(e) * kOamBytes);
+        for (u32 i = 0; i < 16; ++i) {
+            const uint4 q = o[i];
+            sh.oam[4 * i][lane] = q.x; sh.oam[4 * i + 1][lane] = q.y; sh.oam[4 * i + 2][lane] = q.z; sh.oam[4 * i + 3][lane] = q.w;
+        }
+    }
+    __device__ __forceinline__ void stage_out() const {
+        const u64 Np = S.Np;
+        for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * Np + e] = sh.regs[w][lane];
+        for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * Np + e] = sh.ram[i][lane];
+        uint4* o = reinterpret_cast<uint4*>(S.oam + static_cast<u64>(e) * kOamBytes);
+        for (u32 i = 0; i < 16; ++i)
+            o[i] = make_uint4(sh.oam[4 * i][lane], sh.oam[4 * i + 1][lane], sh.oam[4 * i + 2][lane], sh.oam[4 * i + 3][lane]);
+    }
+
+    // -------- register-word access (shared staging)
+    __device__ __forceinline__ u32 rw(int w) const { return sh.regs[w][lane]; }
+    __device__ __forceinline__ void ww(int w, u32 v) const { sh.regs[w][lane] = v; }
     __device__ __forceinline__ u32 field(int w, int shift, u32 maskv) const { return (rw(w) >> shift) & maskv; }
     __device__ __forceinline__ void set_field(int w, int shift, u32 maskv, u32 v) const {
         const u32 old = rw(w);
         ww(w, (old & ~(maskv << shift)) | ((v & maskv) << shift));
     }
 
-    __device__ void load() {
+    __device__ __forceinline__ void load() {
         const u32 w0 = rw(R_PC_SP_P), w1 = rw(R_AXY_PAD);
         pc = w0 & 0xFFFF; sp = (w0 >> 16) & 0xFF; p = w0 >> 24;
         a = w1 & 0xFF; x = (w1 >> 8) & 0xFF; y = (w1 >> 16) & 0xFF; pad = w1 >> 24;
@@ -189,7 +218,7 @@ struct Emu {
         dma = 0;
         now = 0;
     }
-    __device__ void store() {
+    __device__ __forceinline__ void store() {
         ww(R_PC_SP_P, pc | (sp << 16) | (p << 24));
         ww(R_AXY_PAD, a | (x << 8) | (y << 16) | (pad << 24));
         ww(R_CYC_LO, static_cast<u32>(cycles)); ww(R_CYC_HI, static_cast<u32>(cycles >> 32));
@@ -203,17 +232,20 @@ struct Emu {
     }
 
     // -------- memories
-    __device__ __forceinline__ u8* ram8() const { return reinterpret_cast<u8*>(S.ram); }
-    __device__ __forceinline__ u64 ram_index(u32 addr) const {
-        return ((static_cast<u64>(addr >> 2) * Np + e) << 2) | (addr & 3u);
+    __device__ __forceinline__ u32 ram_rd(u32 addr) const {
+        addr &= 0x7FFu;
+        return reinterpret_cast<const u8*>(&sh.ram[addr >> 2][lane])[addr & 3u];
     }
-    __device__ __forceinline__ u32 ram_rd(u32 addr) const { return ram8()[ram_index(addr & 0x7FFu)]; }
-    __device__ __forceinline__ void ram_wr(u32 addr, u32 v) const { ram8()[ram_index(addr & 0x7FFu)] = static_cast<u8>(v); }
+    __device__ __forceinline__ void ram_wr(u32 addr, u32 v) const {
+        addr &= 0x7FFu;
+        reinterpret_cast<u8*>(&sh.ram[addr >> 2][lane])[addr & 3u] = static_cast<u8>(v);
+    }
     __device__ __forceinline__ u8* prgram8() const { return reinterpret_cast<u8*>(S.prg_ram); }
     __device__ __forceinline__ u64 prgram_index(u32 off) const {
-        return ((static_cast<u64>(off >> 2) * Np + e) << 2) | (off & 3u);
+        return ((static_cast<u64>(off >> 2) * S.Np + e) << 2) | (off & 3u);
     }
-    __device__ __forceinline__ u8* oam() const { return S.oam + static_cast<u64>(e) * kOamBytes; }
+    __device__ __forceinline__ u32 oam_rd(u32 i) const { return reinterpret_cast<const u8*>(&sh.oam[i >> 2][lane])[i & 3u]; }
+    __device__ __forceinline__ void oam_wr(u32 i, u32 v) const { reinterpret_cast<u8*>(&sh.oam[i >> 2][lane])[i & 3u] = static_cast<u8>(v); }
     __device__ __forceinline__ u8* nt() const { return S.nt + static_cast<u64>(e) * kNtBytes; }
     __device__ __forceinline__ u8* pal() const { return S.pal + static_cast<u64>(e) * kPalBytes; }
     __device__ __forceinline__ u8* chr_ram() const { return S.chr_ram + static_cast<u64>(e) * kChrRamBytes; }
@@ -262,13 +294,13 @@ struct Emu {
         if ((i & 0x13u) == 0x10u) i &= 0x0Fu;
         return i;
     }
-    __device__ u32 ppu_mem_rd(u32 addr) const {
+    __device__ __forceinline__ u32 ppu_mem_rd(u32 addr) const {
         addr &= 0x3FFFu;
         if (addr < 0x2000u) return chr_rd(addr);
         if (addr < 0x3F00u) return nt()[nt_off(addr >= 0x3000u ? addr - 0x1000u : addr)];
         return pal()[pal_index(addr)];
     }
-    __device__ void ppu_mem_wr(u32 addr, u32 v) const {
+    __device__ __forceinline__ void ppu_mem_wr(u32 addr, u32 v) const {
         addr &= 0x3FFFu;
         if (addr < 0x2000u) { chr_wr(addr, v); return; }
         if (addr < 0x3F00u) { nt()[nt_off(addr >= 0x3000u ? addr - 0x1000u : addr)] = static_cast<u8>(v); return; }
@@ -278,7 +310,7 @@ struct Emu {
     // -------- frame log
     __device__ __forceinline__ bool log_active() const { return now < kVblankDot || now >= kPreRenderDot; }
 
-    __device__ void log_event(u32 kind, u32 value, u32 aux) {
+    __device__ __forceinline__ void log_event(u32 kind, u32 value, u32 aux) {
         if (!log_active()) return;
         u32* bank = writing_bank();
         if (kind == kEvDataWrite && (mask & 0x18u) == 0 && log_n != 0 && log_n <= kLogEv) {
@@ -292,7 +324,7 @@ struct Emu {
         ++log_n;
     }
 
-    __device__ void fill_header(u32* h) const {
+    __device__ __forceinline__ void fill_header(u32* h) const {
         const u32 vt = rw(R_VT);
         const u32 fx = (rw(R_PPU1) >> 8) & 7u;
         uint4 w0, w1, w2, w3;
@@ -317,7 +349,7 @@ struct Emu {
     }
 
     // pre-render: the writing bank starts over from the live state (patch:1080-1088)
-    __device__ void log_capture() {
+    __device__ __forceinline__ void log_capture() {
         u32* h = writing_bank();
         fill_header(h);
         const bool kook = (log_ctl & kLcNextKook) != 0;
@@ -327,10 +359,14 @@ struct Emu {
     }
 
     // FCEUmm's emphasis tint after the frame in `h` (patch:1087-1118)
-    __device__ static u32 emphasis(const u32* h, u32 previous) {
+    __device__ __forceinline__ static u32 emphasis(const u32* h, u32 previous) {
         const u32* ev = h + kLogHdr;
         const u32 count = h[0] & ~kLogOverflow;
         u32 m = (h[1] >> 8) & 0xFFu;
+        if (count == 0) {   // one mask for every line: its emphasis if it is 1..6, else the previous tint
+            const u32 d = m >> 5;
+            return (d >= 1 && d <= 6) ? d : previous;
+        }
         bool any = (m & 0xE0u) != 0;
         for (u32 i = 0; i < count && !any; ++i) any = (ev[2 * i] >> 24) == kEvMask && (ev[2 * i + 1] & 0xE0u) != 0;
         if (!any) return previous;
@@ -353,15 +389,21 @@ struct Emu {
     }
 
     // Copy 16-byte vectors (both pointers 16-byte aligned).
-    __device__ static void copy16(u8* dst, const u8* src, u32 bytes) {
+    __device__ __forceinline__ static void copy16(u8* dst, const u8* src, u32 bytes) {   // bytes: a multiple of 128
         uint4* d = reinterpret_cast<uint4*>(dst);
         const uint4* s = reinterpret_cast<const uint4*>(src);
-        for (u32 i = 0; i < bytes / 16; ++i) d[i] = s[i];
+        for (u32 i = 0; i < bytes / 16; i += 8) {
+            uint4 q[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) q[k] = s[i + k];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) d[i + k] = q[k];
+        }
     }
 
     // vblank: the writing bank becomes the shown one, and the nametable RAM / OAM (/ CHR-RAM) it is drawn from are
     // frozen into this frame's presentation slot (patch:1121-1130, 2487-2520)
-    __device__ void log_freeze() {
+    __device__ __forceinline__ void log_freeze() {
         const u32 shown = log_ctl & kLcBank;
         u32* h = writing_bank();
         const u32* old = log_bank(shown);
@@ -373,18 +415,18 @@ struct Emu {
         log_ctl = (log_ctl & ~kLcBank) | nb;
         const u64 sl = static_cast<u64>(e) * 4 + slot;
         copy16(S.snap_nt + sl * kNtBytes, nt(), kNtBytes);
-        copy16(S.snap_oam + sl * kOamBytes, oam(), kOamBytes);
+        uint4* so = reinterpret_cast<uint4*>(S.snap_oam + sl * kOamBytes);
+        for (u32 i = 0; i < 16; ++i)
+            so[i] = make_uint4(sh.oam[4 * i][lane], sh.oam[4 * i + 1][lane], sh.oam[4 * i + 2][lane], sh.oam[4 * i + 3][lane]);
         if (S.snap_chr && !C.chr) copy16(S.snap_chr + sl * kChrRamBytes, chr_ram(), kChrRamBytes);
         S.slot_bank[sl] = static_cast<u8>(nb);
         ww(R_FSLOT, slot);
     }
 
-    // -------- sprite-0 hit from the log so far (patch:1740-1789), exact, with a closed-form fast path for lines
-    // the log does not touch while they are drawn.
-    __device__ Hit0 sprite0_eval();
+    __device__ __forceinline__ Hit0 sprite0_eval() const;
 
     // -------- PPU settle (patch:2114-2240)
-    __device__ u32 dots_to_event() const {
+    __device__ __forceinline__ u32 dots_to_event() const {
         const u32 cur = frame_dot;
         const u32 skip = (log_ctl & kLcShort) ? 1u : 0u;
         const u32 fd = kFrameDots - skip;
@@ -414,7 +456,7 @@ struct Emu {
         return next;
     }
 
-    __device__ void mmc3_clock() {
+    __device__ __forceinline__ void mmc3_clock() {
         u32 cnt = mreg(12), latch = mreg(11), reload = mreg(14);
         if (cnt == 0 || reload) { cnt = latch; set_mreg(14, 0); }
         else --cnt;
@@ -422,7 +464,7 @@ struct Emu {
         if (cnt == 0 && mreg(13)) set_field(R_IO, 24, 0xFF, 1);
     }
 
-    __device__ void settle(u32 dots) {
+    __device__ __forceinline__ void settle(u32 dots) {
         const u32 start = frame_dot;
         u32 end = start + dots;
         if ((log_ctl & kLcShort) && end >= kFrameDots - 1) end += 1;
@@ -450,7 +492,7 @@ struct Emu {
             if (crossed(kPreRenderDot)) {
                 status &= 0x1Fu;
                 log_capture();
-                const u32 y0 = oam()[0];
+                const u32 y0 = oam_rd(0);
                 ww(R_S0, y0 < 239u ? (nesle_dot(static_cast<int>(y0 + 1) * 341 - 20) | kS0Evaluate) : 0u);
             }
         }
@@ -471,7 +513,7 @@ struct Emu {
     }
 
     // -------- CPU bus
-    __device__ u32 rd_io(u32 addr) {
+    __device__ __forceinline__ u32 rd_io(u32 addr) {
         if (addr < 0x4000u) {
             switch (addr & 7u) {
                 case 2: {
@@ -481,7 +523,7 @@ struct Emu {
                     set_field(R_PPU1, 16, 0xFF, 0);
                     return v;
                 }
-                case 4: return oam()[oam_addr];
+                case 4: return oam_rd(oam_addr);
                 case 7: {
                     u32 vt = rw(R_VT);
                     const u32 v16 = vt & 0xFFFFu;
@@ -530,7 +572,7 @@ struct Emu {
         return rd_io(addr);
     }
 
-    __device__ void mmc1_sync() {
+    __device__ __forceinline__ void mmc1_sync() {
         const u32 ctl = mreg(0), offs = mreg(1) & 0x10u, prg = mreg(3);
         auto prg8 = [&](u32 s, u32 b) { ww(R_PRGPG + s, (b & C.prg_page_mask) << 13); };
         auto prg16 = [&](u32 s, u32 b) { prg8(2 * s, 2 * b); prg8(2 * s + 1, 2 * b + 1); };
@@ -546,7 +588,7 @@ struct Emu {
             set_field(R_PPU2, 24, 0xFF, map);
         }
     }
-    __device__ void mmc3_sync() {
+    __device__ __forceinline__ void mmc3_sync() {
         const u32 sel = mreg(8), r6 = mreg(6) & 0x7Fu;
         auto prg8 = [&](u32 s, u32 b) { ww(R_PRGPG + s, (b & C.prg_page_mask) << 13); };
         auto chr1 = [&](u32 s, u32 b) { ww(R_CHRPG + s, (b & C.chr_page_mask) << 10); };
@@ -560,7 +602,7 @@ struct Emu {
         if (C.arrangement != 2) set_field(R_PPU2, 24, 0xFF, (mreg(9) & 1u) ? kPageHorizontal : kPageVertical);
     }
 
-    __device__ void board_write(u32 addr, u32 v) {
+    __device__ __forceinline__ void board_write(u32 addr, u32 v) {
         if constexpr (BOARD == kMmc1) {
             if (v & 0x80u) { set_mreg(0, mreg(0) | 0x0Cu); set_mreg(4, 0); set_mreg(5, 0); mmc1_sync(); return; }
             const u32 cnt = mreg(5);
@@ -585,7 +627,7 @@ struct Emu {
         }
     }
 
-    __device__ void mapper_write(u32 addr, u32 v) {
+    __device__ __forceinline__ void mapper_write(u32 addr, u32 v) {
         if constexpr (BOARD == kUxrom) {
             prg_bank = v & C.bank_mask;
         } else if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
@@ -605,7 +647,7 @@ struct Emu {
         }
     }
 
-    __device__ void wr_io(u32 addr, u32 v) {
+    __device__ __forceinline__ void wr_io(u32 addr, u32 v) {
         if (addr < 0x4000u) {
             switch (addr & 7u) {
                 case 0: {
@@ -618,7 +660,7 @@ struct Emu {
                 }
                 case 1: mask = v; log_event(kEvMask, v, 0); break;
                 case 3: oam_addr = v; break;
-                case 4: oam()[oam_addr] = static_cast<u8>(v); oam_addr = (oam_addr + 1) & 0xFFu; break;
+                case 4: oam_wr(oam_addr, v); oam_addr = (oam_addr + 1) & 0xFFu; break;
                 case 5: {
                     const u32 p1 = rw(R_PPU1);
                     const u32 w = (p1 >> 16) & 0xFFu;
@@ -671,16 +713,13 @@ struct Emu {
             return;
         }
         if (addr == 0x4014u) {
-            // OAM DMA: 256 bytes from page v; RAM pages are copied as words
-            u8* o = oam();
+            // OAM DMA: 256 bytes from page v; a RAM page into OAM from address 0 is copied as words
             if (v < 0x20u && oam_addr == 0) {
-                const u32 base = (v & 7u) << 8;
-                for (u32 i = 0; i < 64; ++i) {
-                    const u32 w = S.ram[static_cast<u64>((base >> 2) + i) * Np + e];
-                    reinterpret_cast<u32*>(o)[i] = w;
-                }
+                const u32 base = ((v & 7u) << 8) >> 2;
+#pragma unroll 8
+                for (u32 i = 0; i < 64; ++i) sh.oam[i][lane] = sh.ram[base + i][lane];
             } else {
-                for (u32 i = 0; i < 256; ++i) o[(oam_addr + i) & 0xFFu] = static_cast<u8>(rd((v << 8) + i));
+                for (u32 i = 0; i < 256; ++i) oam_wr((oam_addr + i) & 0xFFu, rd((v << 8) + i));
             }
             dma = 1;
             return;
@@ -717,7 +756,7 @@ struct Emu {
     }
 
     // -------- DMC (patch:480-547)
-    __device__ u32 dmc_service(u64 nowc, bool steal) {
+    __device__ __forceinline__ u32 dmc_service(u64 nowc, bool steal) {
         u64 be = rw(R_DMC_END) | (static_cast<u64>(rw(R_DMC_END + 1)) << 32);
         const u32 da = rw(R_DMC_A), db = rw(R_DMC_B);
         u32 bytes_left = da & 0xFFFFu, control = (da >> 16) & 0xFF, length = da >> 24;
@@ -762,7 +801,7 @@ struct Emu {
     __device__ __forceinline__ void nz(u32 v) { p = (p & ~(FZ | FN)) | (v == 0 ? FZ : 0u) | (v & 0x80u); }
     __device__ __forceinline__ u32 fetch(u32 addr) { return addr >= 0x8000u ? prg_rd(addr) : rd(addr); }
 
-    __device__ void interrupt(u32 vector) {
+    __device__ __forceinline__ void interrupt(u32 vector) {
         push(pc >> 8);
         push(pc & 0xFFu);
         push((p & ~FB) | FU);
@@ -773,17 +812,26 @@ struct Emu {
 
     struct Step { u32 cycles, opcode, pc; bool illegal; };
 
-    __device__ Step step6502() {
+    __device__ __forceinline__ Step step6502() {
         const u32 pc0 = pc;
-        const u32 op = fetch(pc0);
+        // opcode and both operand bytes fetched together (PRG: three independent loads)
+        u32 op, b1, b2;
+        if (pc0 >= 0x8000u && pc0 <= 0xFFFDu) {
+            op = prg_rd(pc0); b1 = prg_rd(pc0 + 1); b2 = prg_rd(pc0 + 2);
+        } else {
+            op = fetch(pc0); b1 = 0; b2 = 0;
+        }
         const u32 d = dtab[op];
         const u32 mode = d & 15u, opn = (d >> 4) & 63u;
         u32 cyc = (d >> 10) & 15u;
         if (opn == O_ILL) return Step{0, op, pc0, true};
+        if (pc0 < 0x8000u || pc0 > 0xFFFDu) {
+            if (mode >= M_IMM) b1 = fetch((pc0 + 1) & 0xFFFFu);
+            if (mode >= M_ABS && mode <= M_IND) b2 = fetch((pc0 + 2) & 0xFFFFu);
+        }
         // ---- operand / effective address
         u32 ea = 0, val = 0;
         bool cross = false;
-        const u32 b1 = (mode >= M_IMM) ? fetch((pc0 + 1) & 0xFFFFu) : 0u;
         switch (mode) {
             case M_IMP: case M_ACC: pc = pc0 + 1; break;
             case M_IMM: pc = pc0 + 2; break;
@@ -805,7 +853,7 @@ struct Emu {
                 break;
             }
             default: {   // ABS, ABSX, ABSY, IND
-                const u32 base = b1 | (fetch((pc0 + 2) & 0xFFFFu) << 8);
+                const u32 base = b1 | (b2 << 8);
                 const u32 idx = mode == M_ABSX ? x : mode == M_ABSY ? y : 0u;
                 ea = (base + idx) & 0xFFFFu;
                 cross = ((base ^ ea) & 0xFF00u) != 0;
@@ -925,7 +973,7 @@ struct Emu {
     }
 
     // One instruction with NMI / IRQ entry, frame-log stamps, DMA stall and DMC steals (patch:834-861).
-    __device__ Step console_step(u32 pending, u32& ppu_cycles) {
+    __device__ __forceinline__ Step console_step(u32 pending, u32& ppu_cycles) {
         const u64 before = cycles;
         if (nmi) {
             nmi = 0;
@@ -948,7 +996,7 @@ struct Emu {
         return s;
     }
 
-    __device__ void fast_forward() {
+    __device__ __forceinline__ void fast_forward() {
         if (nmi) return;
         const u32 jumps = (dots_to_event() + 8u) / 9u;
         if (jumps == 0) return;
@@ -959,30 +1007,37 @@ struct Emu {
     }
 
     // Run to absolute PPU dot `target` (rl/csrc/nes_machine.cuh:67-103). Returns pc << 8 | opcode on a fault.
-    __device__ u32 step_until(u64 target) {
+    // Called by all 32 lanes of the warp together (`run` false for lanes with nothing to emulate). Lanes drift to
+    // different 6502 addresses after a divergent branch; each loop turn only the lanes at the lowest program counter
+    // execute, so lanes that skipped a block wait for the others and the warp runs one instruction body per turn.
+    // Every lane's own state advances exactly as in the sequential loop.
+    __device__ __forceinline__ u32 step_until(u64 target, bool run) {
         u32 fault = 0, pending = 0;
-        u32 to_event = dots_to_event();
+        u32 to_event = run ? dots_to_event() : 0u;
         u32 instructions = 0;
-        bool done = false;
-        while (instructions < kBudget && !done) {
+        bool going = run;
+        while (__any_sync(0xFFFFFFFFu, going)) {
+            const u32 lead = __reduce_min_sync(0xFFFFFFFFu, going ? pc : 0x10000u);
+            if (!going || pc != lead) continue;
+            if (instructions >= kBudget) { going = false; continue; }
             if (pending >= to_event) {
                 settle(pending);
                 pending = 0;
                 to_event = dots_to_event();
-                if (frame * kFrameDots + frame_dot >= target) break;
+                if (frame * kFrameDots + frame_dot >= target) { going = false; continue; }
             }
             u32 pc_cycles;
             const Step st = console_step(pending, pc_cycles);
-            if (st.illegal) { fault = (st.pc << 8) | st.opcode; break; }
+            if (st.illegal) { fault = (st.pc << 8) | st.opcode; going = false; continue; }
             pending += pc_cycles;
             ++instructions;
             if (st.opcode == 0x4Cu && pc == st.pc) {
                 settle(pending);
                 pending = 0;
-                if (frame * kFrameDots + frame_dot >= target) break;
+                if (frame * kFrameDots + frame_dot >= target) { going = false; continue; }
                 fast_forward();
                 to_event = dots_to_event();
-                done = frame * kFrameDots + frame_dot >= target;
+                if (frame * kFrameDots + frame_dot >= target) going = false;
             }
         }
         if (pending != 0) settle(pending);
@@ -991,7 +1046,7 @@ struct Emu {
 
     // End of a frame: presentation slot `slot` holds the last frozen frame (copied forward when no vblank froze one
     // during this frame, e.g. a faulted console).
-    __device__ void finish_slot() {
+    __device__ __forceinline__ void finish_slot() {
         const u32 fs = rw(R_FSLOT);
         if (fs == slot) return;
         const u64 a0 = static_cast<u64>(e) * 4 + fs, b0 = static_cast<u64>(e) * 4 + slot;
@@ -1004,46 +1059,58 @@ struct Emu {
 };
 
 // ------------------------------------------------------------------------------------------------ sprite-0 hit
+// FCEUmm's sprite-0 hit from the frame log written so far (patch:1740-1789 frame_sprite0_hit): the replay of lines 0
+// to sprite 0's last line with the check at each line's end. Exact, with closed forms where the log does not touch
+// a line: lines above sprite 0 only step the PPU address (no memory access), and a line drawn without writes needs
+// only the two background tiles under sprite 0. Lines with writes inside their drawn part take the exact tile loop.
+// Out of line and by value, so the emulator's registers never have their address taken.
 
-// Replay state the sprite-0 check needs: PPU address/scroll/control, board CHR/mirroring, sprite-0 scheduling.
+struct S0Ctx {
+    const u32* bank;      // the writing log bank
+    u32 count;
+    const u8* nt;         // live nametable RAM of the env
+    const u32* soam;      // OAM word 0 of the env's shared column (stride 32 words)
+    const u8* chr;        // CHR ROM (nullptr: chr_ram)
+    const u8* chr_ram;    // the env's CHR-RAM
+    u32 chr_size, chr_page_mask, arrangement;
+};
+
 struct S0State {
     u32 v, t, x, ctrl, mask, mirroring;
     u32 chr[8];
     u32 cursor;
-    // last two tile fetches (shift registers) as (lo plane, hi plane, attribute) of tiles (n-2, n-1)
-    u32 sh0, sh1, at;
-    // sprite fetch (FetchSpriteData) and RefreshSprites state, sprite 0 only
+    u32 sh0, sh1, at;          // tile shift registers after the last drawn tiles
+    u32 lazy, lz_v, lz_ctrl;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
+    u32 lz_chr[8], lz_mirroring;
     u32 fetched_n, blurp, f_lo0, f_hi0, f_attr0, f_x0;
     u32 sphitx, sphitdata, hit, hit_x;
 };
 
 template <u32 BOARD>
-__device__ __forceinline__ u32 s0_chr(const Emu<BOARD>& m, const S0State& s, u32 addr) {
+__device__ __forceinline__ u32 s0_chr(const S0Ctx& c, const u32* chr_pages, u32 addr) {
     addr &= 0x1FFFu;
     if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
-        const u32 off = ((s.chr[addr >> 10] & m.C.chr_page_mask) << 10) | (addr & 0x3FFu);
-        return m.C.chr ? __ldg(m.C.chr + off) : m.chr_ram()[off & 0x1FFFu];
+        const u32 off = ((chr_pages[addr >> 10] & c.chr_page_mask) << 10) | (addr & 0x3FFu);
+        return c.chr ? __ldg(c.chr + off) : c.chr_ram[off & 0x1FFFu];
     } else {
-        return m.C.chr ? __ldg(m.C.chr + (addr % m.C.chr_size)) : m.chr_ram()[addr];
+        return c.chr ? __ldg(c.chr + (addr % c.chr_size)) : c.chr_ram[addr];
     }
 }
 
+// One tile fetch at PPU address v: lo | hi << 8 | attribute << 16.
 template <u32 BOARD>
-__device__ __forceinline__ u32 s0_nt(const Emu<BOARD>& m, const S0State& s, u32 addr) {
-    if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return m.nt()[nt_off_map(s.mirroring, addr)];
-    else return m.nt()[nt_off_header(m.C.arrangement, addr)];
-}
-
-// One tile fetch at PPU address v: returns lo | hi << 8 | attribute << 16.
-template <u32 BOARD>
-__device__ __forceinline__ u32 s0_fetch(const Emu<BOARD>& m, const S0State& s, u32 v) {
+__device__ __forceinline__ u32 s0_fetch(const S0Ctx& c, u32 ctrl, const u32* chr_pages, u32 mirroring, u32 v) {
+    auto ntrd = [&](u32 addr) -> u32 {
+        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return c.nt[nt_off_map(mirroring, addr)];
+        else return c.nt[nt_off_header(c.arrangement, addr)];
+    };
     const u32 base = 0x2000u | (v & 0x0C00u);
-    const u32 tile = s0_nt(m, s, base | (v & 0x3FFu));
+    const u32 tile = ntrd(base | (v & 0x3FFu));
     const u32 zz = v & 0x1Fu;
-    const u32 ab = s0_nt(m, s, base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
+    const u32 ab = ntrd(base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
     const u32 cc = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
-    const u32 vadr = (tile << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
-    return s0_chr(m, s, vadr) | (s0_chr(m, s, vadr + 8u) << 8) | (cc << 16);
+    const u32 vadr = (tile << 4) + (((ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
+    return s0_chr<BOARD>(c, chr_pages, vadr) | (s0_chr<BOARD>(c, chr_pages, vadr + 8u) << 8) | (cc << 16);
 }
 
 __device__ __forceinline__ void s0_apply(S0State& s, const u32* ev, u32 i, bool drawing) {
@@ -1073,12 +1140,24 @@ __device__ __forceinline__ void s0_apply(S0State& s, const u32* ev, u32 i, bool 
     }
 }
 
-// The exact FCEUmm tile loop of one line with writes landing inside it (rare on the benchmark carts): keeps only
-// each drawn pixel's "opaque background" bit, which is all the sprite-0 check reads.
 template <u32 BOARD>
-__device__ __noinline__ void s0_event_line(const Emu<BOARD>& m, S0State& s, const u32* ev, u32 count, int kook,
-                                           int l, bool pixels) {
-    u32 opq[8];   // opaque bits of pixels 0..255
+__device__ void s0_materialize(const S0Ctx& c, S0State& s) {
+    if (!s.lazy) return;
+    const u32 f32 = s0_fetch<BOARD>(c, s.lz_ctrl, s.lz_chr, s.lz_mirroring, v_inc_x_n(s.lz_v, 32));
+    const u32 f33 = s0_fetch<BOARD>(c, s.lz_ctrl, s.lz_chr, s.lz_mirroring, v_inc_x_n(s.lz_v, 33));
+    s.sh0 = ((f32 & 0xFFu) << 8) | (f33 & 0xFFu);
+    s.sh1 = (((f32 >> 8) & 0xFFu) << 8) | ((f33 >> 8) & 0xFFu);
+    s.at = ((f32 >> 16) & 3u) | (((f33 >> 16) & 3u) << 2);
+    s.lazy = 0;
+}
+
+// The exact FCEUmm tile loop of one line with writes landing inside it: keeps each drawn pixel's "opaque
+// background" bit, which is all the sprite-0 check reads.
+template <u32 BOARD>
+__device__ void s0_event_line(const S0Ctx& c, S0State& s, int kook, int l, bool pixels) {
+    s0_materialize<BOARD>(c, s);
+    const u32* ev = c.bank + kLogHdr;
+    u32 opq[8];
     for (int i = 0; i < 8; ++i) opq[i] = 0;
     const int start = l * 341 - 16;
     int firsttile = 0, outpos = 0;
@@ -1090,7 +1169,7 @@ __device__ __noinline__ void s0_event_line(const Emu<BOARD>& m, S0State& s, cons
             if (tile >= 2) {
                 if (pixels && outpos < 256) {
                     const u32 lo = ((s.sh0 >> (8 - s.x)) & 0xFFu), hi = ((s.sh1 >> (8 - s.x)) & 0xFFu);
-                    const u32 o = lo | hi;   // bit 7 - k = pixel k opaque
+                    const u32 o = lo | hi;
                     for (int k = 0; k < 8; ++k) {
                         const int px = outpos + k;
                         const u32 bit = (o >> (7 - k)) & 1u;
@@ -1099,10 +1178,10 @@ __device__ __noinline__ void s0_event_line(const Emu<BOARD>& m, S0State& s, cons
                 }
                 outpos += 8;
             }
-            const u32 f = s0_fetch(m, s, s.v);
+            const u32 f = s0_fetch<BOARD>(c, s.ctrl, s.chr, s.mirroring, s.v);
             s.at = ((s.at >> 2) | (((f >> 16) & 3u) << 2)) & 0xFu;
-            s.sh0 = (s.sh0 << 8) | (f & 0xFFu);
-            s.sh1 = (s.sh1 << 8) | ((f >> 8) & 0xFFu);
+            s.sh0 = ((s.sh0 << 8) | (f & 0xFFu)) & 0xFFFFu;
+            s.sh1 = ((s.sh1 << 8) | ((f >> 8) & 0xFFu)) & 0xFFFFu;
             s.v = v_inc_x(s.v);
         }
         if (pixels) {
@@ -1132,7 +1211,7 @@ __device__ __noinline__ void s0_event_line(const Emu<BOARD>& m, S0State& s, cons
         if (pp >= 268 && tofix) { if (s.mask & 0x18u) s.v = v_inc_y(s.v); tofix = false; }
         if (pixels) check(pp);
     };
-    while (s.cursor < count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272) {
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272) {
         const u32 kind = ev[2 * s.cursor] >> 24;
         if (kind != kEvDataWrite && kind != kEvPalette)
             update(fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) + 3 * static_cast<int>((ev[2 * s.cursor] >> 17) & 0xFu) - start);
@@ -1144,13 +1223,12 @@ __device__ __noinline__ void s0_event_line(const Emu<BOARD>& m, S0State& s, cons
 }
 
 template <u32 BOARD>
-__device__ Hit0 Emu<BOARD>::sprite0_eval() {
-    const u32* h = writing_bank();
+__device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
+    const u32* h = c.bank;
     const u32* ev = h + kLogHdr;
-    const u32 count = log_n < kLogEv ? log_n : kLogEv;
     const int kook = (h[15] & kLogKook) ? 1 : 0;
-    const u8* o = oam();
-    const u32 oy = o[0], otile = o[1], oattr = o[2], ox = o[3];
+    auto oamb = [&](u32 i) -> u32 { return reinterpret_cast<const u8*>(c.soam + (i >> 2) * 32)[i & 3u]; };
+    const u32 oy = oamb(0), otile = oamb(1), oattr = oamb(2), ox = oamb(3);
     const int first = static_cast<int>(oy) + 1;
     if (first >= 240) return Hit0{0, false};
     S0State s;
@@ -1160,40 +1238,57 @@ __device__ Hit0 Emu<BOARD>::sprite0_eval() {
     s.mirroring = h[5] & 0xFFu;
     s.cursor = 0;
     s.sh0 = s.sh1 = s.at = 0;
+    s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mirroring = 0;
+    for (int i = 0; i < 8; ++i) s.lz_chr[i] = 0;
     s.fetched_n = 0; s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
     s.sphitx = 0x100u; s.sphitdata = 0; s.hit = 0; s.hit_x = 0;
-    while (s.cursor < count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply(s, ev, s.cursor++, false);
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply(s, ev, s.cursor++, false);
     if (s.mask & 0x18u) s.v = s.t;
     const int last = first + 15 < 239 ? first + 15 : 239;
-    for (int l = 0; l <= last; ++l) {
+    int l = 0;
+    // lines above sprite 0 with no write anywhere in them: only the PPU address moves
+    {
+        const int next_ev = s.cursor < c.count ? fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) : 0x7FFFFFFF;
+        if (s.mask & 0x18u) {
+            while (l < first - 1 && (l + 1) * 341 - 16 <= next_ev) {
+                s.lazy = 1; s.lz_v = s.v; s.lz_ctrl = s.ctrl;
+                s.v = (v_inc_y(v_inc_x_n(s.v, 34)) & 0xFBE0u) | (s.t & 0x041Fu);
+                ++l;
+            }
+            if (s.lazy) {
+                s.lz_mirroring = s.mirroring;
+                for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
+            }
+        } else {
+            while (l < first - 1 && (l + 1) * 341 - 16 <= next_ev) ++l;
+        }
+    }
+    for (; l <= last; ++l) {
         const int start = l * 341 - 16;
         const bool pixels = l >= first;
         const u32 sphitx0 = s.sphitx;
-        if (s.cursor < count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272) {
-            s0_event_line(*this, s, ev, count, kook, l, pixels);
+        if (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272) {
+            s0_event_line<BOARD>(c, s, kook, l, pixels);
         } else if (s.mask & 0x18u) {
-            // no writes while the line is drawn: 34 tile fetches from v, pixels 0..255 from fetches 0..33
             const u32 v0 = s.v;
             if (pixels && s.sphitx != 0x100u && (s.mask & 0x08u)) {
+                // the (at most) two tiles under pixels sphitx..sphitx+7
                 const u32 sx = s.sphitx;
-                for (u32 xx = sx; xx < sx + 8u && xx < 255u; ++xx) {
-                    if (!(s.sphitdata & (0x80u >> (xx - sx)))) continue;
-                    if (xx < 8u && !(s.mask & 0x02u)) continue;   // left 8 pixels hidden
-                    const u32 q = xx + s.x;
-                    const u32 f = s0_fetch(*this, s, v_inc_x_n(v0, q >> 3));
-                    const u32 bit = 7u - (q & 7u);
-                    if (((f >> bit) & 1u) | ((f >> (8u + bit)) & 1u)) { s.hit = 1; s.hit_x = xx; s.sphitx = 0x100u; break; }
-                }
+                const u32 q = sx + s.x, j0 = q >> 3, r = q & 7u;
+                const u32 fa = s0_fetch<BOARD>(c, s.ctrl, s.chr, s.mirroring, v_inc_x_n(v0, j0));
+                const u32 fb = r ? s0_fetch<BOARD>(c, s.ctrl, s.chr, s.mirroring, v_inc_x_n(v0, j0 + 1)) : 0u;
+                const u32 o16 = (((fa | (fa >> 8)) & 0xFFu) << 8) | ((fb | (fb >> 8)) & 0xFFu);
+                u32 win = (o16 >> (8 - r)) & 0xFFu;               // bit 7 - k: pixel sx + k opaque
+                if (sx < 8 && !(s.mask & 0x02u)) win &= (1u << sx) - 1u;     // left 8 pixels hidden
+                if (sx + 8 > 255) win &= (0xFF00u >> (255 - sx)) & 0xFFu;
+                const u32 hits = win & s.sphitdata;
+                if (hits) { s.hit = 1; s.hit_x = sx + (__clz(hits) - 24); s.sphitx = 0x100u; }
             }
-            const u32 f32 = s0_fetch(*this, s, v_inc_x_n(v0, 32));
-            const u32 f33 = s0_fetch(*this, s, v_inc_x_n(v0, 33));
-            s.sh0 = ((f32 & 0xFFu) << 8) | (f33 & 0xFFu);
-            s.sh1 = (((f32 >> 8) & 0xFFu) << 8) | ((f33 >> 8) & 0xFFu);
-            s.at = ((f32 >> 16) & 3u) | (((f33 >> 16) & 3u) << 2);
+            s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mirroring = s.mirroring;
+            for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
             s.v = v_inc_y(v_inc_x_n(v0, 34));
         }
         if (s.hit) {
-            // first pixel at which a 4-cycle $2002 read sees the flag (patch:1762-1773)
             const int hx = static_cast<int>(s.hit_x), spx = static_cast<int>(sphitx0);
             int pp = hx + 17;
             for (;; ++pp) {
@@ -1204,7 +1299,7 @@ __device__ Hit0 Emu<BOARD>::sprite0_eval() {
             }
             return Hit0{nesle_dot(l * 341 - 16 + pp - 12), true};
         }
-        // end of line: sprite fetch for line l + 1 (sprite 0 only matters), Fixit2, RefreshSprites
+        // end of line: sprite fetch for line l + 1 (only sprite 0 matters), Fixit2, RefreshSprites
         s.sphitx = 0x100u;
         if ((s.mask & 0x18u) && l >= first - 1) {
             const u32 hgt = (s.ctrl & 0x20u) ? 16u : 8u;
@@ -1217,31 +1312,40 @@ __device__ Hit0 Emu<BOARD>::sprite0_eval() {
                 if (oattr & 0x80u) { vadr += 7u; vadr -= tt; vadr += (s.ctrl & 0x20u) >> 1; vadr -= tt & 8u; }
                 else { vadr += tt; vadr += tt & 8u; }
                 vadr &= 0x1FFFu;
-                s.f_lo0 = s0_chr(*this, s, vadr);
-                s.f_hi0 = s0_chr(*this, s, vadr + 8u);
+                s.f_lo0 = s0_chr<BOARD>(c, s.chr, vadr);
+                s.f_hi0 = s0_chr<BOARD>(c, s.chr, vadr + 8u);
                 s.f_attr0 = oattr; s.f_x0 = ox;
                 s.fetched_n = 1;
             } else {
-                // sprite 0 not on the next line: whether another sprite is only matters for `fetched_n`
                 u32 any = 0;
-                for (u32 n = 1; n < 64 && !any; ++n) any = static_cast<u32>(l - static_cast<int>(o[4 * n])) < hgt;
+                for (u32 n = 1; n < 64 && !any; ++n) any = static_cast<u32>(l - static_cast<int>(oamb(4 * n))) < hgt;
                 s.fetched_n = any;
             }
         }
-        while (s.cursor < count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply(s, ev, s.cursor++, true);
+        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply(s, ev, s.cursor++, true);
         if (s.mask & 0x18u) s.v = (s.v & 0xFBE0u) | (s.t & 0x041Fu);
-        while (s.cursor < count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply(s, ev, s.cursor++, true);
+        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply(s, ev, s.cursor++, true);
         if ((s.mask & 0x10u) && s.fetched_n && s.blurp && !s.hit) {
             const u32 j = s.f_lo0 | s.f_hi0;
-            if (j) {
-                u32 data = j;
-                if (s.f_attr0 & 0x40u) { data = __brev(j) >> 24; }
-                s.sphitx = s.f_x0;
-                s.sphitdata = data;
-            }
+            if (j) { s.sphitx = s.f_x0; s.sphitdata = (s.f_attr0 & 0x40u) ? (__brev(j) >> 24) : j; }
         }
     }
     return Hit0{nesle_dot(last * 341 + 256), false};
+}
+
+template <u32 BOARD>
+__device__ __forceinline__ Hit0 Emu<BOARD>::sprite0_eval() const {
+    S0Ctx c;
+    c.bank = writing_bank();
+    c.count = log_n < kLogEv ? log_n : kLogEv;
+    c.nt = nt();
+    c.soam = &sh.oam[0][lane];
+    c.chr = C.chr;
+    c.chr_ram = C.chr ? nullptr : chr_ram();
+    c.chr_size = C.chr_size;
+    c.chr_page_mask = C.chr_page_mask;
+    c.arrangement = C.arrangement;
+    return sprite0_hit<BOARD>(c);
 }
 
 }  // namespace gr

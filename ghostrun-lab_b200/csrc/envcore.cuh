@@ -263,6 +263,7 @@ struct EnvArgs {
     const int16_t* actions;
     u8* obs; u8* emph; float* reward; u8* done; u8* masks; u8* timeline; u8* pads; u32* events; float* info;
     float* parts;
+    u8* packed;     // optional [N, 4, 224, 180] packed 6-bit pictures (replaces obs when set)
     u64 run_seed;
     i32 sticky, idle_max, dropout, no_render, episode_level_end;
 };
@@ -325,34 +326,26 @@ static __device__ void gather_record(const StateView& S, u32 e, u8* rec, bool ch
 static __device__ void write_controls(const GameArgs& g, const EnvArgs& A, u32 ge) {
     const Dropout& d = A.drop[ge];
     const int dr = dropped_now(d);
-    u32 dp = 0x1FF, ma = 7, mb = 7, ms = g.start_ok ? 3u : 1u, msel = g.select_ok ? 3u : 1u;
+    u32 dp = 0x1FF, ma = 7, mb = 7;
+    const u32 ms = g.start_ok ? 3u : 1u, msel = g.select_ok ? 3u : 1u;
     if (dr >= 0 && dr < 4) for (u32 k = 0; k < 9; ++k) if (dpad_bits(k) & (0x10u << dr)) dp &= ~(1u << k);
     if (dr == 4) ma &= ~2u;
     if (dr == 6) ma &= ~4u;
     if (dr == 5) mb &= ~2u;
     if (dr == 7) mb &= ~4u;
-    u8 m[20];
-    for (int i = 0; i < 9; ++i) m[i] = (dp >> i) & 1u;
-    for (int i = 0; i < 3; ++i) m[9 + i] = (ma >> i) & 1u;
-    for (int i = 0; i < 3; ++i) m[12 + i] = (mb >> i) & 1u;
-    for (int i = 0; i < 2; ++i) m[15 + i] = (ms >> i) & 1u;
-    for (int i = 0; i < 2; ++i) m[17 + i] = (msel >> i) & 1u;
     u8* mo = A.masks + static_cast<u64>(ge) * kMaskBytes;
-    for (int i = 0; i < kMaskBytes; ++i) mo[i] = m[i];
+    for (int i = 0; i < 9; ++i) mo[i] = (dp >> i) & 1u;
+    for (int i = 0; i < 3; ++i) mo[9 + i] = (ma >> i) & 1u;
+    for (int i = 0; i < 3; ++i) mo[12 + i] = (mb >> i) & 1u;
+    for (int i = 0; i < 2; ++i) mo[15 + i] = (ms >> i) & 1u;
+    for (int i = 0; i < 2; ++i) mo[17 + i] = (msel >> i) & 1u;
+    // timeline [8, 45]: zeros, then a 1 where input b is off at decision now + j
     u8* tl = A.timeline + static_cast<u64>(ge) * kTimelineBytes;
-    // 360 bytes = 90 words: zero, then the dropped inputs
-    u8 row[kTimelineBytes];
-    for (int i = 0; i < kTimelineBytes; ++i) row[i] = 0;
+    u32* tw = reinterpret_cast<u32*>(tl);   // 360 bytes per env: 4-byte aligned rows
+    for (int i = 0; i < kTimelineBytes / 4; ++i) tw[i] = 0u;
     for (int j = 0; j < kTimeline; ++j) {
         const int b = d.ring[(d.head + j) % kRing];
-        if (b >= 0) row[b * kTimeline + j] = 1;
-    }
-    if ((reinterpret_cast<uintptr_t>(tl) & 3u) == 0) {
-        for (int i = 0; i < kTimelineBytes / 4; ++i) {
-            reinterpret_cast<u32*>(tl)[i] = row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) | (static_cast<u32>(row[4 * i + 3]) << 24);
-        }
-    } else {
-        for (int i = 0; i < kTimelineBytes; ++i) tl[i] = row[i];
+        if (b >= 0) tl[b * kTimeline + j] = 1;
     }
 }
 
@@ -384,69 +377,87 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-// Emulation: `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for listed envs.
+// Emulation, one warp = 32 envs per block, consoles staged in shared memory for the whole launch.
+// `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for the listed envs.
+constexpr std::size_t kFramesSmem = sizeof(EmuShared) + 256 * sizeof(u32);
+
 template <u32 BOARD>
-__global__ void __launch_bounds__(128) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
-    __shared__ u32 dtab[256];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) dtab[i] = kDecode.t[i];
-    __syncthreads();
-    u32 total = g.n;
-    if (restart) total = *A.list_count;
-    for (u32 k = blockIdx.x * blockDim.x + threadIdx.x; k < total; k += gridDim.x * blockDim.x) {
-        const u32 ge = restart ? A.list[k] : g.e0 + k;
-        if (restart && (ge < g.e0 || ge >= g.e0 + g.n)) continue;
-        Emu<BOARD> m(A.st, g.cart, ge, dtab);
-        m.load();
-        if (!restart) {
-            const int dr = dropped_now(A.drop[ge]);
-            u64 sctr = A.sticky_ctr[ge];
-            const u64 sseed = A.sticky_seed[ge];
-            int prev = A.prev_applied[ge];
-            const int act = A.actions[ge];
-            u32 pads4 = 0;
-            for (int f = 0; f < kFramesPerDecision; ++f) {
-                Move mv = unpack_move(act);
-                if (A.sticky && rand_u32(sseed, sctr) < kSticky32)
-                    mv = restrict_move(unpack_move(prev), dr, g.start_ok != 0, g.select_ok != 0);
-                prev = pack_move(mv);
-                const u32 pad = pad_byte(mv, A.ep_frame[ge]);
-                pads4 |= pad << (8 * f);
-                m.pad = pad;
-                m.slot = static_cast<u32>(f);
-                if (A.fault[ge] == 0) {
-                    const u32 fl = m.step_until(A.target[ge]);
-                    if (fl) A.fault[ge] = fl;
-                }
-                m.finish_slot();
-                A.target[ge] += kFrameDots;
-                A.ep_frame[ge] += 1;
+__global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
+    extern __shared__ __align__(16) u8 smem_raw[];
+    EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    const u32 lane = threadIdx.x;
+    for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
+    __syncwarp();
+    const u32 total = restart ? *A.list_count : g.n;
+    for (u32 base = blockIdx.x * 32u; base < total; base += gridDim.x * 32u) {
+        const u32 k = base + lane;
+        u32 ge = 0;
+        bool valid = k < total;
+        if (valid) {
+            ge = restart ? A.list[k] : g.e0 + k;
+            valid = ge >= g.e0 && ge < g.e0 + g.n;
+        }
+        Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab);
+        if (valid) { m.stage_in(); m.load(); }
+        u32 fault = valid ? A.fault[ge] : 0u;
+        u64 target = valid ? A.target[ge] : 0ull;
+        u32 ep_frame = valid ? A.ep_frame[ge] : 0u;
+        // per lane: frames to run (decision: 4; restart: idle frames beyond the copied snapshot, then 4 neutral
+        // frames, rl/csrc/rlenv_core.cuh:311-328) - one step_until call site for the whole warp
+        int dr = -1, prev = 0, act = 0, extra = 0;
+        u64 sctr = 0, sseed = 0;
+        if (valid) {
+            if (!restart) {
+                dr = dropped_now(A.drop[ge]);
+                sctr = A.sticky_ctr[ge];
+                sseed = A.sticky_seed[ge];
+                prev = A.prev_applied[ge];
+                act = A.actions[ge];
+            } else {
+                const int idle = A.ep_idle[ge];
+                extra = idle <= static_cast<int>(g.idle_tmpl) ? 0 : idle;
             }
+        }
+        const int nfr = extra + kFramesPerDecision;
+        const int most = __reduce_max_sync(0xFFFFFFFFu, valid ? nfr : 0);
+        u32 pads4 = 0;
+        for (int i = 0; i < most; ++i) {
+            const bool mine = valid && i < nfr;
+            if (mine) {
+                u32 pad = 0;
+                if (!restart) {
+                    Move mv = unpack_move(act);
+                    if (A.sticky && rand_u32(sseed, sctr) < kSticky32)
+                        mv = restrict_move(unpack_move(prev), dr, g.start_ok != 0, g.select_ok != 0);
+                    prev = pack_move(mv);
+                    pad = pad_byte(mv, ep_frame);
+                    pads4 |= pad << (8 * i);
+                }
+                m.pad = pad;
+                m.slot = i < extra ? 0u : static_cast<u32>(i - extra);
+            }
+            const u32 fl = m.step_until(target, mine && fault == 0);
+            if (mine) {
+                if (fl) fault = fl;
+                m.finish_slot();
+                target += kFrameDots;
+                ep_frame += 1;
+            }
+        }
+        if (valid && !restart) {
             A.sticky_ctr[ge] = sctr;
             A.prev_applied[ge] = static_cast<int16_t>(prev);
             reinterpret_cast<u32*>(A.pads)[ge] = pads4;
-        } else {
-            // ph_reset_idle: frames beyond the copied snapshot, then 4 neutral frames (rl/csrc/rlenv_core.cuh:311-328)
-            const int idle = A.ep_idle[ge];
-            const int have = idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
-            for (int i = have; i < idle; ++i) {
-                m.pad = 0;
-                m.slot = 0;
-                if (A.fault[ge] == 0) { const u32 fl = m.step_until(A.target[ge]); if (fl) A.fault[ge] = fl; }
-                m.finish_slot();
-                A.target[ge] += kFrameDots;
-                A.ep_frame[ge] += 1;
-            }
-            for (int f = 0; f < kFramesPerDecision; ++f) {
-                m.pad = 0;
-                m.slot = static_cast<u32>(f);
-                if (A.fault[ge] == 0) { const u32 fl = m.step_until(A.target[ge]); if (fl) A.fault[ge] = fl; }
-                m.finish_slot();
-                A.target[ge] += kFrameDots;
-                A.ep_frame[ge] += 1;
-            }
         }
-        m.store();
-        if (restart) {
+        if (valid) {
+            m.store();
+            m.stage_out();
+            A.fault[ge] = fault;
+            A.target[ge] = target;
+            A.ep_frame[ge] = ep_frame;
+        }
+        if (restart && valid) {
             // ph_reset_finish_controls: first tracker update (no reward), counters, controls
             Tracker t = A.trk[ge];
             (void)reward_update(g.spec, observe_synth(A.st, ge), A.ep_idle[ge] + kFramesPerDecision, t);
@@ -457,6 +468,7 @@ __global__ void __launch_bounds__(128) k_frames(const __grid_constant__ GameArgs
             A.resetting[ge] = 0;
             write_controls(g, A, ge);
         }
+        __syncwarp();
     }
 }
 
@@ -531,92 +543,88 @@ __global__ void __launch_bounds__(256) k_render(const __grid_constant__ RenderAr
         const u32 k = it / R.frames, f = it % R.frames;
         const u32 ge = R.list ? R.list[k] : R.e0 + k;
         if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
-        rd.draw(ge, f, R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels, R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH);
+        u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)
+                           : R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels;
+        rd.draw(ge, f, out, R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH, R.packed != nullptr);
     }
 }
 
 // ------------------------------------------------------------------------------------------------ set-up kernels
 
-// Power-on of env slot `e` (NeSLE cold reset, restated; RAM 0xFF as rl/csrc/rlenv_build.hpp:86).
+// Power-on of env slot `e` (NeSLE cold reset, restated; RAM 0xFF as rl/csrc/rlenv_build.hpp:86), then the boot:
+// `boot_n` frames with the given pads; after the boot and after each of `idle_n` further idle frames the state is
+// written as a snapshot record. One warp, lane 0 emulates.
 template <u32 BOARD>
-__global__ void k_power_on(const __grid_constant__ GameArgs g, StateView S, u32 e) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = 0;
-    for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * S.Np + e] = 0xFFFFFFFFu;
-    for (u32 i = 0; i < kPrgRamWords; ++i) S.prg_ram[static_cast<u64>(i) * S.Np + e] = 0;
-    for (u32 i = 0; i < kOamBytes; ++i) S.oam[static_cast<u64>(e) * kOamBytes + i] = 0;
-    for (u32 i = 0; i < kNtBytes; ++i) S.nt[static_cast<u64>(e) * kNtBytes + i] = 0;
-    for (u32 i = 0; i < kPalBytes; ++i) S.pal[static_cast<u64>(e) * kPalBytes + i] = 0;
-    if (S.chr_ram) for (u32 i = 0; i < kChrRamBytes; ++i) S.chr_ram[static_cast<u64>(e) * kChrRamBytes + i] = 0;
-    for (u32 i = 0; i < kLogBanks * kLogBankWords; ++i) S.log[static_cast<u64>(e) * kLogBanks * kLogBankWords + i] = 0;
-    __shared__ u32 dt[256];
-    for (int i = 0; i < 256; ++i) dt[i] = kDecode.t[i];
-    Emu<BOARD> m(S, g.cart, e, dt);
-    auto W = [&](int w, u32 v) { S.regs[static_cast<u64>(w) * S.Np + e] = v; };
-    // board power-on (patch:3057-3085)
-    // paged boards keep a run-time page map (the others mirror by the header and have none)
-    const u32 hmap = g.cart.arrangement == 1 ? kPageHorizontal : kPageVertical;
-    W(R_PPU2, (BOARD == kMmc1 || BOARD == kMmc3) ? (hmap << 24) : 0u);
-    if constexpr (BOARD == kMmc1) { m.set_mreg(0, 0x0C); m.mmc1_sync(); }
-    if constexpr (BOARD == kMmc3) {
-        m.set_mreg(1, 2); m.set_mreg(2, 4); m.set_mreg(3, 5); m.set_mreg(4, 6); m.set_mreg(5, 7); m.set_mreg(7, 1);
-        m.set_mreg(9, g.cart.arrangement == 1 ? 1 : 0);
-        m.mmc3_sync();
+__global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g, StateView S, u32 e, const u8* boot_pads,
+                                             u32 boot_n, u32 idle_n, u8* recs, u32* fault_out) {
+    extern __shared__ __align__(16) u8 smem_raw[];
+    EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    const u32 lane = threadIdx.x;
+    for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
+    const bool me = lane == 0;
+    if (me) {
+        for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = 0;
+        for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * S.Np + e] = 0xFFFFFFFFu;
+        for (u32 i = 0; i < kPrgRamWords; ++i) S.prg_ram[static_cast<u64>(i) * S.Np + e] = 0;
+        for (u32 i = 0; i < kOamBytes; ++i) S.oam[static_cast<u64>(e) * kOamBytes + i] = 0;
+        for (u32 i = 0; i < kNtBytes; ++i) S.nt[static_cast<u64>(e) * kNtBytes + i] = 0;
+        for (u32 i = 0; i < kPalBytes; ++i) S.pal[static_cast<u64>(e) * kPalBytes + i] = 0;
+        if (S.chr_ram) for (u32 i = 0; i < kChrRamBytes; ++i) S.chr_ram[static_cast<u64>(e) * kChrRamBytes + i] = 0;
+        for (u32 i = 0; i < kLogBanks * kLogBankWords; ++i) S.log[static_cast<u64>(e) * kLogBanks * kLogBankWords + i] = 0;
+        for (u32 i = 0; i < kNtBytes; ++i) S.snap_nt[static_cast<u64>(e) * 4 * kNtBytes + i] = 0;
+        for (u32 i = 0; i < kOamBytes; ++i) S.snap_oam[static_cast<u64>(e) * 4 * kOamBytes + i] = 0;
+        S.slot_bank[static_cast<u64>(e) * 4] = 0;
     }
-    // CPU
-    m.prg_bank = 0;
-    const u32 lo = m.prg_rd(0xFFFCu), hi = m.prg_rd(0xFFFDu);
-    W(R_PC_SP_P, (lo | (hi << 8)) | (0xFDu << 16) | (0x24u << 24));
-    W(R_CYC_LO, 7);
-    // DMC power-on: byte_end = now + 1 + 7 * 428, idle
-    const u64 be = 7ull + 1ull + 7ull * 428ull;
-    W(R_DMC_END, static_cast<u32>(be)); W(R_DMC_END + 1, 0);
-    W(R_DMC_EV, 0xFFFFFFFFu); W(R_DMC_EV + 1, 0xFFFFFFFFu);
-    // both log banks 0 and 1 start from the reset state (frame_log_reset, patch:1133-1150); bank 0 shown
-    m.load();
-    m.fill_header(m.log_bank(0));
-    m.fill_header(m.log_bank(1));
-    // presentation slot 0 = the reset state
-    for (u32 i = 0; i < kNtBytes; ++i) S.snap_nt[static_cast<u64>(e) * 4 * kNtBytes + i] = 0;
-    for (u32 i = 0; i < kOamBytes; ++i) S.snap_oam[static_cast<u64>(e) * 4 * kOamBytes + i] = 0;
-    S.slot_bank[static_cast<u64>(e) * 4] = 0;
-}
-
-// Boot: run `frames` frames on env slot `e` with the given pads; after the boot and after each extra idle frame the
-// state is written as a snapshot record. Single thread.
-template <u32 BOARD>
-__global__ void k_boot(const __grid_constant__ GameArgs g, StateView S, u32 e, const u8* boot_pads, u32 boot_n,
-                       u32 idle_n, u8* recs, u32* fault_out) {
-    __shared__ u32 dt[256];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) dt[i] = kDecode.t[i];
-    __syncthreads();
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    Emu<BOARD> m(S, g.cart, e, dt);
-    m.load();
+    __syncwarp();
+    Emu<BOARD> m(S, g.cart, e, lane, sh, dtab);
+    if (me) {
+        m.stage_in();
+        // paged boards keep a run-time page map (the others mirror by the header and have none); power-on registers
+        // (patch:3057-3085)
+        const u32 hmap = g.cart.arrangement == 1 ? kPageHorizontal : kPageVertical;
+        m.ww(R_PPU2, (BOARD == kMmc1 || BOARD == kMmc3) ? (hmap << 24) : 0u);
+        if constexpr (BOARD == kMmc1) { m.set_mreg(0, 0x0C); m.mmc1_sync(); }
+        if constexpr (BOARD == kMmc3) {
+            m.set_mreg(1, 2); m.set_mreg(2, 4); m.set_mreg(3, 5); m.set_mreg(4, 6); m.set_mreg(5, 7); m.set_mreg(7, 1);
+            m.set_mreg(9, g.cart.arrangement == 1 ? 1 : 0);
+            m.mmc3_sync();
+        }
+        m.prg_bank = 0;
+        const u32 lo = m.prg_rd(0xFFFCu), hi = m.prg_rd(0xFFFDu);
+        m.ww(R_PC_SP_P, (lo | (hi << 8)) | (0xFDu << 16) | (0x24u << 24));
+        m.ww(R_CYC_LO, 7);
+        const u64 be = 7ull + 1ull + 7ull * 428ull;   // DMC power-on: one cycle to the first bit clock, rate 0
+        m.ww(R_DMC_END, static_cast<u32>(be)); m.ww(R_DMC_END + 1, 0);
+        m.ww(R_DMC_EV, 0xFFFFFFFFu); m.ww(R_DMC_EV + 1, 0xFFFFFFFFu);
+        m.load();
+        m.fill_header(m.log_bank(0));   // both banks start from the reset state (frame_log_reset, patch:1133-1150)
+        m.fill_header(m.log_bank(1));
+    }
     u64 target = kVblankDot;
     u32 fault = 0;
-    if (boot_n == 0) {
-        m.store();
-        gather_record(S, e, recs, g.cart.chr == nullptr);
-        m.load();
-    }
+    if (me && boot_n == 0) { m.store(); m.stage_out(); gather_record(S, e, recs, g.cart.chr == nullptr); }
     for (u32 k = 0; k < boot_n + idle_n; ++k) {
-        m.pad = k < boot_n ? boot_pads[k] : 0u;
-        m.slot = k & 3u;
-        const u32 f = m.step_until(target);
-        m.finish_slot();
-        target += kFrameDots;
-        if (f && !fault) fault = f;
-        if (k + 1 >= boot_n) {
-            m.store();
-            gather_record(S, e, recs + static_cast<u64>(k + 1 - boot_n) * kRecBytes, g.cart.chr == nullptr);
-            m.load();
+        if (me) { m.pad = k < boot_n ? boot_pads[k] : 0u; m.slot = k & 3u; }
+        const u32 f = m.step_until(target, me);
+        if (me) {
+            m.finish_slot();
+            target += kFrameDots;
+            if (f && !fault) fault = f;
+            if (k + 1 >= boot_n) {
+                m.store();
+                m.stage_out();
+                gather_record(S, e, recs + static_cast<u64>(k + 1 - boot_n) * kRecBytes, g.cart.chr == nullptr);
+            }
         }
     }
-    m.store();
-    fault_out[0] = fault;
-    fault_out[1] = static_cast<u32>(target);
-    fault_out[2] = static_cast<u32>(target >> 32);
+    if (me) {
+        m.store();
+        m.stage_out();
+        fault_out[0] = fault;
+        fault_out[1] = static_cast<u32>(target);
+        fault_out[2] = static_cast<u32>(target >> 32);
+    }
 }
 
 // Canonical dump of env slot e (same bytes as the CPU oracle's oracle_dump_env).

@@ -87,6 +87,59 @@ inline std::vector<u32> expand_chr(const std::vector<u8>& chr) {
     return out;
 }
 
+// Per-kernel device time on the launching stream (CUDA events around each launch), for the benchmark's roofline
+// and launch count. Off by default: no events are recorded.
+enum KernelKind : int { kKFrames = 0, kKRender, kKFinish, kKRestart, kKRestartRender, kKPack6, kKinds };
+
+struct KTimer {
+    bool on = false;
+    double ms[kKinds] = {};
+    unsigned long long launches[kKinds] = {};
+    unsigned long long total_launches = 0;
+    std::vector<cudaEvent_t> pool;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending;
+    cudaEvent_t cur_a = nullptr;
+    cudaEvent_t take() {
+        if (pool.empty()) { cudaEvent_t e; ck(cudaEventCreate(&e), "event"); return e; }
+        cudaEvent_t e = pool.back(); pool.pop_back(); return e;
+    }
+    void begin(int kind, cudaStream_t s) {
+        ++total_launches;
+        ++launches[kind];
+        if (!on) return;
+        cur_a = take();
+        ck(cudaEventRecord(cur_a, s), "event");
+    }
+    void end(int kind, cudaStream_t s) {
+        if (!on) return;
+        cudaEvent_t b = take();
+        ck(cudaEventRecord(b, s), "event");
+        pending.push_back({kind, {cur_a, b}});
+    }
+    void collect() {
+        for (auto& p : pending) {
+            float t = 0;
+            ck(cudaEventSynchronize(p.second.second), "event sync");
+            ck(cudaEventElapsedTime(&t, p.second.first, p.second.second), "elapsed");
+            ms[p.first] += t;
+            pool.push_back(p.second.first);
+            pool.push_back(p.second.second);
+        }
+        pending.clear();
+    }
+    void reset() { collect(); for (int k = 0; k < kKinds; ++k) { ms[k] = 0; launches[k] = 0; } total_launches = 0; }
+    ~KTimer() { for (auto e : pool) cudaEventDestroy(e); for (auto& p : pending) { cudaEventDestroy(p.second.first); cudaEventDestroy(p.second.second); } }
+};
+
+// A sub-range of one game's envs and / or other picture outputs (rlenv_step_game / rlenv_step_range).
+struct Range {
+    int start = 0, count = -1;
+    u8* obs = nullptr;
+    u8* emph = nullptr;
+};
+
+inline std::size_t render_smem(bool chrx_smem) { return 1024 + (chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp); }
+
 struct Game {
     int game_id = 0;
     GameArgs g{};
@@ -100,9 +153,10 @@ struct Env {
     u32 Np = 0;
     std::vector<Game> games;
     EnvArgs A{};
+    KTimer* timer = nullptr;
     bool chr_ram_any = false;
     cudaEvent_t ev = nullptr;
-    ~Env() { if (ev) cudaEventDestroy(ev); }
+    ~Env() { if (ev) cudaEventDestroy(ev); delete timer; }
 };
 
 inline void check_launch(const char* what) {
@@ -111,9 +165,12 @@ inline void check_launch(const char* what) {
 }
 
 template <u32 B>
-void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s) {
-    const GameArgs& g = gm.g;
-    const EnvArgs& A = env.A;
+void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
+    GameArgs g = gm.g;
+    const EnvArgs& A0 = env.A;
+    EnvArgs A = A0;
+    if (rg.obs) { A.obs = rg.obs; A.emph = rg.emph; }
+    if (rg.count >= 0) { g.e0 = gm.g.e0 + static_cast<u32>(rg.start); g.n = static_cast<u32>(rg.count); }
     const u32 n = g.n;
     if (n == 0) return;
     const u32 tb = 128;
@@ -122,32 +179,44 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s) {
     R.st = A.st;
     R.obs = A.obs;
     R.emph = A.emph;
+    R.packed = A.packed;
     R.e0 = g.e0;
     R.count = n;
     R.frames = kFramesPerDecision;
     R.chrx_smem = gm.chrx_smem ? 1u : 0u;
-    const std::size_t smem = 1024 + (gm.chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp);
+    const std::size_t smem = render_smem(gm.chrx_smem);
+    KTimer& T = *env.timer;
     if (!start) {
-        k_frames<B><<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, 0);
+        T.begin(kKFrames, s);
+        k_frames<B><<<(n + 31) / 32, 32, kFramesSmem, s>>>(g, A, 0);
+        T.end(kKFrames, s);
         check_launch("k_frames");
         if (!A.no_render) {
             R.list = nullptr;
             const u32 items = n * kFramesPerDecision;
             const u32 blocks = std::min<u32>((items + 7) / 8, 148u * 16u);
+            T.begin(kKRender, s);
             k_render<B><<<blocks, 256, smem, s>>>(R);
+            T.end(kKRender, s);
             check_launch("k_render");
         }
     }
+    T.begin(kKFinish, s);
     k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
+    T.end(kKFinish, s);
     check_launch("k_finish");
-    const u32 rb = start ? (n + tb - 1) / tb : std::min<u32>((n + tb - 1) / tb, 148u);
-    k_frames<B><<<rb, tb, 0, s>>>(g, A, 1);
+    const u32 rb = start ? (n + 31) / 32 : std::min<u32>((n + 31) / 32, 148u);
+    T.begin(kKRestart, s);
+    k_frames<B><<<rb, 32, kFramesSmem, s>>>(g, A, 1);
+    T.end(kKRestart, s);
     check_launch("k_frames restart");
     if (!A.no_render) {
         R.list = A.list;
         R.list_count = A.list_count;
         const u32 blocks = start ? std::min<u32>((n * kFramesPerDecision + 7) / 8, 148u * 16u) : 148u;
+        T.begin(kKRestartRender, s);
         k_render<B><<<blocks, 256, smem, s>>>(R);
+        T.end(kKRestartRender, s);
         check_launch("k_render restart");
     }
 }
@@ -159,9 +228,9 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
     u32* fault = env.mem.allocn<u32>(4);
     const u32 idle = idle_max > 0 ? static_cast<u32>(idle_max) : 0u;
     u8* recs = env.mem.allocn<u8>(static_cast<std::size_t>(idle + 1) * kRecBytes);
-    k_power_on<B><<<1, 32>>>(gm.g, env.A.st, slot);
-    check_launch("k_power_on");
-    k_boot<B><<<1, 32>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
+    ck(cudaFuncSetAttribute(k_frames<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
+    ck(cudaFuncSetAttribute(k_boot<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
+    k_boot<B><<<1, 32, kFramesSmem>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
     check_launch("k_boot");
     u32 hf[4] = {0, 0, 0, 0};
     ck(cudaMemcpy(hf, fault, 16, cudaMemcpyDeviceToHost), "boot");
@@ -177,7 +246,7 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
 
 
 #define GR_BOARD_TEMPLATES(EXT, B)                                                                   \
-    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t);                    \
+    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t, const Range&);      \
     EXT template void boot_game<B>(Env&, Game&, const u8*, std::size_t, int, u32);
 GR_BOARD_TEMPLATES(extern, kNrom)
 GR_BOARD_TEMPLATES(extern, kUxrom)

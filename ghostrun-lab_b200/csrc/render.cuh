@@ -28,6 +28,8 @@ struct RSprites {   // per warp, shared memory: a sprite line (FetchSpriteData /
 
 struct RWarp {      // per-warp shared scratch
     RSprites spr[2];     // fetched / drawn (double buffer)
+    u32 pal[8];          // palette RAM of the replay (4 bytes per word)
+    u32 chr[8];          // 1 KB CHR page per slot (paged boards)
     alignas(16) u8 px[256];   // exact-path line buffer
     u8 emph[224];
 };
@@ -36,6 +38,7 @@ struct RenderArgs {
     CartView cart;
     StateView st;
     u8* obs;             // [N, 4, 224, 240]
+    u8* packed;          // [N, 4, 224, 180] 6-bit packed pictures, or nullptr
     u8* emph;            // [N, 4, 224]
     const u32* list;     // env list (restart pass), nullptr = all envs [e0, e0 + count)
     const u32* list_count;
@@ -70,8 +73,6 @@ __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0
 
 struct RState {
     u32 v, t, x, ctrl, mask, mirroring;
-    u32 chr[8];
-    u32 pal[8];          // palette RAM, 4 bytes per word
     u32 sh0, sh1, at;    // tile shift registers (low 16 bits) and attribute latch
     u32 blurp, spork, hit, sphitx, sphitdata, hit_x;
     u32 fb;              // which of the two sprite buffers is `fetched`
@@ -101,7 +102,7 @@ struct Renderer {
         : A(a), lane(ln), chrx(cx), spread(sp), W(w) {}
 
     __device__ __forceinline__ int ev_time(u32 i) const { return fceumm_time(ev[2 * i] & 0x1FFFFu, kook); }
-    __device__ __forceinline__ u32 pal_byte(u32 i) const { return (s.pal[i >> 2] >> ((i & 3) * 8)) & 0xFFu; }
+    __device__ __forceinline__ u32 pal_byte(u32 i) const { return reinterpret_cast<const u8*>(W.pal)[i]; }
 
     __device__ __forceinline__ u32 nt_rd(u32 addr) const {
         if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return nt[nt_off_map(s.mirroring, addr)];
@@ -110,7 +111,7 @@ struct Renderer {
     __device__ __forceinline__ u32 chr_byte(u32 addr) const {
         addr &= 0x1FFFu;
         if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
-            const u32 off = ((s.chr[addr >> 10] & A.cart.chr_page_mask) << 10) | (addr & 0x3FFu);
+            const u32 off = ((W.chr[addr >> 10] & A.cart.chr_page_mask) << 10) | (addr & 0x3FFu);
             return chr_ram ? chr_ram[off & 0x1FFFu] : __ldg(A.cart.chr + off);
         } else {
             return chr_ram ? chr_ram[addr] : __ldg(A.cart.chr + (addr % A.cart.chr_size));
@@ -158,12 +159,17 @@ struct Renderer {
                 else s.v = (s.v + inc) & 0x7FFFu;
                 break;
             case kEvPalette: {
-                const u32 k = aux & 31u;
-                s.pal[k >> 2] = (s.pal[k >> 2] & ~(0xFFu << ((k & 3) * 8))) | (value << ((k & 3) * 8));
+                __syncwarp();
+                if (lane == 0) reinterpret_cast<u8*>(W.pal)[aux & 31u] = static_cast<u8>(value);
+                __syncwarp();
                 s.v = (s.v + inc) & 0x7FFFu;
                 break;
             }
-            case kEvChr: s.chr[aux & 7u] = value; break;
+            case kEvChr:
+                __syncwarp();
+                if (lane == 0) W.chr[aux & 7u] = value;
+                __syncwarp();
+                break;
             case kEvMirror: s.mirroring = value; break;
             default: break;
         }
@@ -313,7 +319,7 @@ struct Renderer {
             const RSprites& f = W.spr[s.fb];
             if (f.n != 0) {
                 s.fb ^= 1u;    // drawn = fetched (the other buffer becomes the next fetch target)
-                for (int q = 0; q < 4; ++q) s.spal[q] = s.pal[4 + q] & 0x3F3F3F3Fu;
+                for (int q = 0; q < 4; ++q) s.spal[q] = W.pal[4 + q] & 0x3F3F3F3Fu;
                 const u32 raw0 = f.raw[0];
                 const u32 j = (raw0 & 0xFFu) | ((raw0 >> 8) & 0xFFu);
                 if (s.blurp && !s.hit && j) {
@@ -325,7 +331,7 @@ struct Renderer {
         }
     }
 
-    __device__ void draw(u32 ge, u32 f, u8* obs_out, u8* emph_out) {
+    __device__ void draw(u32 ge, u32 f, u8* obs_out, u8* emph_out, bool pack6) {
         env = ge;
         const u64 sl = static_cast<u64>(ge) * 4 + f;
         const u32 bank = A.st.slot_bank[sl];
@@ -339,9 +345,13 @@ struct Renderer {
         // header (patch:1318-1343)
         s.ctrl = h[1] & 0xFFu; s.mask = (h[1] >> 8) & 0xFFu; s.x = (h[1] >> 16) & 7u;
         s.v = h[2] & 0x7FFFu; s.t = (h[2] >> 16) & 0x7FFFu;
-        for (int i = 0; i < 8; ++i) s.chr[i] = (h[3 + (i >> 2)] >> ((i & 3) * 8)) & 0xFFu;
+        __syncwarp();
+        if (lane < 8) {
+            W.chr[lane] = (h[3 + (lane >> 2)] >> ((lane & 3) * 8)) & 0xFFu;
+            W.pal[lane] = h[7 + lane];
+        }
+        __syncwarp();
         s.mirroring = h[5] & 0xFFu;
-        for (int i = 0; i < 8; ++i) s.pal[i] = h[7 + i];
         s.sh0 = s.sh1 = s.at = 0;
         s.blurp = 0; s.spork = 0; s.hit = 0; s.sphitx = 0x100u; s.sphitdata = 0; s.hit_x = 0;
         s.fb = 0;
@@ -379,8 +389,8 @@ struct Renderer {
                     if (lane == 31) cn = c32;
                     const u32 sel = __funnelshift_r(ca, cn, 4 * s.x);
                     // backdrop for colour 0 of every sub-palette
-                    const u32 P0 = (s.pal[0] & 0x3F3F3F00u) | bd, P1 = (s.pal[1] & 0x3F3F3F00u) | bd;
-                    const u32 P2 = (s.pal[2] & 0x3F3F3F00u) | bd, P3 = (s.pal[3] & 0x3F3F3F00u) | bd;
+                    const u32 P0 = (W.pal[0] & 0x3F3F3F00u) | bd, P1 = (W.pal[1] & 0x3F3F3F00u) | bd;
+                    const u32 P2 = (W.pal[2] & 0x3F3F3F00u) | bd, P3 = (W.pal[3] & 0x3F3F3F00u) | bd;
                     if (s.mask & 0x08u) {
                         w0 = pal_lookup4(sel, P0, P1, P2, P3);
                         w1 = pal_lookup4(sel >> 16, P0, P1, P2, P3);
@@ -443,8 +453,21 @@ struct Renderer {
             w1 &= keep;
             if (l >= kObsY0) {
                 const int y = l - kObsY0;
-                if (lane >= 1 && lane <= 30)
-                    reinterpret_cast<uint2*>(obs_out + static_cast<u64>(y) * kObsW)[lane - 1] = make_uint2(w0, w1);
+                if (!pack6) {
+                    if (lane >= 1 && lane <= 30)
+                        reinterpret_cast<uint2*>(obs_out + static_cast<u64>(y) * kObsW)[lane - 1] = make_uint2(w0, w1);
+                } else {
+                    // 16 pixels of lanes L, L+1 (L odd) -> 12 bytes: four 24-bit groups of 4 colour numbers
+                    const u32 n0 = __shfl_down_sync(0xFFFFFFFFu, w0, 1), n1 = __shfl_down_sync(0xFFFFFFFFu, w1, 1);
+                    if ((lane & 1u) && lane <= 29) {
+                        auto g6 = [](u32 w) { return (w & 0x3Fu) | (((w >> 8) & 0x3Fu) << 6) | (((w >> 16) & 0x3Fu) << 12) | (((w >> 24) & 0x3Fu) << 18); };
+                        const u32 v0 = g6(w0), v1 = g6(w1), v2 = g6(n0), v3 = g6(n1);
+                        u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3)) + 3 * ((lane - 1) >> 1);
+                        row[0] = v0 | (v1 << 24);
+                        row[1] = (v1 >> 8) | (v2 << 16);
+                        row[2] = (v2 >> 16) | (v3 << 8);
+                    }
+                }
                 if (lane == 0) W.emph[y] = static_cast<u8>((s.mask >> 5) & 7u);
             }
             end_of_line(l);

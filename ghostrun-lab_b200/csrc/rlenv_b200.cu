@@ -29,16 +29,60 @@ std::map<int, Spec> g_specs;   // rl10 game id -> reward parameters (rl10_regist
 
 int fail(const std::exception& ex) { g_error = ex.what(); return 1; }
 
-void launch_all(Env& env, bool start, cudaStream_t s) {
-    ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
-    for (const Game& gm : env.games) {
-        switch (gm.g.cart.board) {
-            case kNrom: launch_game<kNrom>(env, gm, start, s); break;
-            case kUxrom: launch_game<kUxrom>(env, gm, start, s); break;
-            case kMmc1: launch_game<kMmc1>(env, gm, start, s); break;
-            default: launch_game<kMmc3>(env, gm, start, s); break;
-        }
+void launch_one(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
+    switch (gm.g.cart.board) {
+        case kNrom: launch_game<kNrom>(env, gm, start, s, rg); break;
+        case kUxrom: launch_game<kUxrom>(env, gm, start, s, rg); break;
+        case kMmc1: launch_game<kMmc1>(env, gm, start, s, rg); break;
+        default: launch_game<kMmc3>(env, gm, start, s, rg); break;
     }
+}
+
+void launch_all(Env& env, bool start, cudaStream_t s) {
+    if (!env.A.actions || !env.A.masks) throw std::runtime_error("rlenv_bind was not called");
+    ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
+    for (const Game& gm : env.games) launch_one(env, gm, start, s, Range{});
+}
+
+// 4 colour numbers (6 bits) -> 3 bytes, little-endian 24-bit groups (rl/csrc/rlenv.cu:126-134 layout); 16 pixels per
+// thread: one 16-byte load, three 4-byte stores.
+__global__ void __launch_bounds__(256) k_pack6(const uint4* __restrict__ src, u32* __restrict__ dst, std::size_t n16) {
+    for (std::size_t i = blockIdx.x * static_cast<std::size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
+        const uint4 q = src[i];
+        auto v = [](u32 w) { return (w & 0x3Fu) | (((w >> 8) & 0x3Fu) << 6) | (((w >> 16) & 0x3Fu) << 12) | (((w >> 24) & 0x3Fu) << 18); };
+        const u32 v0 = v(q.x), v1 = v(q.y), v2 = v(q.z), v3 = v(q.w);
+        dst[3 * i] = v0 | (v1 << 24);
+        dst[3 * i + 1] = (v1 >> 8) | (v2 << 16);
+        dst[3 * i + 2] = (v2 >> 16) | (v3 << 8);
+    }
+}
+__global__ void k_pack6_tail(const u8* src, u8* dst, std::size_t g0, std::size_t groups) {
+    const std::size_t i = g0 + blockIdx.x * static_cast<std::size_t>(blockDim.x) + threadIdx.x;
+    if (i >= groups) return;
+    const u32 v = (src[4 * i] & 0x3Fu) | ((src[4 * i + 1] & 0x3Fu) << 6) | ((src[4 * i + 2] & 0x3Fu) << 12) | ((src[4 * i + 3] & 0x3Fu) << 18);
+    dst[3 * i] = v & 0xFF; dst[3 * i + 1] = (v >> 8) & 0xFF; dst[3 * i + 2] = (v >> 16) & 0xFF;
+}
+__global__ void __launch_bounds__(256) k_unpack6(const u32* __restrict__ src, uint4* __restrict__ dst, std::size_t n16) {
+    for (std::size_t i = blockIdx.x * static_cast<std::size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
+        const u32 a = src[3 * i], b = src[3 * i + 1], c = src[3 * i + 2];
+        const u32 v0 = a & 0xFFFFFFu, v1 = (a >> 24) | ((b & 0xFFFFu) << 8), v2 = (b >> 16) | ((c & 0xFFu) << 16), v3 = c >> 8;
+        auto w = [](u32 g) { return (g & 63u) | (((g >> 6) & 63u) << 8) | (((g >> 12) & 63u) << 16) | (((g >> 18) & 63u) << 24); };
+        dst[i] = make_uint4(w(v0), w(v1), w(v2), w(v3));
+    }
+}
+__global__ void k_unpack6_tail(const u8* src, u8* dst, std::size_t g0, std::size_t groups) {
+    const std::size_t i = g0 + blockIdx.x * static_cast<std::size_t>(blockDim.x) + threadIdx.x;
+    if (i >= groups) return;
+    const u32 v = src[3 * i] | (static_cast<u32>(src[3 * i + 1]) << 8) | (static_cast<u32>(src[3 * i + 2]) << 16);
+    dst[4 * i] = v & 63; dst[4 * i + 1] = (v >> 6) & 63; dst[4 * i + 2] = (v >> 12) & 63; dst[4 * i + 3] = (v >> 18) & 63;
+}
+__global__ void k_gather_rows(uint4* __restrict__ dst, const uint4* __restrict__ src, const std::int64_t* rows, std::size_t row_vecs) {
+    const std::size_t j = blockIdx.x;
+    const uint4* sr = src + static_cast<std::size_t>(rows[j]) * row_vecs;
+    uint4* d = dst + j * row_vecs;
+    for (std::size_t i = blockIdx.y * static_cast<std::size_t>(blockDim.x) + threadIdx.x; i < row_vecs; i += static_cast<std::size_t>(gridDim.y) * blockDim.x) d[i] = sr[i];
 }
 
 }  // namespace
@@ -178,6 +222,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             if (smem > 48 * 1024) throw std::logic_error("render shared memory exceeds the default limit");
         }
         ck(cudaEventCreateWithFlags(&env->ev, cudaEventDisableTiming), "event");
+        env->timer = new KTimer();
         ck(cudaDeviceSynchronize(), "create");
         return env;
     } catch (const std::exception& ex) {
@@ -200,6 +245,9 @@ void rlenv_bind(void* h, const std::int16_t* actions, std::uint8_t* obs, std::ui
     A.timeline = timeline; A.pads = pads; A.events = events; A.info = info;
 }
 void rlenv_bind_parts(void* h, float* parts) { static_cast<Env*>(h)->A.parts = parts; }
+// Pictures as packed 6-bit colour numbers [N, 4, 224, 180] (the rl_pack6 layout of obs) written by the renderer
+// itself instead of the [N, 4, 224, 240] bytes; nullptr restores the byte output.
+void rlenv_bind_obs_pack6(void* h, std::uint8_t* packed) { static_cast<Env*>(h)->A.packed = packed; }
 void rlenv_bind_obs(void* h, std::uint8_t* obs, std::uint8_t* emph) {
     EnvArgs& A = static_cast<Env*>(h)->A;
     A.obs = obs;
@@ -249,6 +297,126 @@ int rlenv_load(void* h, const std::uint8_t* in, void* stream) {
 
 const char* rlenv_error() { return g_error.c_str(); }
 void rlenv_destroy(void* h) { delete static_cast<Env*>(h); }
+
+int rlenv_step_game(void* h, int gi, std::uint8_t* obs, std::uint8_t* emph, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("step_game: bad game index");
+        auto s = static_cast<cudaStream_t>(stream);
+        ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
+        Range rg;
+        rg.obs = obs; rg.emph = emph;
+        launch_one(env, env.games[gi], false, s, rg);
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rlenv_step_range(void* h, int gi, int start, int count, std::uint8_t* obs, std::uint8_t* emph, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("step_range: bad game index");
+        const Game& gm = env.games[gi];
+        if (start < 0 || count <= 0 || start + count > static_cast<int>(gm.g.n)) throw std::runtime_error("step_range: bad range");
+        auto s = static_cast<cudaStream_t>(stream);
+        ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
+        Range rg;
+        rg.start = start; rg.count = count; rg.obs = obs; rg.emph = emph;
+        launch_one(env, gm, false, s, rg);
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// ---- host-memory rollout storage and the 6-bit picture format (rl/csrc/rlenv.cu:369-421)
+void* rl_host_alloc(std::size_t bytes) {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, bytes, cudaHostAllocPortable) != cudaSuccess) { g_error = "cudaHostAlloc failed"; return nullptr; }
+    return p;
+}
+void rl_host_free(void* p) { cudaFreeHost(p); }
+int rl_pack6(const void* src, void* dst, std::size_t pixels, void* stream) {
+    try {
+        if (pixels % 4) throw std::runtime_error("pack6: pixel count must be divisible by four");
+        auto s = static_cast<cudaStream_t>(stream);
+        const std::size_t groups = pixels / 4;
+        const bool vec = (reinterpret_cast<std::uintptr_t>(src) % 16 == 0) && (reinterpret_cast<std::uintptr_t>(dst) % 4 == 0);
+        const std::size_t n16 = vec ? pixels / 16 : 0;
+        if (n16) {
+            const unsigned blocks = static_cast<unsigned>(std::min<std::size_t>((n16 + 255) / 256, 148 * 32));
+            k_pack6<<<blocks, 256, 0, s>>>(static_cast<const uint4*>(src), static_cast<u32*>(dst), n16);
+        }
+        const std::size_t g0 = n16 * 4;
+        if (groups > g0)
+            k_pack6_tail<<<static_cast<unsigned>((groups - g0 + 255) / 256), 256, 0, s>>>(static_cast<const u8*>(src), static_cast<u8*>(dst), g0, groups);
+        check_launch("pack6");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rl_unpack6(const void* src, void* dst, std::size_t pixels, void* stream) {
+    try {
+        if (pixels % 4) throw std::runtime_error("unpack6: pixel count must be divisible by four");
+        auto s = static_cast<cudaStream_t>(stream);
+        const std::size_t groups = pixels / 4;
+        const bool vec = (reinterpret_cast<std::uintptr_t>(src) % 4 == 0) && (reinterpret_cast<std::uintptr_t>(dst) % 16 == 0);
+        const std::size_t n16 = vec ? pixels / 16 : 0;
+        if (n16) {
+            const unsigned blocks = static_cast<unsigned>(std::min<std::size_t>((n16 + 255) / 256, 148 * 32));
+            k_unpack6<<<blocks, 256, 0, s>>>(static_cast<const u32*>(src), static_cast<uint4*>(dst), n16);
+        }
+        const std::size_t g0 = n16 * 4;
+        if (groups > g0)
+            k_unpack6_tail<<<static_cast<unsigned>((groups - g0 + 255) / 256), 256, 0, s>>>(static_cast<const u8*>(src), static_cast<u8*>(dst), g0, groups);
+        check_launch("unpack6");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rl_memcpy_async(void* dst, const void* src, std::size_t bytes, void* stream) {
+    if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+        g_error = std::string("memcpy: ") + cudaGetErrorString(cudaGetLastError());
+        return 1;
+    }
+    return 0;
+}
+int rl_gather_rows(void* dst, const void* src, const std::int64_t* rows, int nrows, std::size_t row_bytes, void* stream) {
+    try {
+        if (row_bytes % 16) throw std::runtime_error("gather_rows: row_bytes must be a multiple of 16");
+        if (nrows <= 0) return 0;
+        dim3 grid(static_cast<unsigned>(nrows), 32);
+        k_gather_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), rows, row_bytes / 16);
+        check_launch("gather_rows");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+// Copy-engine gather: dst[t * n + j] = src[t * N + envs[j]] for t < T (one 2-D copy per env; envs in host memory).
+int rl_gather_envs(void* dst, const void* src, const std::int64_t* envs, int n, int T, int N, std::size_t row_bytes, void* stream) {
+    auto s = static_cast<cudaStream_t>(stream);
+    for (int j = 0; j < n; ++j) {
+        if (cudaMemcpy2DAsync(static_cast<char*>(dst) + j * row_bytes, static_cast<std::size_t>(n) * row_bytes,
+                              static_cast<const char*>(src) + envs[j] * row_bytes, static_cast<std::size_t>(N) * row_bytes,
+                              row_bytes, static_cast<std::size_t>(T), cudaMemcpyDefault, s) != cudaSuccess) {
+            g_error = "gather2d failed";
+            return 1;
+        }
+    }
+    return 0;
+}
+
+// ---- measurement: per-kernel device time on the launching stream (CUDA events), launch counts
+void rlenv_set_timing(void* h, int on) {
+    KTimer& T = *static_cast<Env*>(h)->timer;
+    T.collect();
+    T.on = on != 0;
+}
+// out[0..5] = ms of frames / render / finish / restart frames / restart render / pack6 kernels since the last reset,
+// out[6..11] their launch counts, out[12] all launches; reset != 0 clears the counters afterwards.
+int rlenv_timing(void* h, double* out, int reset) {
+    try {
+        KTimer& T = *static_cast<Env*>(h)->timer;
+        T.collect();
+        for (int k = 0; k < kKinds; ++k) { out[k] = T.ms[k]; out[kKinds + k] = static_cast<double>(T.launches[k]); }
+        out[2 * kKinds] = static_cast<double>(T.total_launches);
+        if (reset) T.reset();
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
 
 // Canonical machine state of global env `ge` into host memory (layout: include/rlenv_api.h).
 std::size_t rlenv_dump_bytes() { return kDumpBytes; }

@@ -76,6 +76,10 @@ def _load(path: Path):
         lib.rlenv_set_episode_level_end.argtypes = [P, I]
     if hasattr(lib, 'rlenv_set_no_render'):
         lib.rlenv_set_no_render.argtypes = [P, I]
+    if hasattr(lib, 'rlenv_bind_obs_pack6'):
+        lib.rlenv_bind_obs_pack6.argtypes = [P, P]
+        lib.rlenv_set_timing.argtypes = [P, I]
+        lib.rlenv_timing.argtypes = [P, P, I]
     if hasattr(lib, 'rlenv_dump_env'):
         lib.rlenv_dump_env.argtypes = [P, I, P, P]
         lib.rlenv_env_scalars.argtypes = [P, I, P, P]
@@ -193,6 +197,29 @@ class RlEnv:
         assert obs.is_contiguous() and emph.is_contiguous() and obs.shape == (self.n, FRAMES, OBS_H, OBS_W)
         self._obs_keep = (obs, emph)
         self.lib.rlenv_bind_obs(self.h, ctypes.c_void_p(obs.data_ptr()), ctypes.c_void_p(emph.data_ptr()))
+
+    def bind_obs_pack6(self, packed):
+        """Let the renderer write the pictures as packed 6-bit colour numbers ([N,4,224,180] uint8, the rl_pack6
+        layout of obs) into `packed` instead of filling env.obs; None restores the byte output."""
+        if packed is None:
+            self.lib.rlenv_bind_obs_pack6(self.h, None)
+            self._packed_keep = None
+            return
+        assert packed.is_contiguous() and packed.dtype == torch.uint8 and packed.numel() == self.n * FRAMES * OBS_H * OBS_W // 4 * 3
+        self._packed_keep = packed
+        self.lib.rlenv_bind_obs_pack6(self.h, ctypes.c_void_p(packed.data_ptr()))
+
+    def set_timing(self, on: bool):
+        """Record CUDA events around every kernel launch (per-kernel device time, see timing())."""
+        self.lib.rlenv_set_timing(self.h, int(bool(on)))
+
+    def timing(self, reset=False) -> dict:
+        """Per-kernel device milliseconds and launch counts since the last reset."""
+        out = np.zeros(13, np.float64)
+        self._check(self.lib.rlenv_timing(self.h, out.ctypes.data_as(ctypes.c_void_p), int(bool(reset))), 'timing')
+        names = ('frames', 'render', 'finish', 'restart_frames', 'restart_render', 'pack6')
+        return dict(ms={k: float(out[i]) for i, k in enumerate(names)},
+                    launches={k: int(out[6 + i]) for i, k in enumerate(names)}, total_launches=int(out[12]))
 
     def game_slices(self):
         out, a = [], 0
