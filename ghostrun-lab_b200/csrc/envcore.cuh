@@ -527,7 +527,7 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
 
 // Warp per (env, frame). Grid-stride over the work items of this game slice (or the restart list).
 template <u32 BOARD>
-__global__ void __launch_bounds__(256) k_render(const __grid_constant__ RenderArgs R) {
+__global__ void __launch_bounds__(256, 4) k_render(const __grid_constant__ RenderArgs R) {
     extern __shared__ __align__(16) u8 smem[];
     u32* spread = reinterpret_cast<u32*>(smem);                 // 1 KB
     u32* chrx = spread + 256;                                   // 16 KB when staged

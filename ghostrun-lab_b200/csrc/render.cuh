@@ -1,17 +1,21 @@
-// Warp-per-frame renderer for sm_100a: one warp draws one (env, frame) observation, 240x224 colour numbers plus
-// 224 emphasis bytes, by replaying the frame log through FCEUmm's line renderer (the reference's batch_frame.cuh,
-// third_party/nesle-extensions.patch:1246-1738, as called by rl/csrc/nes_machine.cuh:133-155 render_obs).
+// Warp-per-frame renderer for sm_100a: one warp draws one (env, frame) observation, 240x224 colour numbers (or
+// their 6-bit packed form) plus 224 emphasis bytes, by replaying the frame log through FCEUmm's line renderer
+// (the reference's batch_frame.cuh, third_party/nesle-extensions.patch:1246-1738, as called by
+// rl/csrc/nes_machine.cuh:133-155 render_obs).
 //
 // The replay state (PPU address, scroll, control, palette, sprite lists, sprite-0 bookkeeping) is identical in all
 // 32 lanes and advanced in lockstep; only the parallel parts are split:
-//   * tile fetch: lane L fetches tile L of the line (lanes 0-1 also tiles 32-33), the pattern row comes from a
-//     4-bit-per-pixel table ("sel" word: pixel k of the tile in bits 4k..4k+1) in shared memory or, for banked /
-//     CHR-RAM boards, from the raw CHR bytes through a bit-spread table;
-//   * pixels: lane L draws pixels 8L..8L+7 from fetches L and L+1 (a funnel shift applies fine x), palette lookup
-//     is three byte permutes per four pixels;
-//   * sprite evaluation: 64 OAM entries checked two per lane with a ballot, the first 8 kept in OAM order;
+//   * tile fetch: lane L fetches tile L of the line from the frame's nametable (staged in shared memory); the
+//     pattern row comes from a 4-bit-per-pixel table ("sel" word: pixel k of the tile in bits 4k..4k+1) in shared
+//     memory or, for banked / CHR-RAM boards, from the raw CHR bytes through a bit-spread table. Tiles 32-33 only
+//     feed pixels right of the 240-pixel crop; they are fetched when a sprite-0 check reaches there or when an exact
+//     line needs the shift registers;
+//   * pixels: lane L draws pixels 8L..8L+7 from fetches L and L+1 (a funnel shift applies fine x); the palette
+//     lookup is three byte permutes per four pixels;
+//   * sprite evaluation: each lane holds OAM entries L and L+32 in registers for the frame; a ballot finds the
+//     sprites on the next line and the first 8 in OAM order are fetched; lines without sprites skip it;
 //   * sprite composition: per lane, bit-parallel over its 8 pixels;
-//   * output: each lane stores its 8 pixels of the 240-pixel crop (lanes 1..30, 8-byte stores, one row per line).
+//   * output: lanes 1..30 hold the 240-pixel crop; 8-byte stores, or 12-byte 6-bit packed groups per lane pair.
 // Lines with frame-log writes landing inside the drawn part (mid-line splits) take the exact sequential tile loop
 // (every lane runs it in lockstep) into a 256-byte shared line buffer.
 #pragma once
@@ -22,7 +26,7 @@ namespace gr {
 struct RSprites {   // per warp, shared memory: a sprite line (FetchSpriteData / RefreshSprites)
     u32 cw[8];      // colour nibbles of the 8 pixels left to right (flip applied), 0 = transparent
     u32 meta[8];    // palette attr (bits 0-1) | behind (bit 2) | x << 8
-    u32 raw[8];     // lo | hi << 8 (unflipped pattern bytes: sprite-0 hit data)
+    u32 opq0;       // first fetched sprite: bit k = its pixel k (screen order) is opaque (sprite-0 hit data)
     u32 n;
 };
 
@@ -30,6 +34,8 @@ struct RWarp {      // per-warp shared scratch
     RSprites spr[2];     // fetched / drawn (double buffer)
     u32 pal[8];          // palette RAM of the replay (4 bytes per word)
     u32 chr[8];          // 1 KB CHR page per slot (paged boards)
+    u32 lzchr[8];        // CHR pages of the line whose shift registers are kept lazily
+    alignas(16) u8 nt[2048];  // the frame's nametable snapshot
     alignas(16) u8 px[256];   // exact-path line buffer
     u8 emph[224];
 };
@@ -55,8 +61,15 @@ __device__ __forceinline__ u32 spread8(u32 b) {   // bit (7-k) of b -> bit 4k
 }
 
 __device__ __forceinline__ u32 nib_reverse(u32 w) {   // nibble k -> nibble 7-k
-    u32 r = __byte_perm(w, 0, 0x0123);
+    const u32 r = __byte_perm(w, 0, 0x0123);
     return ((r >> 4) & 0x0F0F0F0Fu) | ((r << 4) & 0xF0F0F0F0u);
+}
+
+__device__ __forceinline__ u32 nib_opaque8(u32 w) {   // bit k = nibble k has a colour
+    u32 t = (w | (w >> 1)) & 0x11111111u;
+    t = (t | (t >> 3)) & 0x03030303u;
+    t = (t | (t >> 6)) & 0x000F000Fu;
+    return (t | (t >> 12)) & 0xFFu;
 }
 
 // 4 pixels from 4 nibbles (c | attr << 2) through a 16-entry palette held as 4 words.
@@ -71,13 +84,18 @@ __device__ __forceinline__ u32 pal_lookup4(u32 sel16, u32 p0, u32 p1, u32 p2, u3
 // nibble mask (4 nibbles, each 0 or 0xF, low 16 bits) -> byte mask
 __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0xFFFFFFFFu, nm16 & 0x4444u); }
 
+// 4 colour numbers (bytes) -> one 24-bit 6-bit group (rl/csrc/rlenv.cu:126-134 layout)
+__device__ __forceinline__ u32 pack_group6(u32 w) {
+    return (w & 0x3Fu) | ((w >> 2) & 0xFC0u) | ((w >> 4) & 0x3F000u) | ((w >> 6) & 0xFC0000u);
+}
+
 struct RState {
     u32 v, t, x, ctrl, mask, mirroring;
     u32 sh0, sh1, at;    // tile shift registers (low 16 bits) and attribute latch
-    u32 blurp, spork, hit, sphitx, sphitdata, hit_x;
+    u32 blurp, spork, hit, sphitx, sphitmask, hit_x;
     u32 fb;              // which of the two sprite buffers is `fetched`
     u32 spal[4];         // sprite palette taken at RefreshSprites (& 0x3F)
-    u32 lazy, lz32, lz33;   // shift registers still as the colour nibbles of fetches 32 / 33 of the last fast line
+    u32 lazy, lz_v, lz_ctrl, lz_mir;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
     u32 cursor;
 };
 
@@ -88,14 +106,12 @@ struct Renderer {
     const u32* __restrict__ chrx;    // shared (or global) pattern table
     const u32* __restrict__ spread;  // shared 256-entry bit spread table
     RWarp& W;
-    u32 env;
     const u32* h;
     const u32* ev;
     u32 count;
     int kook;
-    const u8* nt;
-    const u8* oam;
     const u8* chr_ram;   // per-frame CHR-RAM snapshot, nullptr on CHR-ROM carts
+    u32 spA, spB;        // OAM entries lane and lane + 32: y | tile << 8 | attr << 16 | x << 24
     RState s;
 
     __device__ Renderer(const RenderArgs& a, u32 ln, const u32* cx, const u32* sp, RWarp& w)
@@ -103,39 +119,40 @@ struct Renderer {
 
     __device__ __forceinline__ int ev_time(u32 i) const { return fceumm_time(ev[2 * i] & 0x1FFFFu, kook); }
     __device__ __forceinline__ u32 pal_byte(u32 i) const { return reinterpret_cast<const u8*>(W.pal)[i]; }
+    __device__ __forceinline__ static constexpr bool paged() { return BOARD == kMmc1 || BOARD == kMmc3; }
 
-    __device__ __forceinline__ u32 nt_rd(u32 addr) const {
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return nt[nt_off_map(s.mirroring, addr)];
-        else return nt[nt_off_header(A.cart.arrangement, addr)];
+    __device__ __forceinline__ u32 nt_rd(u32 mir, u32 addr) const {
+        if constexpr (paged()) return W.nt[nt_off_map(mir, addr)];
+        else return W.nt[nt_off_header(A.cart.arrangement, addr)];
     }
-    __device__ __forceinline__ u32 chr_byte(u32 addr) const {
+    __device__ __forceinline__ u32 chr_byte(const u32* pages, u32 addr) const {
         addr &= 0x1FFFu;
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
-            const u32 off = ((W.chr[addr >> 10] & A.cart.chr_page_mask) << 10) | (addr & 0x3FFu);
+        if constexpr (paged()) {
+            const u32 off = ((pages[addr >> 10] & A.cart.chr_page_mask) << 10) | (addr & 0x3FFu);
             return chr_ram ? chr_ram[off & 0x1FFFu] : __ldg(A.cart.chr + off);
         } else {
-            return chr_ram ? chr_ram[addr] : __ldg(A.cart.chr + (addr % A.cart.chr_size));
+            return chr_ram ? chr_ram[addr] : __ldg(A.cart.chr + addr);   // CHR ROM is >= 8 KB: no wrap needed
         }
     }
-    // colour nibbles of pattern row (vadr: low-plane address)
-    __device__ __forceinline__ u32 chr_sel(u32 vadr) const {
+    // colour nibbles of the pattern row at vadr (low-plane address)
+    __device__ __forceinline__ u32 chr_sel(const u32* pages, u32 vadr) const {
         if constexpr (BOARD == kNrom || BOARD == kUxrom) {
             if (A.chrx_smem) {
                 const u32 a = vadr & 0x1FFFu;
                 return chrx[(a & 7u) * 512u + (a >> 4)];
             }
         }
-        return spread[chr_byte(vadr)] | (spread[chr_byte(vadr + 8u)] << 1);
+        return spread[chr_byte(pages, vadr)] | (spread[chr_byte(pages, vadr + 8u)] << 1);
     }
     // One tile fetch at PPU address v: colour nibbles with the attribute in bits 2-3 of each nibble.
-    __device__ __forceinline__ u32 fetch(u32 v, u32& attr) const {
+    __device__ __forceinline__ u32 fetch(u32 v, u32 ctrl, u32 mir, const u32* pages) const {
         const u32 base = 0x2000u | (v & 0x0C00u);
-        const u32 tile = nt_rd(base | (v & 0x3FFu));
+        const u32 tile = nt_rd(mir, base | (v & 0x3FFu));
         const u32 zz = v & 0x1Fu;
-        const u32 ab = nt_rd(base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
-        attr = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
-        const u32 vadr = (tile << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
-        return chr_sel(vadr);
+        const u32 ab = nt_rd(mir, base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
+        const u32 attr = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
+        const u32 vadr = (tile << 4) + (((ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
+        return chr_sel(pages, vadr) | (attr * 0x44444444u);
     }
 
     __device__ void apply(u32 i, bool drawing) {
@@ -158,13 +175,12 @@ struct Renderer {
                 if (drawing && (s.mask & 0x18u)) s.v = v_inc_y(s.v);
                 else s.v = (s.v + inc) & 0x7FFFu;
                 break;
-            case kEvPalette: {
+            case kEvPalette:
                 __syncwarp();
                 if (lane == 0) reinterpret_cast<u8*>(W.pal)[aux & 31u] = static_cast<u8>(value);
                 __syncwarp();
                 s.v = (s.v + inc) & 0x7FFFu;
                 break;
-            }
             case kEvChr:
                 __syncwarp();
                 if (lane == 0) W.chr[aux & 7u] = value;
@@ -175,21 +191,25 @@ struct Renderer {
         }
     }
 
-    // ---- exact sequential path for a line with writes inside its drawn part (all lanes in lockstep)
+    // The shift registers after the last fast line: its fetches 32 and 33.
     __device__ void materialize_shift() {
         if (!s.lazy) return;
+        __syncwarp();
+        const u32 c32 = fetch(v_inc_x_n(s.lz_v, 32), s.lz_ctrl, s.lz_mir, W.lzchr);
+        const u32 c33 = fetch(v_inc_x_n(s.lz_v, 33), s.lz_ctrl, s.lz_mir, W.lzchr);
         u32 lo32 = 0, hi32 = 0, lo33 = 0, hi33 = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            lo32 |= ((s.lz32 >> (4 * k)) & 1u) << (7 - k); hi32 |= ((s.lz32 >> (4 * k + 1)) & 1u) << (7 - k);
-            lo33 |= ((s.lz33 >> (4 * k)) & 1u) << (7 - k); hi33 |= ((s.lz33 >> (4 * k + 1)) & 1u) << (7 - k);
+            lo32 |= ((c32 >> (4 * k)) & 1u) << (7 - k); hi32 |= ((c32 >> (4 * k + 1)) & 1u) << (7 - k);
+            lo33 |= ((c33 >> (4 * k)) & 1u) << (7 - k); hi33 |= ((c33 >> (4 * k + 1)) & 1u) << (7 - k);
         }
         s.sh0 = (lo32 << 8) | lo33;
         s.sh1 = (hi32 << 8) | hi33;
-        s.at = ((s.lz32 >> 2) & 3u) | (((s.lz33 >> 2) & 3u) << 2);
+        s.at = ((c32 >> 2) & 3u) | (((c33 >> 2) & 3u) << 2);
         s.lazy = 0;
     }
 
+    // ---- exact sequential path for a line with writes inside its drawn part (all lanes in lockstep)
     __device__ void exact_line(int l) {
         materialize_shift();
         const int start = l * 341 - 16;
@@ -219,14 +239,13 @@ struct Renderer {
                     outpos += 8;
                 }
                 const u32 v = s.v;
-                u32 attr;
                 const u32 base = 0x2000u | (v & 0x0C00u);
-                const u32 tile_i = nt_rd(base | (v & 0x3FFu));
+                const u32 tile_i = nt_rd(s.mirroring, base | (v & 0x3FFu));
                 const u32 zz = v & 0x1Fu;
-                const u32 ab = nt_rd(base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
-                attr = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
+                const u32 ab = nt_rd(s.mirroring, base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
+                const u32 attr = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
                 const u32 vadr = (tile_i << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
-                const u32 p0 = chr_byte(vadr), p1 = chr_byte(vadr + 8u);
+                const u32 p0 = chr_byte(W.chr, vadr), p1 = chr_byte(W.chr, vadr + 8u);
                 s.at = ((s.at >> 2) | (attr << 2)) & 0xFu;
                 s.sh0 = ((s.sh0 << 8) | p0) & 0xFFFFu;
                 s.sh1 = ((s.sh1 << 8) | p1) & 0xFFFFu;
@@ -245,7 +264,7 @@ struct Renderer {
         auto check = [&](int pp) {
             if (s.sphitx == 0x100u) return;
             for (int xx = static_cast<int>(s.sphitx); xx < static_cast<int>(s.sphitx) + 8 && xx < pp - 16 && xx < 255; ++xx) {
-                if ((s.sphitdata & (0x80u >> (xx - s.sphitx))) && !(W.px[xx] & 0x40u)) {
+                if (((s.sphitmask >> (xx - static_cast<int>(s.sphitx))) & 1u) && !(W.px[xx] & 0x40u)) {
                     s.hit = 1; s.hit_x = static_cast<u32>(xx); s.sphitx = 0x100u; return;
                 }
             }
@@ -272,40 +291,40 @@ struct Renderer {
     }
 
     // ---- end of line: sprite fetch for line l + 1, Fixit2, RefreshSprites (patch:1652-1711)
-    __device__ void end_of_line(int l) {
+    __device__ __forceinline__ void end_of_line(int l) {
         const int start = l * 341 - 16;
         s.sphitx = 0x100u;
         if (s.mask & 0x18u) {
             RSprites& f = W.spr[s.fb];
             const u32 c = s.ctrl;
             const u32 hgt = (c & 0x20u) ? 16u : 8u;
-            const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
-            const u32 y0 = oam[4 * lane], y1 = oam[4 * (lane + 32)];
-            const bool in0 = static_cast<u32>(l - static_cast<int>(y0)) < hgt;
-            const bool in1 = static_cast<u32>(l - static_cast<int>(y1)) < hgt;
+            const bool in0 = static_cast<u32>(l - static_cast<int>(spA & 0xFFu)) < hgt;
+            const bool in1 = static_cast<u32>(l - static_cast<int>(spB & 0xFFu)) < hgt;
             const u32 b0 = __ballot_sync(0xFFFFFFFFu, in0), b1 = __ballot_sync(0xFFFFFFFFu, in1);
-            const u32 lt = (1u << lane) - 1u;
-            const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
-            const u32 n = min(__popc(b0) + __popc(b1), 8);
             s.blurp = b0 & 1u;
+            u32 n = 0;
+            if (b0 | b1) {
+                const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
+                const u32 lt = (1u << lane) - 1u;
+                const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
+                n = min(__popc(b0) + __popc(b1), 8);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const bool in = half ? in1 : in0;
-                const u32 r = half ? r1 : r0;
-                if (in && r < 8) {
-                    const u8* sp = oam + 4 * (lane + 32 * half);
-                    const u32 yy = sp[0], tile = sp[1], attr = sp[2], xx = sp[3];
-                    const u32 t = static_cast<u32>(l - static_cast<int>(yy));
-                    u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
-                    if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (c & 0x20u) >> 1; vadr -= t & 8u; }
-                    else { vadr += t; vadr += t & 8u; }
-                    vadr &= 0x1FFFu;
-                    const u32 lo = chr_byte(vadr), hi = chr_byte(vadr + 8u);
-                    u32 cw = spread[lo] | (spread[hi] << 1);
-                    if (attr & 0x40u) cw = nib_reverse(cw);
-                    f.cw[r] = cw;
-                    f.meta[r] = (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8);
-                    f.raw[r] = lo | (hi << 8) | ((attr & 0x40u) << 10);
+                for (int half = 0; half < 2; ++half) {
+                    const bool in = half ? in1 : in0;
+                    const u32 r = half ? r1 : r0;
+                    if (in && r < 8) {
+                        const u32 sp = half ? spB : spA;
+                        const u32 tile = (sp >> 8) & 0xFFu, attr = (sp >> 16) & 0xFFu, xx = sp >> 24;
+                        const u32 t = static_cast<u32>(l - static_cast<int>(sp & 0xFFu));
+                        u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+                        if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (c & 0x20u) >> 1; vadr -= t & 8u; }
+                        else { vadr += t; vadr += t & 8u; }
+                        u32 cw = chr_sel(W.chr, vadr & 0x1FFFu);
+                        if (attr & 0x40u) cw = nib_reverse(cw);
+                        f.cw[r] = cw;
+                        f.meta[r] = (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8);
+                        if (r == 0) f.opq0 = nib_opaque8(cw);
+                    }
                 }
             }
             if (lane == 0) f.n = n;
@@ -320,11 +339,9 @@ struct Renderer {
             if (f.n != 0) {
                 s.fb ^= 1u;    // drawn = fetched (the other buffer becomes the next fetch target)
                 for (int q = 0; q < 4; ++q) s.spal[q] = W.pal[4 + q] & 0x3F3F3F3Fu;
-                const u32 raw0 = f.raw[0];
-                const u32 j = (raw0 & 0xFFu) | ((raw0 >> 8) & 0xFFu);
-                if (s.blurp && !s.hit && j) {
+                if (s.blurp && !s.hit && f.opq0) {
                     s.sphitx = f.meta[0] >> 8;
-                    s.sphitdata = (raw0 & 0x10000u) ? (__brev(j) >> 24) : j;
+                    s.sphitmask = f.opq0;
                 }
                 s.spork = 1;
             }
@@ -332,40 +349,45 @@ struct Renderer {
     }
 
     __device__ void draw(u32 ge, u32 f, u8* obs_out, u8* emph_out, bool pack6) {
-        env = ge;
         const u64 sl = static_cast<u64>(ge) * 4 + f;
         const u32 bank = A.st.slot_bank[sl];
         h = A.st.log + (static_cast<u64>(ge) * kLogBanks + bank) * kLogBankWords;
         ev = h + kLogHdr;
         count = min(h[0] & ~kLogOverflow, kLogEv);
         kook = (h[15] & kLogKook) ? 1 : 0;
-        nt = A.st.snap_nt + sl * kNtBytes;
-        oam = A.st.snap_oam + sl * kOamBytes;
         chr_ram = (A.cart.chr == nullptr && A.st.snap_chr) ? A.st.snap_chr + sl * kChrRamBytes : nullptr;
+        {   // the frame's nametable into shared memory, its OAM into registers (2 entries per lane)
+            const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
+            uint4* nts = reinterpret_cast<uint4*>(W.nt);
+            const uint4 q0 = ntg[lane], q1 = ntg[lane + 32], q2 = ntg[lane + 64], q3 = ntg[lane + 96];
+            const u32* oamw = reinterpret_cast<const u32*>(A.st.snap_oam + sl * kOamBytes);
+            spA = oamw[lane];
+            spB = oamw[lane + 32];
+            __syncwarp();
+            nts[lane] = q0; nts[lane + 32] = q1; nts[lane + 64] = q2; nts[lane + 96] = q3;
+        }
         // header (patch:1318-1343)
         s.ctrl = h[1] & 0xFFu; s.mask = (h[1] >> 8) & 0xFFu; s.x = (h[1] >> 16) & 7u;
         s.v = h[2] & 0x7FFFu; s.t = (h[2] >> 16) & 0x7FFFu;
-        __syncwarp();
         if (lane < 8) {
             W.chr[lane] = (h[3 + (lane >> 2)] >> ((lane & 3) * 8)) & 0xFFu;
             W.pal[lane] = h[7 + lane];
         }
+        if (lane == 0) { W.spr[0].n = 0; W.spr[1].n = 0; }
         __syncwarp();
         s.mirroring = h[5] & 0xFFu;
         s.sh0 = s.sh1 = s.at = 0;
-        s.blurp = 0; s.spork = 0; s.hit = 0; s.sphitx = 0x100u; s.sphitdata = 0; s.hit_x = 0;
+        s.blurp = 0; s.spork = 0; s.hit = 0; s.sphitx = 0x100u; s.sphitmask = 0; s.hit_x = 0;
         s.fb = 0;
         s.spal[0] = s.spal[1] = s.spal[2] = s.spal[3] = 0;
-        s.lazy = 0; s.lz32 = s.lz33 = 0;
+        s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mir = 0;
         s.cursor = 0;
-        if (lane == 0) { W.spr[0].n = 0; W.spr[1].n = 0; }
-        __syncwarp();
         while (s.cursor < count && ev_time(s.cursor) < -16) apply(s.cursor++, false);
         if (s.mask & 0x18u) s.v = s.t;
 
         for (int l = 0; l < kObsY0 + kObsH; ++l) {
             const int start = l * 341 - 16;
-            u32 w0, w1;   // this lane's 8 background pixels (colour | 0x40 transparent), bytes k = pixel 8L+k
+            u32 w0, w1;   // this lane's 8 background pixels (colour | 0x40 transparent), byte k = pixel 8L+k
             if (s.cursor < count && ev_time(s.cursor) < start + 272) {
                 exact_line(l);
                 const uint2 q = reinterpret_cast<const uint2*>(W.px)[lane];
@@ -377,21 +399,16 @@ struct Renderer {
                     w0 = w1 = bdw;   // rendering off: backdrop, nothing fetched, v unchanged
                 } else {
                     const u32 v0 = s.v;
-                    u32 at_a, at_b = 0;
-                    const u32 sel_a = fetch(v_inc_x_n(v0, lane), at_a);
-                    u32 sel_b = 0;
-                    if (lane < 2) sel_b = fetch(v_inc_x_n(v0, 32 + lane), at_b);
-                    const u32 ca = sel_a | (at_a * 0x44444444u);
-                    const u32 cb = sel_b | (at_b * 0x44444444u);
+                    const u32 ca = fetch(v_inc_x_n(v0, lane), s.ctrl, s.mirroring, W.chr);
                     u32 cn = __shfl_down_sync(0xFFFFFFFFu, ca, 1);
-                    const u32 c32 = __shfl_sync(0xFFFFFFFFu, cb, 0);
-                    const u32 c33 = __shfl_sync(0xFFFFFFFFu, cb, 1);
-                    if (lane == 31) cn = c32;
+                    // fetch 32 only feeds pixels 248..255 (right of the crop): needed for a sprite-0 check there
+                    const bool need32 = s.sphitx != 0x100u && s.sphitx >= 241u;
+                    if (need32 && lane == 31) cn = fetch(v_inc_x_n(v0, 32), s.ctrl, s.mirroring, W.chr);
                     const u32 sel = __funnelshift_r(ca, cn, 4 * s.x);
-                    // backdrop for colour 0 of every sub-palette
-                    const u32 P0 = (W.pal[0] & 0x3F3F3F00u) | bd, P1 = (W.pal[1] & 0x3F3F3F00u) | bd;
-                    const u32 P2 = (W.pal[2] & 0x3F3F3F00u) | bd, P3 = (W.pal[3] & 0x3F3F3F00u) | bd;
                     if (s.mask & 0x08u) {
+                        // colour 0 of every sub-palette shows the backdrop
+                        const u32 P0 = (W.pal[0] & 0x3F3F3F00u) | bd, P1 = (W.pal[1] & 0x3F3F3F00u) | bd;
+                        const u32 P2 = (W.pal[2] & 0x3F3F3F00u) | bd, P3 = (W.pal[3] & 0x3F3F3F00u) | bd;
                         w0 = pal_lookup4(sel, P0, P1, P2, P3);
                         w1 = pal_lookup4(sel >> 16, P0, P1, P2, P3);
                         if (lane == 0 && !(s.mask & 0x02u)) { w0 = bdw; w1 = bdw; }
@@ -409,12 +426,12 @@ struct Renderer {
                         const u32 olo = __shfl_sync(0xFFFFFFFFu, ob, lo_l & 31u);
                         const u32 ohi = __shfl_sync(0xFFFFFFFFu, ob, (lo_l + 1) & 31u);
                         const u32 win = ((olo | (lo_l + 1 < 32 ? (ohi << 8) : 0u)) >> (sx & 7u)) & 0xFFu;
-                        const u32 sprb = __brev(s.sphitdata) >> 24;   // bit k = sprite pixel k opaque
                         const u32 lim = sx + 8u <= 255u ? 0xFFu : ((1u << (255u - sx)) - 1u);
-                        const u32 hits = win & sprb & lim;
+                        const u32 hits = win & s.sphitmask & lim;
                         if (hits) { s.hit = 1; s.hit_x = sx + (__ffs(hits) - 1); s.sphitx = 0x100u; }
                     }
-                    s.lazy = 1; s.lz32 = c32; s.lz33 = c33;
+                    s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mir = s.mirroring;
+                    if constexpr (paged()) { if (lane < 8) W.lzchr[lane] = W.chr[lane]; }
                     s.v = v_inc_y(v_inc_x_n(v0, 34));
                 }
             }
@@ -438,8 +455,8 @@ struct Renderer {
                 }
                 if (lane == 0 && !(s.mask & 0x04u)) sany = 0;
                 if (sany) {
-                    const u32 S0 = s.spal[0], S1 = s.spal[1], S2 = s.spal[2], S3 = s.spal[3];
-                    const u32 c0 = pal_lookup4(snib, S0, S1, S2, S3), c1 = pal_lookup4(snib >> 16, S0, S1, S2, S3);
+                    const u32 c0 = pal_lookup4(snib, s.spal[0], s.spal[1], s.spal[2], s.spal[3]);
+                    const u32 c1 = pal_lookup4(snib >> 16, s.spal[0], s.spal[1], s.spal[2], s.spal[3]);
                     const u32 any0 = nib_to_bytes(sany), any1 = nib_to_bytes(sany >> 16);
                     const u32 beh0 = nib_to_bytes(sbeh), beh1 = nib_to_bytes(sbeh >> 16);
                     const u32 tr0 = ((w0 & 0x40404040u) >> 6) * 0xFFu, tr1 = ((w1 & 0x40404040u) >> 6) * 0xFFu;
@@ -458,14 +475,13 @@ struct Renderer {
                         reinterpret_cast<uint2*>(obs_out + static_cast<u64>(y) * kObsW)[lane - 1] = make_uint2(w0, w1);
                 } else {
                     // 16 pixels of lanes L, L+1 (L odd) -> 12 bytes: four 24-bit groups of 4 colour numbers
-                    const u32 n0 = __shfl_down_sync(0xFFFFFFFFu, w0, 1), n1 = __shfl_down_sync(0xFFFFFFFFu, w1, 1);
+                    const u32 g0 = pack_group6(w0), g1 = pack_group6(w1);
+                    const u32 n0 = __shfl_down_sync(0xFFFFFFFFu, g0, 1), n1 = __shfl_down_sync(0xFFFFFFFFu, g1, 1);
                     if ((lane & 1u) && lane <= 29) {
-                        auto g6 = [](u32 w) { return (w & 0x3Fu) | (((w >> 8) & 0x3Fu) << 6) | (((w >> 16) & 0x3Fu) << 12) | (((w >> 24) & 0x3Fu) << 18); };
-                        const u32 v0 = g6(w0), v1 = g6(w1), v2 = g6(n0), v3 = g6(n1);
                         u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3)) + 3 * ((lane - 1) >> 1);
-                        row[0] = v0 | (v1 << 24);
-                        row[1] = (v1 >> 8) | (v2 << 16);
-                        row[2] = (v2 >> 16) | (v3 << 8);
+                        row[0] = g0 | (g1 << 24);
+                        row[1] = (g1 >> 8) | (n0 << 16);
+                        row[2] = (n0 >> 16) | (n1 << 8);
                     }
                 }
                 if (lane == 0) W.emph[y] = static_cast<u8>((s.mask >> 5) & 7u);
