@@ -1,0 +1,91 @@
+// C-ABI of librlenv_b200.so, the batched NES environment for B200 (ghostrun-lab_b200/csrc). Every entry point the
+// reference's Python side binds (rl/rlenv.py:76-119 _load) is here with the same name, argument meaning and error
+// behaviour; each line cites the reference declaration it replaces. Plain pointers and sizes only: all buffers given
+// to rlenv_bind* are device pointers, `stream` is a cudaStream_t (the caller's torch stream). Calls return int 0 on
+// success and non-zero on failure with a message in rlenv_error() (thread-local); rlenv_create returns NULL on
+// failure; no C++ exception crosses the ABI. There is no CPU path: without a CUDA device every call fails.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// ---------------------------------------------------------------- lifecycle (rl/csrc/rlenv_api.h:9-12, 43-46)
+
+// rl/csrc/rlenv_api.h:9-11. game_ids: rl10 game ids (0..11 the reference's commercial games, 12..23 the seeded
+// synthetic games of ghostrun-lab_b200/synth.py; a game needs its reward spec registered first, rl10_register_game).
+// roms: iNES images (mappers 0 NROM, 1 MMC1, 2 UxROM, 4 MMC3); boot_pads: pad byte of every frame from power-on to
+// the boot snapshot; n_envs: envs per game. sticky / dropout: 0/1; idle_max: 0..idle_max random idle frames at
+// episode starts; device: CUDA device index.
+void* rlenv_create(int ngames, const int* game_ids, const uint8_t* const* roms, const size_t* rom_sizes,
+                   const uint8_t* const* boot_pads, const size_t* boot_sizes, const int* n_envs, uint64_t run_seed,
+                   int sticky, int idle_max, int dropout, int device);
+int rlenv_num_envs(void* h);                                              // rl/csrc/rlenv_api.h:12
+const char* rlenv_error(void);                                            // rl/csrc/rlenv_api.h:45
+void rlenv_destroy(void* h);                                              // rl/csrc/rlenv_api.h:46
+
+// ---------------------------------------------------------------- outputs (rl/csrc/rlenv_api.h:15-21)
+
+// rl/csrc/rlenv_api.h:15-17: actions i16[N]; obs u8[N,4,224,240]; emph u8[N,4,224]; reward f32[N]; done u8[N];
+// masks u8[N,19]; timeline u8[N,8,45]; pads u8[N,4]; events u32[N]; info f32[N,8]. Takes effect at the next call.
+void rlenv_bind(void* h, const int16_t* actions, uint8_t* obs, uint8_t* emph, float* reward, uint8_t* done,
+                uint8_t* masks, uint8_t* timeline, uint8_t* pads, uint32_t* events, float* info);
+void rlenv_bind_parts(void* h, float* parts);                             // rl/csrc/rlenv_api.h:19, f32[N,7]
+void rlenv_bind_obs(void* h, uint8_t* obs, uint8_t* emph);                // rl/csrc/rlenv_api.h:21
+// Extension (no reference counterpart; replaces the reference's rl_pack6 pass after the step, rl/csrc/rlenv.cu:
+// 380-386, when set): the renderer writes the pictures directly as packed 6-bit colour numbers u8[N,4,224,180] in
+// the rl_pack6 layout; NULL restores the byte output.
+void rlenv_bind_obs_pack6(void* h, uint8_t* packed);
+
+// ---------------------------------------------------------------- decisions (rl/csrc/rlenv_api.h:40-41)
+
+int rlenv_start(void* h, void* stream);   // rl/csrc/rlenv_api.h:40: first episode of every env
+int rlenv_step(void* h, void* stream);    // rl/csrc/rlenv_api.h:41: one decision (4 frames) of every env
+int rlenv_num_games(void* h);                                             // rl/csrc/rlenv.cu:247
+int rlenv_step_game(void* h, int gi, uint8_t* obs, uint8_t* emph, void* stream);               // rl/csrc/rlenv.cu:248-255
+int rlenv_step_range(void* h, int gi, int start, int count, uint8_t* obs, uint8_t* emph, void* stream);  // rl/csrc/rlenv.cu:257-267
+void rlenv_set_episode_level_end(void* h, int level);                     // rl/csrc/rlenv_api.h:14
+void rlenv_set_no_render(void* h, int v);                                 // rl/csrc/rlenv.cu:364-366
+
+// ---------------------------------------------------------------- exact resume (rl/csrc/rlenv_api.h:42-44)
+
+size_t rlenv_state_bytes(void* h);                                        // rl/csrc/rlenv_api.h:42
+int rlenv_save(void* h, uint8_t* host_out, void* stream);                 // rl/csrc/rlenv_api.h:43 (synchronous)
+int rlenv_load(void* h, const uint8_t* host_in, void* stream);            // rl/csrc/rlenv_api.h:44 (synchronous)
+
+// ---------------------------------------------------------------- 6-bit pictures and host storage (rl/csrc/rlenv.cu:369-421)
+
+void* rl_host_alloc(size_t bytes);                                        // rl/csrc/rlenv.cu:371-378 (pinned, portable)
+void rl_host_free(void* p);                                               // rl/csrc/rlenv.cu:379
+int rl_pack6(const void* src, void* dst, size_t pixels, void* stream);    // rl/csrc/rlenv.cu:380-386
+int rl_unpack6(const void* src, void* dst, size_t pixels, void* stream);  // rl/csrc/rlenv.cu:387-393
+int rl_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);                   // rl/csrc/rlenv.cu:394-398
+int rl_gather_rows(void* dst, const void* src, const int64_t* rows, int nrows, size_t row_bytes, void* stream);  // rl/csrc/rlenv.cu:400-409
+int rl_gather_envs(void* dst, const void* src, const int64_t* envs, int n, int T, int N, size_t row_bytes,
+                   void* stream);                                         // rl/csrc/rlenv.cu:411-421
+
+// ---------------------------------------------------------------- extensions (no reference counterpart)
+
+// Reward parameters of one rl10 game id: 20 float64 in the order of ghostrun-lab_b200/synth.py SPEC_FIELDS
+// (the reference hard-codes its 12 games' constants in rl/csrc/reward10_consts.h; synthetic games are seeded).
+// Process-wide; call before rlenv_create.
+int rl10_register_game(int game_id, const double* spec, int n);
+
+// Canonical machine state of global env `ge` (CPU registers, RAM, PPU registers, nametables, palette, OAM, board
+// registers and page tables, DMC, the shown frame-log bank, cartridge RAM, CHR-RAM): RLENV_DUMP_BYTES bytes into
+// host memory, synchronous. The CPU oracle exports the same layout (oracle_dump_env), which the parity tests compare.
+#define RLENV_DUMP_BYTES 23040
+size_t rlenv_dump_bytes(void);
+int rlenv_dump_env(void* h, int ge, uint8_t* host_out, void* stream);
+// target, ep_frame, episode, fault, sticky counter of env ge into host memory (synchronous).
+int rlenv_env_scalars(void* h, int ge, uint64_t* host_out, void* stream);
+
+// Per-kernel device time (CUDA events on the launching stream) and launch counts, for benchmarks.
+void rlenv_set_timing(void* h, int on);
+int rlenv_timing(void* h, double* out13, int reset);
+
+#ifdef __cplusplus
+}
+#endif
