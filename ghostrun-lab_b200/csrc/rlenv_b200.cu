@@ -455,3 +455,76 @@ int rlenv_env_scalars(void* h, int ge, std::uint64_t* out, void* stream) {
 }
 
 }  // extern "C"
+
+// ---- machine dump without any device allocation
+//
+// Who cannot allocate: a watchdog or debugger that inspects envs of a running rollout after the GPU's memory is
+// spent (env state, device picture buffers and the caching allocator's pools sized to fill HBM), where the
+// cudaMallocAsync staging of rlenv_dump_env fails exactly when a dump is wanted, and hosts whose memory policy fixes
+// all device memory at start-up and forbids later allocation. rlenv_dump_envs_noalloc stages through the file-scope
+// device array below instead and calls no cudaMalloc, cudaFree or allocating library routine.
+namespace {
+
+constexpr int kNoAllocMaxEnvs = 8;                 // RLENV_DUMP_NOALLOC_MAX_ENVS
+constexpr int kNoAllocMaxDevices = 64;
+// 8 x 23,040 B = 184,320 B. Every GPU that loads this library holds it until the process exits. Records start
+// 256-byte aligned (23,040 = 90 x 256).
+static __device__ __align__(256) u8 g_dump_scratch[kNoAllocMaxEnvs * kDumpBytes];
+static_assert(kDumpBytes % 256 == 0, "dump records keep the scratch alignment");
+
+std::mutex g_scratch_mu;
+u8* g_scratch_ptr[kNoAllocMaxDevices] = {};        // device address of g_dump_scratch, per device, after set-up
+
+// Set-up, once per device, with that device current: look up the array's device address. The first call on a
+// device may load this library's device code there, which is why it must come before any stream capture.
+u8* noalloc_scratch(int device) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (device < 0 || device >= kNoAllocMaxDevices) throw std::runtime_error("rlenv_dump_envs_noalloc: bad device");
+    if (g_scratch_ptr[device]) return g_scratch_ptr[device];
+    int prev = 0;
+    ck(cudaGetDevice(&prev), "rlenv_dump_envs_noalloc: cudaGetDevice");
+    ck(cudaSetDevice(device), "rlenv_dump_envs_noalloc: cudaSetDevice");
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_dump_scratch);
+    const cudaError_t rc_back = cudaSetDevice(prev);
+    if (rc != cudaSuccess)
+        throw std::runtime_error(std::string("rlenv_dump_envs_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(rc));
+    if (rc_back != cudaSuccess) throw std::runtime_error("rlenv_dump_envs_noalloc: cudaSetDevice (restore) failed");
+    g_scratch_ptr[device] = static_cast<u8*>(p);
+    return g_scratch_ptr[device];
+}
+
+}  // namespace
+
+extern "C" {
+
+// rlenv_dump_env for envs[0..n) in one call, n <= 8, without allocating: n x 23,040 bytes into host_out, same
+// layout. k_dump zero-fills each record it writes before setting the fields, so nothing of an earlier call's
+// contents (the array keeps them) reaches the output. Every call and every handle on a device shares the one array:
+// calls whose work overlaps on the GPU (two host threads, or two streams) race. A call runs its kernels and copy on
+// `stream` and synchronises it before returning.
+int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, std::uint8_t* host_out, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (n < 1 || n > kNoAllocMaxEnvs)
+            throw std::runtime_error("rlenv_dump_envs_noalloc: " + std::to_string(n) + " envs requested; one call dumps 1.." +
+                                     std::to_string(kNoAllocMaxEnvs) + " envs (fixed scratch of " +
+                                     std::to_string(kNoAllocMaxEnvs) + " x RLENV_DUMP_BYTES)");
+        if (!envs || !host_out) throw std::runtime_error("rlenv_dump_envs_noalloc: null pointer");
+        for (int i = 0; i < n; ++i)
+            if (envs[i] < 0 || envs[i] >= env.total) throw std::runtime_error("rlenv_dump_envs_noalloc: bad env index");
+        u8* scratch = noalloc_scratch(env.device);
+        auto s = static_cast<cudaStream_t>(stream);
+        for (int i = 0; i < n; ++i) {
+            k_dump<<<1, 32, 0, s>>>(env.A.st, static_cast<u32>(envs[i]), env.chr_ram_any ? 1u : 0u,
+                                    scratch + static_cast<std::size_t>(i) * kDumpBytes);
+            check_launch("k_dump");
+        }
+        ck(cudaMemcpyAsync(host_out, scratch, static_cast<std::size_t>(n) * kDumpBytes, cudaMemcpyDeviceToHost, s),
+           "rlenv_dump_envs_noalloc: copy");
+        ck(cudaStreamSynchronize(s), "rlenv_dump_envs_noalloc");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+}  // extern "C"

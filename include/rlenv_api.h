@@ -81,6 +81,17 @@ size_t rlenv_dump_bytes(void);
 int rlenv_dump_env(void* h, int ge, uint8_t* host_out, void* stream);
 // target, ep_frame, episode, fault, sticky counter of env ge into host memory (synchronous).
 int rlenv_env_scalars(void* h, int ge, uint64_t* host_out, void* stream);
+// No counterpart in the reference. rlenv_dump_env without any device allocation, for callers that cannot allocate
+// device memory: a watchdog or debugger inspecting a rollout that has spent the GPU's memory (where the staging
+// allocation of rlenv_dump_env would fail), or a host whose policy fixes device memory at start-up. Dumps
+// envs[0..n) (host array, 1 <= n <= RLENV_DUMP_NOALLOC_MAX_ENVS; more is rejected with a message) into host_out,
+// n x RLENV_DUMP_BYTES in the rlenv_dump_env layout, synchronous on `stream`. It stages through one file-scope
+// device array of 8 x RLENV_DUMP_BYTES = 184,320 bytes, which every GPU that loads the library holds until exit.
+// The first call on a device looks the array up (cudaGetSymbolAddress, which may load the library's device code):
+// make that first call before any stream capture. All calls and handles on a device share the array; calls whose
+// work overlaps on the GPU (two threads, two streams) race.
+#define RLENV_DUMP_NOALLOC_MAX_ENVS 8
+int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, uint8_t* host_out, void* stream);
 
 // Per-kernel device time (CUDA events on the launching stream) and launch counts, for benchmarks.
 void rlenv_set_timing(void* h, int on);
