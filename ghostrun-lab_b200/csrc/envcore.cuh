@@ -237,6 +237,18 @@ struct GameArgs {   // one game slice
     u32 idle_tmpl;
     u64 tmpl_target;
     u32 start_ok, select_ok;
+    u32 game_e0;               // first env of the whole game (a range step moves e0, never this)
+    // Level starts (rl/csrc/rlenv_core.cuh GameCtx lv_*): lv_cap saved states, slots < lv_levels level entrances,
+    // the rest places. lv_deaths -1 = nothing saved; lv_claim = this decision's best arrival (deaths << 32 | env
+    // within the game), ~0 = none. lv_cap 0 = level starts off.
+    u32 lv_cap, lv_levels, lv_thresh, lv_weighted;
+    u8* lv_rec;                // [lv_cap][kRecBytes]
+    Tracker* lv_st;
+    u64* lv_target;
+    u32* lv_frame;
+    i32* lv_deaths;
+    unsigned long long* lv_claim;
+    const u32* lv_cdf;         // [lv_cap] level pick CDF (lv_weighted)
 };
 
 struct EnvArgs {
@@ -264,6 +276,10 @@ struct EnvArgs {
     u8* obs; u8* emph; float* reward; u8* done; u8* masks; u8* timeline; u8* pads; u32* events; float* info;
     float* parts;
     u8* packed;     // optional [N, 4, 224, 180] packed 6-bit pictures (replaces obs when set)
+    i32* ep_start;      // [N] slot the episode started from, -1 = power-on; nullptr = level starts off
+    i32* start_out;     // optional [N]: ep_start of the episode that just ended (where done)
+    i32* level_out;     // optional [N]: level after the decision's update, -1 = not known yet
+    float* progress_out;   // optional [N]: within-level progress / progress_unit, NaN = not valid now
     u64 run_seed;
     i32 sticky, idle_max, dropout, no_render, episode_level_end;
 };
@@ -296,24 +312,24 @@ static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, 
     S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
 }
 
-// record <- env slot
-static __device__ void gather_record(const StateView& S, u32 e, u8* rec, bool chr_ram) {
+// record <- env slot; threads tid of nt share the copy (one thread: 0 of 1)
+static __device__ void gather_record(const StateView& S, u32 e, u8* rec, bool chr_ram, u32 tid = 0, u32 nt = 1) {
     u32* rr = reinterpret_cast<u32*>(rec + kRecRegs);
-    for (int w = 0; w < 64; ++w) rr[w] = w < kRegWords ? S.regs[static_cast<u64>(w) * S.Np + e] : 0u;
+    for (u32 w = tid; w < 64; w += nt) rr[w] = w < static_cast<u32>(kRegWords) ? S.regs[static_cast<u64>(w) * S.Np + e] : 0u;
     u32* ram = reinterpret_cast<u32*>(rec + kRecRam);
-    for (u32 i = 0; i < kRamWords; ++i) ram[i] = S.ram[static_cast<u64>(i) * S.Np + e];
+    for (u32 i = tid; i < kRamWords; i += nt) ram[i] = S.ram[static_cast<u64>(i) * S.Np + e];
     u32* pr = reinterpret_cast<u32*>(rec + kRecPrgRam);
-    for (u32 i = 0; i < kPrgRamWords; ++i) pr[i] = S.prg_ram[static_cast<u64>(i) * S.Np + e];
-    auto cp = [](u8* d, const u8* s, u32 n) {
+    for (u32 i = tid; i < kPrgRamWords; i += nt) pr[i] = S.prg_ram[static_cast<u64>(i) * S.Np + e];
+    auto cp = [tid, nt](u8* d, const u8* s, u32 n) {
         uint4* dv = reinterpret_cast<uint4*>(d);
         const uint4* sv = reinterpret_cast<const uint4*>(s);
-        for (u32 i = 0; i < n / 16; ++i) dv[i] = sv[i];
+        for (u32 i = tid; i < n / 16; i += nt) dv[i] = sv[i];
     };
     cp(rec + kRecOam, S.oam + static_cast<u64>(e) * kOamBytes, kOamBytes);
     cp(rec + kRecNt, S.nt + static_cast<u64>(e) * kNtBytes, kNtBytes);
     cp(rec + kRecPal, S.pal + static_cast<u64>(e) * kPalBytes, kPalBytes);
     if (chr_ram) cp(rec + kRecChrRam, S.chr_ram + static_cast<u64>(e) * kChrRamBytes, kChrRamBytes);
-    else for (u32 i = 0; i < kChrRamBytes / 4; ++i) reinterpret_cast<u32*>(rec + kRecChrRam)[i] = 0;
+    else for (u32 i = tid; i < kChrRamBytes / 4; i += nt) reinterpret_cast<u32*>(rec + kRecChrRam)[i] = 0;
     cp(rec + kRecLog, reinterpret_cast<const u8*>(S.log + static_cast<u64>(e) * kLogBanks * kLogBankWords), kLogBanks * kLogBankWords * 4);
     const u32 fs = S.regs[static_cast<u64>(R_FSLOT) * S.Np + e];
     const u64 sl = static_cast<u64>(e) * 4 + fs;
@@ -349,7 +365,8 @@ static __device__ void write_controls(const GameArgs& g, const EnvArgs& A, u32 g
     }
 }
 
-// rl/csrc/rlenv_core.cuh:208-263 (power-on / idle-snapshot restart)
+// rl/csrc/rlenv_core.cuh:208-263: idle count, level-start coin and pick (drawn only when level starts are on),
+// then the snapshot record: a saved level start, the boot snapshot after k idle frames, or the boot snapshot.
 static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) {
     const u32 ep = ++A.episode[ge];
     const u64 seed = splitmix64(splitmix64(A.run_seed ^ 0xD20F0D20F0ull) ^ (static_cast<u64>(ge) << 40) ^ static_cast<u64>(ep));
@@ -357,15 +374,37 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
     u64 ctr = 0;
     int idle = 0;
     if (A.idle_max > 0) idle = static_cast<int>(rand_below(ss, ctr, static_cast<u32>(A.idle_max + 1)));
+    int lv = -1;
+    if (g.lv_cap > 0 && g.lv_thresh != 0 && rand_u32(ss, ctr) < g.lv_thresh) {
+        u32 saved = 0;
+        for (u32 s = 0; s < g.lv_cap; ++s) saved += g.lv_deaths[s] >= 0 ? 1u : 0u;
+        if (g.lv_weighted) {
+            const u32 u = rand_u32(ss, ctr);
+            for (u32 s = 0; s < g.lv_cap && lv < 0; ++s)
+                if (u < g.lv_cdf[s]) lv = static_cast<int>(s);
+        } else if (saved > 0) {
+            u32 pick = rand_below(ss, ctr, saved);
+            for (u32 s = 0; s < g.lv_cap && lv < 0; ++s)
+                if (g.lv_deaths[s] >= 0 && pick-- == 0) lv = static_cast<int>(s);
+        }
+    }
     A.sticky_seed[ge] = ss;
     A.sticky_ctr[ge] = ctr;
-    const int k = idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
-    scatter_record(A.st, ge, g.recs + static_cast<u64>(k) * kRecBytes, g.cart.chr == nullptr);
-    A.target[ge] = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
-    A.ep_frame[ge] = static_cast<u32>(k);
-    Tracker t;
-    memset(&t, 0, sizeof t);
-    A.trk[ge] = t;
+    const int k = lv < 0 && idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
+    if (lv >= 0) {
+        scatter_record(A.st, ge, g.lv_rec + static_cast<u64>(lv) * kRecBytes, g.cart.chr == nullptr);
+        A.target[ge] = g.lv_target[lv];
+        A.ep_frame[ge] = g.lv_frame[lv];
+        A.trk[ge] = g.lv_st[lv];
+    } else {
+        scatter_record(A.st, ge, g.recs + static_cast<u64>(k) * kRecBytes, g.cart.chr == nullptr);
+        A.target[ge] = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
+        A.ep_frame[ge] = static_cast<u32>(k);
+        Tracker t;
+        memset(&t, 0, sizeof t);
+        A.trk[ge] = t;
+    }
+    if (A.ep_start) A.ep_start[ge] = lv;
     A.fault[ge] = 0;
     Dropout d;
     dropout_reset(d, seed, A.dropout != 0);
@@ -416,7 +455,8 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
                 act = A.actions[ge];
             } else {
                 const int idle = A.ep_idle[ge];
-                extra = idle <= static_cast<int>(g.idle_tmpl) ? 0 : idle;
+                const bool lv = A.ep_start && A.ep_start[ge] >= 0;   // a level start emulates every idle frame
+                extra = !lv && idle <= static_cast<int>(g.idle_tmpl) ? 0 : idle;
             }
         }
         const int nfr = extra + kFramesPerDecision;
@@ -464,7 +504,8 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
             A.trk[ge] = t;
             A.ep_ret[ge] = 0.0f;
             A.ep_len[ge] = 0;
-            A.ep_maxlvl[ge] = 0;
+            const int sl = A.ep_start ? A.ep_start[ge] : -1;   // a place: its level is the tracker's
+            A.ep_maxlvl[ge] = sl >= static_cast<int>(g.lv_levels) ? (t.has_best_level ? t.best_level : 0) : sl > 0 ? sl : 0;
             A.resetting[ge] = 0;
             write_controls(g, A, ge);
         }
@@ -504,7 +545,16 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
         Dropout d = A.drop[ge];
         dropout_advance(d, A.dropout != 0);
         A.drop[ge] = d;
+        if (g.lv_cap > 0 && !done && (u.events & kEvLevel) && u.event_level >= 0 && u.event_level < static_cast<int>(g.lv_levels)) {
+            const u64 dd = t.deaths < 0 ? 0u : static_cast<u64>(t.deaths);
+            atomicMin(&g.lv_claim[u.event_level], static_cast<unsigned long long>((dd << 32) | (ge - g.game_e0)));
+        }
+        if (A.level_out) A.level_out[ge] = t.has_best_level ? t.best_level : -1;
+        if (A.progress_out)
+            A.progress_out[ge] = t.has_prev && t.prev_progress_valid
+                ? __double2float_rn(__ddiv_rn(t.prev_progress, g.spec.progress_unit)) : __int_as_float(0x7FC00000);
         if (done) {
+            if (A.start_out) A.start_out[ge] = A.ep_start ? A.ep_start[ge] : -1;
             float* inf = A.info + static_cast<u64>(ge) * kInfo;
             inf[0] = ret;
             inf[1] = static_cast<float>(len);
@@ -522,6 +572,47 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
         A.list[slot] = ge;
     } else {
         write_controls(g, A, ge);
+    }
+}
+
+// Level-start saves after a decision's k_finish (rl/csrc/rlenv.cu:89-97, rl/csrc/rlenv_core.cuh:344-387): block s
+// takes slot s's claimed arrival when nothing is saved yet or it died no more often; the block copies the env's
+// state record, then thread 0 commits the tracker, frame target and deaths and clears the claim.
+static __global__ void __launch_bounds__(128) k_archive(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A) {
+    const u32 s = blockIdx.x;
+    const unsigned long long cl = g.lv_claim[s];
+    if (cl == ~0ull) return;   // same for the whole block
+    const bool take = g.lv_deaths[s] < 0 || static_cast<i32>(cl >> 32) <= g.lv_deaths[s];
+    const u32 ge = g.game_e0 + static_cast<u32>(cl & 0xFFFFFFFFull);
+    if (take) gather_record(A.st, ge, g.lv_rec + static_cast<u64>(s) * kRecBytes, g.cart.chr == nullptr, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (take) {
+            g.lv_st[s] = A.trk[ge];
+            g.lv_target[s] = A.target[ge];
+            g.lv_frame[s] = A.ep_frame[ge];
+            g.lv_deaths[s] = static_cast<i32>(cl >> 32);
+        }
+        g.lv_claim[s] = ~0ull;
+    }
+}
+
+// Place saves (rl/places.py; rl/csrc/rlenv.cu:99-107): block j copies env env_idx[j] of the game (index within the
+// game) into slot slot_idx[j], skipped unless lv_levels <= slot < lv_cap; the no-progress clock restarts.
+static __global__ void __launch_bounds__(128) k_place_save(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A,
+                                                           const i32* env_idx, const i32* slot_idx) {
+    const i32 s = slot_idx[blockIdx.x], e = env_idx[blockIdx.x];
+    if (s < static_cast<i32>(g.lv_levels) || s >= static_cast<i32>(g.lv_cap) || e < 0 || e >= static_cast<i32>(g.n)) return;
+    const u32 ge = g.game_e0 + static_cast<u32>(e);
+    gather_record(A.st, ge, g.lv_rec + static_cast<u64>(s) * kRecBytes, g.cart.chr == nullptr, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Tracker t = A.trk[ge];
+        t.idle_frames = 0;
+        g.lv_st[s] = t;
+        g.lv_target[s] = A.target[ge];
+        g.lv_frame[s] = A.ep_frame[ge];
+        g.lv_deaths[s] = 0;
     }
 }
 

@@ -150,6 +150,7 @@ struct Env {
     DevMem mem;
     int device = 0;
     int total = 0;
+    int lv_cap = 0, lv_levels = 0;   // level starts (rlenv_enable_places); 0 = off
     u32 Np = 0;
     std::vector<Game> games;
     EnvArgs A{};
@@ -205,6 +206,12 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
     T.end(kKFinish, s);
     check_launch("k_finish");
+    if (!start && g.lv_cap > 0) {   // level-start saves: after every env's finish, before the restarts
+        T.begin(kKFinish, s);
+        k_archive<<<g.lv_levels, 128, 0, s>>>(g, A);
+        T.end(kKFinish, s);
+        check_launch("k_archive");
+    }
     const u32 rb = start ? (n + 31) / 32 : std::min<u32>((n + 31) / 32, 148u);
     T.begin(kKRestart, s);
     k_frames<B><<<rb, 32, kFramesSmem, s>>>(g, A, 1);

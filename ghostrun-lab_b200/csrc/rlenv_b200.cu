@@ -204,6 +204,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             C.prg_page_mask = hc.prg_page_mask;
             C.chr_page_mask = hc.chr_page_mask;
             gm.g.e0 = static_cast<u32>(offset);
+            gm.g.game_e0 = static_cast<u32>(offset);
             gm.g.n = static_cast<u32>(n_envs[i]);
             gm.g.start_ok = gm.g.spec.start_ok != 0.0;
             gm.g.select_ok = gm.g.spec.select_ok != 0.0;
@@ -297,6 +298,129 @@ int rlenv_load(void* h, const std::uint8_t* in, void* stream) {
 
 const char* rlenv_error() { return g_error.c_str(); }
 void rlenv_destroy(void* h) { delete static_cast<Env*>(h); }
+
+// ---- level starts and places (rl/csrc/rlenv.cu:331-362, rl/csrc/rlenv_build.hpp:212-252)
+// Room for `cap` saved states per game, empty; slots < `levels` are level entrances saved by the archive after each
+// decision, the rest places saved by rlenv_place_save. Call once, before start / load. The new state (episode start
+// slots, then per game: records, trackers, frame targets, frames, deaths) is saved after everything else, so a state
+// saved without level starts is a prefix of one saved with them.
+int rlenv_enable_places(void* h, int cap, int levels) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (env.lv_cap != 0 || cap <= 0 || levels <= 0 || levels > cap)
+            throw std::logic_error("level starts: enable once, 0 < levels <= cap");
+        DevMem& M = env.mem;
+        const std::size_t N = static_cast<std::size_t>(env.total) + 1;
+        env.A.ep_start = M.allocn<i32>(N, true);
+        {
+            std::vector<i32> none(N, -1);
+            ck(cudaMemcpy(env.A.ep_start, none.data(), N * 4, cudaMemcpyHostToDevice), "level starts");
+        }
+        const std::size_t C = static_cast<std::size_t>(cap);
+        for (Game& gm : env.games) {
+            GameArgs& g = gm.g;
+            g.lv_cap = static_cast<u32>(cap);
+            g.lv_levels = static_cast<u32>(levels);
+            g.lv_rec = M.allocn<u8>(C * kRecBytes, true);
+            g.lv_st = M.allocn<Tracker>(C, true);
+            g.lv_target = M.allocn<u64>(C, true);
+            g.lv_frame = M.allocn<u32>(C, true);
+            g.lv_deaths = M.allocn<i32>(C, true);
+            g.lv_claim = M.allocn<unsigned long long>(C);
+            u32* cdf = M.allocn<u32>(C);
+            g.lv_cdf = cdf;
+            std::vector<i32> none(C, -1);
+            ck(cudaMemcpy(g.lv_deaths, none.data(), C * 4, cudaMemcpyHostToDevice), "level starts");
+            std::vector<unsigned long long> free_(C, ~0ull);
+            ck(cudaMemcpy(g.lv_claim, free_.data(), C * 8, cudaMemcpyHostToDevice), "level starts");
+        }
+        env.lv_cap = cap;
+        env.lv_levels = levels;
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+int rlenv_enable_level_starts(void* h, int cap) { return rlenv_enable_places(h, cap, cap); }
+
+// Level-start share p and level weights (cdf: lv_cap u32 in host memory, nullptr = uniform over the saved slots)
+// of game gi, for episodes that start from the next launch on. Synchronous.
+void rlenv_set_level_plan(void* h, int gi, double p, const std::uint32_t* cdf) {
+    Env& env = *static_cast<Env*>(h);
+    if (gi < 0 || gi >= static_cast<int>(env.games.size())) return;
+    GameArgs& g = env.games[static_cast<std::size_t>(gi)].g;
+    if (g.lv_cap == 0) return;
+    g.lv_thresh = static_cast<u32>(p <= 0.0 ? 0.0 : p >= 1.0 ? 4294967295.0 : p * 4294967296.0);
+    g.lv_weighted = cdf != nullptr ? 1u : 0u;
+    if (cdf) {
+        const cudaError_t e = cudaMemcpy(const_cast<u32*>(g.lv_cdf), cdf, static_cast<std::size_t>(g.lv_cap) * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) g_error = std::string("set_level_plan: ") + cudaGetErrorString(e);
+    }
+}
+void rlenv_bind_start(void* h, std::int32_t* start_out) { static_cast<Env*>(h)->A.start_out = start_out; }
+void rlenv_bind_level(void* h, std::int32_t* level_out) { static_cast<Env*>(h)->A.level_out = level_out; }
+void rlenv_bind_progress(void* h, float* progress_out) { static_cast<Env*>(h)->A.progress_out = progress_out; }
+
+// Deaths of each saved slot of game gi (-1 = nothing saved), lv_cap entries into host memory (synchronous).
+int rlenv_level_deaths(void* h, int gi, std::int32_t* out, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("level_deaths: bad game");
+        const GameArgs& g = env.games[static_cast<std::size_t>(gi)].g;
+        if (g.lv_cap == 0) return 0;
+        auto s = static_cast<cudaStream_t>(stream);
+        ck(cudaMemcpyAsync(out, g.lv_deaths, static_cast<std::size_t>(g.lv_cap) * 4, cudaMemcpyDeviceToHost, s), "level_deaths");
+        ck(cudaStreamSynchronize(s), "level_deaths");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// env_idx[j] (index within game gi) -> place slot slot_idx[j] (device int32 arrays; slots < levels are skipped),
+// on `stream` after the step.
+int rlenv_place_save(void* h, int gi, const std::int32_t* env_idx, const std::int32_t* slot_idx, int count, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("place_save: bad game");
+        const GameArgs& g = env.games[static_cast<std::size_t>(gi)].g;
+        if (g.lv_cap == 0 || count <= 0) return 0;
+        k_place_save<<<count, 128, 0, static_cast<cudaStream_t>(stream)>>>(g, env.A, env_idx, slot_idx);
+        check_launch("k_place_save");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// Slot src[j] -> slot dst[j] of game gi, whole saved state (host int32 arrays; synchronous).
+int rlenv_place_copy(void* h, int gi, const std::int32_t* src, const std::int32_t* dst, int count, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("place_copy: bad game");
+        const GameArgs& g = env.games[static_cast<std::size_t>(gi)].g;
+        const int cap = static_cast<int>(g.lv_cap);
+        for (int i = 0; i < count; ++i)
+            if (src[i] < 0 || dst[i] < 0 || src[i] >= cap || dst[i] >= cap) throw std::runtime_error("place_copy: bad slot");
+        auto s = static_cast<cudaStream_t>(stream);
+        for (int i = 0; i < count; ++i) {
+            const std::size_t a = static_cast<std::size_t>(src[i]), b = static_cast<std::size_t>(dst[i]);
+            ck(cudaMemcpyAsync(g.lv_rec + b * kRecBytes, g.lv_rec + a * kRecBytes, kRecBytes, cudaMemcpyDeviceToDevice, s), "place_copy");
+            ck(cudaMemcpyAsync(g.lv_st + b, g.lv_st + a, sizeof(Tracker), cudaMemcpyDeviceToDevice, s), "place_copy");
+            ck(cudaMemcpyAsync(g.lv_target + b, g.lv_target + a, 8, cudaMemcpyDeviceToDevice, s), "place_copy");
+            ck(cudaMemcpyAsync(g.lv_frame + b, g.lv_frame + a, 4, cudaMemcpyDeviceToDevice, s), "place_copy");
+            ck(cudaMemcpyAsync(g.lv_deaths + b, g.lv_deaths + a, 4, cudaMemcpyDeviceToDevice, s), "place_copy");
+        }
+        ck(cudaStreamSynchronize(s), "place_copy");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// Sizes of one game's saved-slot state, as rl/csrc/rlenv.cu:356-360: stride of a slot's state record, key slots
+// (none: the synthetic reader keeps no key set), tracker bytes, cap, levels.
+void rlenv_level_layout(void* h, int gi, std::uint32_t* out) {
+    const Env& env = *static_cast<Env*>(h);
+    const GameArgs& g = env.games[static_cast<std::size_t>(gi)].g;
+    out[0] = static_cast<u32>(kRecBytes);
+    out[1] = 0;
+    out[2] = static_cast<u32>(sizeof(Tracker));
+    out[3] = g.lv_cap;
+    out[4] = g.lv_levels;
+}
 
 int rlenv_step_game(void* h, int gi, std::uint8_t* obs, std::uint8_t* emph, void* stream) {
     try {

@@ -83,6 +83,17 @@ def _load(path: Path):
     if hasattr(lib, 'rlenv_dump_env'):
         lib.rlenv_dump_env.argtypes = [P, I, P, P]
         lib.rlenv_env_scalars.argtypes = [P, I, P, P]
+    if hasattr(lib, 'rlenv_enable_places'):
+        lib.rlenv_enable_level_starts.argtypes = [P, I]
+        lib.rlenv_enable_places.argtypes = [P, I, I]
+        lib.rlenv_set_level_plan.argtypes = [P, I, ctypes.c_double, P]
+        lib.rlenv_bind_start.argtypes = [P, P]
+        lib.rlenv_bind_level.argtypes = [P, P]
+        lib.rlenv_bind_progress.argtypes = [P, P]
+        lib.rlenv_level_deaths.argtypes = [P, I, P, P]
+        lib.rlenv_place_save.argtypes = [P, I, P, P, I, P]
+        lib.rlenv_place_copy.argtypes = [P, I, P, P, I, P]
+        lib.rlenv_level_layout.argtypes = [P, I, P]
     for name, args in (('rl_pack6', [P, P, SZ, P]), ('rl_unpack6', [P, P, SZ, P]), ('rl_memcpy_async', [P, P, SZ, P]),
                        ('rl_gather_rows', [P, P, P, I, SZ, P]), ('rl_gather_envs', [P, P, P, I, I, I, SZ, P]),
                        ('rlenv_step_game', [P, I, P, P, P]), ('rlenv_step_range', [P, I, I, I, P, P, P])):
@@ -99,7 +110,12 @@ class RlEnv:
     def __init__(self, counts: dict, device='cuda', seed=0, sticky=True, idle_max=30, dropout=True, roms=None,
                  lib_path=None, level_cap=0, level_slots=None, boot=None):
         """counts: game slug -> number of envs (envs are laid out in GAMES order). roms: optional slug -> iNES bytes
-        or path (synthetic slugs default to their generated cartridge); boot: optional slug -> boot pad bytes."""
+        or path (synthetic slugs default to their generated cartridge); boot: optional slug -> boot pad bytes.
+        level_cap > 0: save level starts (levels 0..level_cap-1 of each game, the best arrival of each decision), used
+        by new episodes with the chance set by set_level_prob / set_level_plan (default 0). self.start_level: slot a
+        finished episode started from, -1 = power-on (valid where done).
+        level_slots < level_cap: only slots 0..level_slots-1 are level starts; the rest are places, saved by
+        place_save. (rl/rlenv.py:172-243.)"""
         self.device = torch.device(device)
         self.games = [g for g in GAMES if counts.get(g, 0) > 0]
         unknown = set(counts) - set(GAMES)
@@ -117,8 +133,6 @@ class RlEnv:
             if not Path(lib_path).exists():
                 raise RuntimeError(f'{lib_path} is missing: build it with ghostrun-lab_b200/build.py')
         self.lib = _load(Path(lib_path))
-        if int(level_cap) > 0:
-            raise NotImplementedError('level starts / places are not part of this build yet')
         roms, boot = roms or {}, boot or {}
         rom_bytes, boots = [], []
         for g in self.games:
@@ -165,9 +179,94 @@ class RlEnv:
                             p(self.masks), p(self.timeline), p(self.pads), p(self.events), p(self.info))
         self.parts = torch.zeros(N, NUM_PARTS, dtype=torch.float32, device=d)
         self.lib.rlenv_bind_parts(self.h, p(self.parts))
-        self.level_cap = 0
-        self.level_slots = 0
+        self.level_cap = int(level_cap)
+        self.level_slots = int(level_slots if level_slots is not None else level_cap)
         self.start_level = torch.full((N,), -1, dtype=torch.int32, device=d)
+        if self.level_cap > 0:
+            rc = (self.lib.rlenv_enable_places(self.h, self.level_cap, self.level_slots) if self.level_slots < self.level_cap
+                  else self.lib.rlenv_enable_level_starts(self.h, self.level_cap))
+            self._check(rc, 'level starts')
+            self.lib.rlenv_bind_start(self.h, p(self.start_level))
+            self.level_now = torch.full((N,), -1, dtype=torch.int32, device=d)    # level after the last decision
+            self.lib.rlenv_bind_level(self.h, p(self.level_now))
+            # within-level progress / one level's progress unit, NaN = not valid now; never an actor input
+            self.progress_now = torch.full((N,), float('nan'), dtype=torch.float32, device=d)
+            self.lib.rlenv_bind_progress(self.h, p(self.progress_now))
+
+    # ---- level starts and places (rl/rlenv.py:245-310)
+    def set_level_prob(self, prob: float):
+        """Chance that a new episode starts from a saved level start (uniform over the game's saved levels)."""
+        assert self.level_cap > 0 or prob == 0
+        for gi in range(len(self.games)):
+            self.set_level_plan(gi, prob)
+
+    def set_level_plan(self, gi, prob, weights=None):
+        """Game gi's chance of a level start and its slot weights ([level_cap], only saved slots > 0, sum 1; None =
+        uniform over the saved slots). Call between decisions."""
+        if self.level_cap == 0:
+            return
+        cdf = None
+        if weights is not None:
+            w = np.asarray(weights, np.float64)
+            cdf = np.minimum(np.cumsum(w) * 2.0 ** 32, 2.0 ** 32 - 1).astype(np.uint32)
+            cdf[np.flatnonzero(w)[-1]:] = 2 ** 32 - 1
+        if self.device.type == 'cuda':
+            torch.cuda.synchronize(self.device)
+        self.lib.rlenv_set_level_plan(self.h, gi, float(prob), None if cdf is None else cdf.ctypes.data_as(ctypes.c_void_p))
+
+    def saved_levels(self):
+        """game slug -> {level: deaths of the saved arrival} (synchronous)."""
+        out = {}
+        for gi, g in enumerate(self.games):
+            buf = self.level_deaths(gi)
+            out[g] = {int(l): int(dd) for l, dd in enumerate(buf[:self.level_slots]) if dd >= 0}
+        return out
+
+    def level_deaths(self, gi) -> np.ndarray:
+        """Deaths of every saved slot of game gi, -1 = nothing saved (synchronous)."""
+        buf = np.full(max(self.level_cap, 1), -1, np.int32)
+        if self.level_cap > 0:
+            if self.device.type == 'cuda':
+                torch.cuda.synchronize(self.device)
+            self._check(self.lib.rlenv_level_deaths(self.h, gi, buf.ctypes.data_as(ctypes.c_void_p), self._stream()),
+                        'level_deaths')
+        return buf[:self.level_cap]
+
+    def place_save(self, gi, env_idx, slot_idx):
+        """After a step, on the current stream: env env_idx[j] (index within game gi) -> place slot slot_idx[j]
+        (skipped where < level_slots). int32 tensors on the env's device."""
+        assert env_idx.dtype == torch.int32 and slot_idx.dtype == torch.int32 and env_idx.is_contiguous()
+        self._check(self.lib.rlenv_place_save(self.h, gi, ctypes.c_void_p(env_idx.data_ptr()),
+                                              ctypes.c_void_p(slot_idx.data_ptr()), int(env_idx.numel()), self._stream()),
+                    'place_save')
+
+    def place_copy(self, gi, src, dst):
+        """Slot src[j] -> slot dst[j] of game gi (whole saved state), synchronous."""
+        a, b = np.ascontiguousarray(src, np.int32), np.ascontiguousarray(dst, np.int32)
+        if len(a):
+            self._check(self.lib.rlenv_place_copy(self.h, gi, a.ctypes.data_as(ctypes.c_void_p),
+                                                  b.ctypes.data_as(ctypes.c_void_p), len(a), self._stream()), 'place_copy')
+
+    def level_layout(self, gi):
+        out = np.zeros(5, np.uint32)
+        self.lib.rlenv_level_layout(self.h, gi, out.ctypes.data_as(ctypes.c_void_p))
+        return dict(stride=int(out[0]), key_cap=int(out[1]), st=int(out[2]), cap=int(out[3]), levels=int(out[4]))
+
+    def _grow_archive(self, buf, old_cap, need):
+        """A state saved with old_cap slots per game -> this env's level_cap (new slots empty); None if buf is not
+        such a state. The level-start state is last: per game records, trackers, keys, targets, frames, deaths."""
+        lay = [self.level_layout(gi) for gi in range(len(self.games))]
+        sizes = lambda cap, l: [cap * l['stride'], cap * l['st'], cap * l['key_cap'] * 4, cap * 8, cap * 4, cap * 4]  # noqa: E731
+        old_tail = sum(sum(sizes(old_cap, l)) for l in lay)
+        if len(buf) - old_tail + sum(sum(sizes(self.level_cap, l)) for l in lay) != need:
+            return None
+        out, o = [buf[:len(buf) - old_tail]], len(buf) - old_tail
+        for l in lay:
+            for k, (a, b) in enumerate(zip(sizes(old_cap, l), sizes(self.level_cap, l))):
+                out.append(buf[o:o + a])
+                o += a
+                out.append(np.full(b - a, 0xFF, np.uint8) if k == 5 else np.zeros(b - a, np.uint8))   # deaths -1 = empty
+        return np.concatenate(out)
 
     # ---- the reference API
     def _stream(self):
@@ -182,6 +281,17 @@ class RlEnv:
 
     def step(self):
         self._check(self.lib.rlenv_step(self.h, self._stream()), 'rlenv_step')
+
+    def step_game(self, gi, obs, emph):
+        """Step only the gi-th game (of self.games) on the current stream, its pictures into obs/emph ([N,...] whole
+        batch tensors; only that game's rows are written). GPU library only."""
+        self._check(self.lib.rlenv_step_game(self.h, gi, ctypes.c_void_p(obs.data_ptr()), ctypes.c_void_p(emph.data_ptr()),
+                                             self._stream()), 'rlenv_step_game')
+
+    def step_range(self, gi, start, count, obs, emph):
+        """Like step_game, for envs [start, start+count) of the gi-th game only. GPU library only."""
+        self._check(self.lib.rlenv_step_range(self.h, gi, start, count, ctypes.c_void_p(obs.data_ptr()),
+                                              ctypes.c_void_p(emph.data_ptr()), self._stream()), 'rlenv_step_range')
 
     def set_episode_level_end(self, level):
         self.lib.rlenv_set_episode_level_end(self.h, int(level))
@@ -241,7 +351,15 @@ class RlEnv:
     def load_state_dict(self, sd):
         assert sd['games'] == self.games and sd['counts'] == self.counts, 'env layout changed'
         buf = np.ascontiguousarray(sd['env'])
-        assert len(buf) == self.lib.rlenv_state_bytes(self.h), 'env state size changed'
+        need = self.lib.rlenv_state_bytes(self.h)
+        old_cap = sd.get('level_cap', 64)
+        if len(buf) < need and self.level_cap > old_cap > 0:
+            grown = self._grow_archive(buf, old_cap, need)
+            buf = buf if grown is None else grown
+        if len(buf) < need and self.level_cap > 0:
+            # saved before level starts were on: the level-start state comes last; take it from this fresh env
+            buf = np.concatenate([buf, self.state_dict()['env'][len(buf):]])
+        assert len(buf) == need, 'env state size changed'
         if self.device.type == 'cuda':
             torch.cuda.synchronize(self.device)
         self._check(self.lib.rlenv_load(self.h, buf.ctypes.data_as(ctypes.c_void_p), self._stream()), 'rlenv_load')

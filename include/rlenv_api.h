@@ -39,6 +39,30 @@ void rlenv_bind_obs(void* h, uint8_t* obs, uint8_t* emph);                // rl/
 // the rl_pack6 layout; NULL restores the byte output.
 void rlenv_bind_obs_pack6(void* h, uint8_t* packed);
 
+// ---------------------------------------------------------------- level starts and places (rl/csrc/rlenv_api.h:22-39)
+
+// rl/csrc/rlenv_api.h:26,36: room for `cap` saved states per game (call once, before start / load); slots < levels
+// are level entrances saved after each decision by the best arrival (fewest deaths, then lowest env), the rest
+// places. enable_level_starts(h, cap) = enable_places(h, cap, cap). The state they add is saved last (a state
+// saved without them is a prefix).
+int rlenv_enable_level_starts(void* h, int cap);                          // rl/csrc/rlenv_api.h:26
+int rlenv_enable_places(void* h, int cap, int levels);                    // rl/csrc/rlenv_api.h:36
+// rl/csrc/rlenv_api.h:27: chance p that a new episode of game gi starts from a saved slot, and cumulative slot
+// weights * 2^32 (cap entries in host memory; NULL = uniform over the saved slots). Between decisions.
+void rlenv_set_level_plan(void* h, int gi, double p, const uint32_t* cdf);
+void rlenv_bind_start(void* h, int32_t* start_out);      // rl/csrc/rlenv_api.h:28: [N] start slot of a finished episode, -1 power-on
+void rlenv_bind_level(void* h, int32_t* level_out);      // rl/csrc/rlenv_api.h:29: [N] level after each decision, -1 unknown
+void rlenv_bind_progress(void* h, float* progress_out);  // rl/csrc/rlenv_api.h:30: [N] progress / progress_unit, NaN invalid
+int rlenv_level_deaths(void* h, int gi, int32_t* host_out, void* stream);  // rl/csrc/rlenv_api.h:31 (synchronous)
+// rl/csrc/rlenv_api.h:37: env_idx[j] (index within game gi) -> slot_idx[j] (skipped unless levels <= slot < cap);
+// device int32 arrays, after a step on the same stream.
+int rlenv_place_save(void* h, int gi, const int32_t* env_idx, const int32_t* slot_idx, int count, void* stream);
+// rl/csrc/rlenv_api.h:38: slot src[j] -> dst[j] of game gi, host int32 arrays, synchronous.
+int rlenv_place_copy(void* h, int gi, const int32_t* src, const int32_t* dst, int count, void* stream);
+// rl/csrc/rlenv_api.h:39: out[5] = slot stride, key slots (0: the synthetic reader keeps no key set), tracker
+// bytes, cap, levels.
+void rlenv_level_layout(void* h, int gi, uint32_t* out);
+
 // ---------------------------------------------------------------- decisions (rl/csrc/rlenv_api.h:40-41)
 
 int rlenv_start(void* h, void* stream);   // rl/csrc/rlenv_api.h:40: first episode of every env

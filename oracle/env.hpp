@@ -10,6 +10,7 @@
 #pragma once
 #include <cmath>
 #include <cstdint>
+#include <limits>
 #include <vector>
 
 #include "nes.hpp"
@@ -274,12 +275,28 @@ struct Game {
     u64 tmpl_target = 0;
     int idle_tmpl = 0;
     bool start_ok = false, select_ok = false;
+    // Level starts (rl/csrc/rlenv_core.cuh GameCtx lv_*, rl/csrc/rlenv_build.hpp:212-252): lv_cap saved states,
+    // slots < lv_levels are level entrances, the rest places. lv_deaths -1 = nothing saved; lv_claim = this
+    // decision's best arrival (deaths << 32 | env), ~0 = none.
+    int lv_cap = 0, lv_levels = 0;
+    u32 lv_thresh = 0;
+    bool lv_weighted = false;
+    std::vector<Console> lv_con;
+    std::vector<rw::EnvState> lv_st;
+    std::vector<u64> lv_target;
+    std::vector<u32> lv_frame;
+    std::vector<int32_t> lv_deaths;
+    std::vector<u64> lv_claim;
+    std::vector<u32> lv_cdf;
 };
 
 struct Outputs {
     const int16_t* actions = nullptr;
     u8* obs = nullptr; u8* emph = nullptr; float* reward = nullptr; u8* done = nullptr; u8* masks = nullptr;
     u8* timeline = nullptr; u8* pads = nullptr; u32* events = nullptr; float* info = nullptr; float* parts = nullptr;
+    int32_t* start_out = nullptr;    // ep_start of the episode that just ended (where done)
+    int32_t* level_out = nullptr;    // level after the decision's update, -1 = not known yet
+    float* progress_out = nullptr;   // within-level progress / progress_unit, NaN = not valid now
 };
 
 struct PerEnv {
@@ -303,7 +320,13 @@ struct World {
     u64 run_seed = 0;
     int sticky = 1, idle_max = 0, dropout = 1, no_render = 0, episode_level_end = -1;
     int total = 0;
+    std::vector<int32_t> ep_start;   // [total] slot each episode started from, -1 = power-on; empty = level starts off
 };
+
+inline void atomic_min_u64(u64* p, u64 v) {
+    u64 cur = __atomic_load_n(p, __ATOMIC_RELAXED);
+    while (v < cur && !__atomic_compare_exchange_n(p, &cur, v, true, __ATOMIC_RELAXED, __ATOMIC_RELAXED)) {}
+}
 
 inline void emu_frame(Game& g, PerEnv& pe, int e, u8 pad) {
     Console& m = g.con[e];
@@ -351,7 +374,8 @@ inline void ph_render(Game& g, World& w, int e, int f, bool restart_pass) {
                w.out.emph + (static_cast<u64>(ge) * kFramesPerDecision + f) * kObsH);
 }
 
-// rl/csrc/rlenv_core.cuh:208-263 (power-on starts only; level starts are not part of the oracle yet)
+// rl/csrc/rlenv_core.cuh:208-263: idle count, level-start coin and pick (drawn only when level starts are on),
+// then the snapshot: a saved level start, the boot snapshot after k idle frames, or the boot snapshot.
 inline void reset_state(Game& g, World& w, int e) {
     const int ge = g.offset + e;
     PerEnv& pe = w.env[ge];
@@ -361,11 +385,33 @@ inline void reset_state(Game& g, World& w, int e) {
     pe.sticky_ctr = 0;
     int idle = 0;
     if (w.idle_max > 0) idle = static_cast<int>(ctl::rand_below(pe.sticky_seed, pe.sticky_ctr, static_cast<u32>(w.idle_max + 1)));
-    const int k = idle <= g.idle_tmpl ? idle : 0;
-    g.con[e] = k == 0 ? g.con[g.n] : g.idle_snap[k - 1];
-    pe.target = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
-    pe.ep_frame = static_cast<u32>(k);
-    pe.st = rw::EnvState{};
+    int lv = -1;
+    if (g.lv_cap > 0 && g.lv_thresh != 0 && ctl::rand_u32(pe.sticky_seed, pe.sticky_ctr) < g.lv_thresh) {
+        u32 saved = 0;
+        for (int s = 0; s < g.lv_cap; ++s) saved += g.lv_deaths[s] >= 0 ? 1u : 0u;
+        if (g.lv_weighted) {
+            const u32 u = ctl::rand_u32(pe.sticky_seed, pe.sticky_ctr);
+            for (int s = 0; s < g.lv_cap && lv < 0; ++s)
+                if (u < g.lv_cdf[s]) lv = s;
+        } else if (saved > 0) {
+            u32 pick = ctl::rand_below(pe.sticky_seed, pe.sticky_ctr, saved);
+            for (int s = 0; s < g.lv_cap && lv < 0; ++s)
+                if (g.lv_deaths[s] >= 0 && pick-- == 0) lv = s;
+        }
+    }
+    const int k = lv < 0 && idle <= g.idle_tmpl ? idle : 0;
+    if (lv >= 0) {
+        g.con[e] = g.lv_con[lv];
+        pe.target = g.lv_target[lv];
+        pe.ep_frame = g.lv_frame[lv];
+        pe.st = g.lv_st[lv];
+    } else {
+        g.con[e] = k == 0 ? g.con[g.n] : g.idle_snap[k - 1];
+        pe.target = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
+        pe.ep_frame = static_cast<u32>(k);
+        pe.st = rw::EnvState{};
+    }
+    if (!w.ep_start.empty()) w.ep_start[ge] = lv;
     pe.fault = 0;
     ctl::dropout_reset(pe.drop, seed, w.dropout != 0);
     pe.prev_applied = 0;
@@ -395,7 +441,16 @@ inline void ph_finish(Game& g, World& w, int e) {
     ++pe.ep_len;
     if (u.event_level > pe.ep_maxlvl) pe.ep_maxlvl = u.event_level;
     ctl::dropout_advance(pe.drop, w.dropout != 0);
+    if (g.lv_cap > 0 && !done && (u.events & rw::kEvLevel) != 0 && u.event_level >= 0 && u.event_level < g.lv_levels) {
+        const int d = pe.st.deaths < 0 ? 0 : pe.st.deaths;
+        atomic_min_u64(&g.lv_claim[u.event_level], (static_cast<u64>(d) << 32) | static_cast<u32>(e));
+    }
+    if (w.out.level_out) w.out.level_out[ge] = pe.st.has_best_level ? pe.st.best_level : -1;
+    if (w.out.progress_out)
+        w.out.progress_out[ge] = pe.st.has_prev && pe.st.prev.progress_valid
+            ? static_cast<float>(pe.st.prev.progress / g.spec.progress_unit) : std::numeric_limits<float>::quiet_NaN();
     if (done) {
+        if (w.out.start_out) w.out.start_out[ge] = w.ep_start.empty() ? -1 : w.ep_start[ge];
         float* inf = w.out.info + static_cast<u64>(ge) * kInfo;
         inf[0] = pe.ep_ret;
         inf[1] = static_cast<float>(pe.ep_len);
@@ -413,7 +468,8 @@ inline void ph_finish(Game& g, World& w, int e) {
 inline void ph_reset_idle(Game& g, World& w, int e) {
     PerEnv& pe = w.env[g.offset + e];
     if (!pe.resetting) return;
-    const int done = pe.ep_idle <= g.idle_tmpl ? pe.ep_idle : 0;
+    const bool lv = !w.ep_start.empty() && w.ep_start[g.offset + e] >= 0;   // a level start emulates every idle frame
+    const int done = !lv && pe.ep_idle <= g.idle_tmpl ? pe.ep_idle : 0;
     for (int i = done; i < pe.ep_idle; ++i) emu_frame(g, pe, e, 0);
 }
 
@@ -430,7 +486,8 @@ inline void ph_reset_finish_controls(Game& g, World& w, int e) {
         (void)rw::update(g.spec, g.con[e].ram, pe.ep_idle + kFramesPerDecision, pe.st);
         pe.ep_ret = 0.0f;
         pe.ep_len = 0;
-        pe.ep_maxlvl = 0;
+        const int sl = w.ep_start.empty() ? -1 : w.ep_start[ge];   // a place: its level is the tracker's
+        pe.ep_maxlvl = sl >= g.lv_levels ? (pe.st.has_best_level ? pe.st.best_level : 0) : sl > 0 ? sl : 0;
         pe.resetting = 0;
     }
     write_controls(g, w, ge);
@@ -454,6 +511,39 @@ inline void env_step(Game& g, World& w, int e) {
     }
     ph_finish(g, w, e);
     restart_phases(g, w, e);
+}
+
+// Level-start saves after every env's decision (rl/csrc/rlenv_core.cuh:344-387, order of rl/csrc/rlenv_cpu.cpp:
+// 100-116): the claimed arrival replaces the saved one when nothing is saved yet or it died no more often.
+inline void archive(Game& g, World& w) {
+    for (int s = 0; s < g.lv_levels; ++s) {
+        const u64 cl = g.lv_claim[s];
+        if (cl == ~0ull) continue;
+        const bool take = g.lv_deaths[s] < 0 || static_cast<int32_t>(cl >> 32) <= g.lv_deaths[s];
+        if (take) {
+            const int e = static_cast<int>(cl & 0xFFFFFFFFull);
+            const PerEnv& pe = w.env[g.offset + e];
+            g.lv_con[s] = g.con[e];
+            g.lv_st[s] = pe.st;
+            g.lv_target[s] = pe.target;
+            g.lv_frame[s] = pe.ep_frame;
+            g.lv_deaths[s] = static_cast<int32_t>(cl >> 32);
+        }
+        g.lv_claim[s] = ~0ull;
+    }
+}
+
+// Place save (rl/places.py, rl/csrc/rlenv_core.cuh:366-375): env e's whole state into slot s >= lv_levels; the
+// no-progress clock restarts.
+inline void place_save(Game& g, World& w, int e, int s) {
+    if (s < g.lv_levels || s >= g.lv_cap || e < 0 || e >= g.n) return;
+    const PerEnv& pe = w.env[g.offset + e];
+    g.lv_con[s] = g.con[e];
+    g.lv_st[s] = pe.st;
+    g.lv_st[s].idle_frames = 0;
+    g.lv_target[s] = pe.target;
+    g.lv_frame[s] = pe.ep_frame;
+    g.lv_deaths[s] = 0;
 }
 
 }  // namespace orc

@@ -70,6 +70,24 @@ void each_env(World& w, F&& f) {
     }
 }
 
+// Exact resume: every console (snapshot slots included) and every per-env record, then (level starts on) the
+// episode start slots and each game's saved level starts, last, in the order of rl/csrc/rlenv_build.hpp:266-279,
+// so a state saved without level starts is a prefix.
+template <class F>
+void for_each_state(World& w, F&& f) {
+    for (auto& g : w.games) f(g.con.data(), g.con.size() * sizeof(Console));
+    f(w.env.data(), w.env.size() * sizeof(PerEnv));
+    if (!w.ep_start.empty()) {
+        f(w.ep_start.data(), w.ep_start.size() * 4);
+        for (auto& g : w.games) {
+            f(g.lv_con.data(), g.lv_con.size() * sizeof(Console));
+            f(g.lv_st.data(), g.lv_st.size() * sizeof(rw::EnvState));
+            f(g.lv_target.data(), g.lv_target.size() * 8);
+            f(g.lv_frame.data(), g.lv_frame.size() * 4);
+            f(g.lv_deaths.data(), g.lv_deaths.size() * 4);
+        }
+    }
+}
 }  // namespace
 
 extern "C" {
@@ -169,26 +187,83 @@ int rlenv_start(void* h, void*) {
 int rlenv_step(void* h, void*) {
     World& w = static_cast<Handle*>(h)->w;
     each_env(w, [&](Game& g, int e) { env_step(g, w, e); });
+    for (auto& g : w.games) archive(g, w);   // after every env's decision, as rl/csrc/rlenv_cpu.cpp:100-116
     return 0;
 }
 
-// Exact resume: every console (snapshot slots included) and every per-env record, in a fixed order.
+// ---- level starts and places (rl/csrc/rlenv_cpu.cpp:119-170, rl/csrc/rlenv_build.hpp:212-252)
+
+int rlenv_enable_places(void* h, int cap, int levels) {
+    World& w = static_cast<Handle*>(h)->w;
+    if (!w.ep_start.empty() || cap <= 0 || levels <= 0 || levels > cap) {
+        g_error = "level starts: enable once, 0 < levels <= cap";
+        return 1;
+    }
+    for (auto& g : w.games) {
+        g.lv_cap = cap;
+        g.lv_levels = levels;
+        g.lv_con.assign(static_cast<std::size_t>(cap), Console{});
+        g.lv_st.assign(static_cast<std::size_t>(cap), rw::EnvState{});
+        g.lv_target.assign(static_cast<std::size_t>(cap), 0);
+        g.lv_frame.assign(static_cast<std::size_t>(cap), 0);
+        g.lv_deaths.assign(static_cast<std::size_t>(cap), -1);
+        g.lv_claim.assign(static_cast<std::size_t>(cap), ~0ull);
+        g.lv_cdf.assign(static_cast<std::size_t>(cap), 0);
+    }
+    w.ep_start.assign(static_cast<std::size_t>(w.total), -1);
+    return 0;
+}
+int rlenv_enable_level_starts(void* h, int cap) { return rlenv_enable_places(h, cap, cap); }
+void rlenv_set_level_plan(void* h, int gi, double p, const std::uint32_t* cdf) {
+    Game& g = static_cast<Handle*>(h)->w.games[static_cast<std::size_t>(gi)];
+    if (g.lv_cap == 0) return;
+    g.lv_thresh = static_cast<u32>(p <= 0.0 ? 0.0 : p >= 1.0 ? 4294967295.0 : p * 4294967296.0);
+    g.lv_weighted = cdf != nullptr;
+    if (cdf) std::memcpy(g.lv_cdf.data(), cdf, static_cast<std::size_t>(g.lv_cap) * 4);
+}
+void rlenv_bind_start(void* h, std::int32_t* p) { static_cast<Handle*>(h)->w.out.start_out = p; }
+void rlenv_bind_level(void* h, std::int32_t* p) { static_cast<Handle*>(h)->w.out.level_out = p; }
+void rlenv_bind_progress(void* h, float* p) { static_cast<Handle*>(h)->w.out.progress_out = p; }
+int rlenv_level_deaths(void* h, int gi, std::int32_t* out, void*) {
+    const Game& g = static_cast<Handle*>(h)->w.games[static_cast<std::size_t>(gi)];
+    if (g.lv_cap) std::memcpy(out, g.lv_deaths.data(), static_cast<std::size_t>(g.lv_cap) * 4);
+    return 0;
+}
+int rlenv_place_save(void* h, int gi, const std::int32_t* env_idx, const std::int32_t* slot_idx, int count, void*) {
+    World& w = static_cast<Handle*>(h)->w;
+    Game& g = w.games[static_cast<std::size_t>(gi)];
+    if (g.lv_cap == 0) return 0;
+    for (int i = 0; i < count; ++i) place_save(g, w, env_idx[i], slot_idx[i]);
+    return 0;
+}
+int rlenv_place_copy(void* h, int gi, const std::int32_t* src, const std::int32_t* dst, int count, void*) {
+    Game& g = static_cast<Handle*>(h)->w.games[static_cast<std::size_t>(gi)];
+    for (int i = 0; i < count; ++i)
+        if (src[i] < 0 || dst[i] < 0 || src[i] >= g.lv_cap || dst[i] >= g.lv_cap) { g_error = "place_copy: bad slot"; return 1; }
+    for (int i = 0; i < count; ++i) {
+        const std::size_t a = static_cast<std::size_t>(src[i]), b = static_cast<std::size_t>(dst[i]);
+        g.lv_con[b] = g.lv_con[a]; g.lv_st[b] = g.lv_st[a]; g.lv_target[b] = g.lv_target[a];
+        g.lv_frame[b] = g.lv_frame[a]; g.lv_deaths[b] = g.lv_deaths[a];
+    }
+    return 0;
+}
+void rlenv_level_layout(void* h, int gi, std::uint32_t* out) {
+    const Game& g = static_cast<Handle*>(h)->w.games[static_cast<std::size_t>(gi)];
+    out[0] = static_cast<u32>(sizeof(Console)); out[1] = 0; out[2] = static_cast<u32>(sizeof(rw::EnvState));
+    out[3] = static_cast<u32>(g.lv_cap); out[4] = static_cast<u32>(g.lv_levels);
+}
+
 std::size_t rlenv_state_bytes(void* h) {
-    const World& w = static_cast<Handle*>(h)->w;
     std::size_t n = 0;
-    for (const auto& g : w.games) n += g.con.size() * sizeof(Console);
-    return n + w.env.size() * sizeof(PerEnv);
+    for_each_state(static_cast<Handle*>(h)->w, [&](void*, std::size_t b) { n += b; });
+    return n;
 }
 int rlenv_save(void* h, std::uint8_t* out, void*) {
-    World& w = static_cast<Handle*>(h)->w;
-    for (auto& g : w.games) { std::memcpy(out, g.con.data(), g.con.size() * sizeof(Console)); out += g.con.size() * sizeof(Console); }
-    std::memcpy(out, w.env.data(), w.env.size() * sizeof(PerEnv));
+    for_each_state(static_cast<Handle*>(h)->w, [&](void* p, std::size_t b) { std::memcpy(out, p, b); out += b; });
     return 0;
 }
 int rlenv_load(void* h, const std::uint8_t* in, void*) {
-    World& w = static_cast<Handle*>(h)->w;
-    for (auto& g : w.games) { std::memcpy(g.con.data(), in, g.con.size() * sizeof(Console)); in += g.con.size() * sizeof(Console); }
-    std::memcpy(w.env.data(), in, w.env.size() * sizeof(PerEnv));
+    for_each_state(static_cast<Handle*>(h)->w, [&](void* p, std::size_t b) { std::memcpy(p, in, b); in += b; });
     return 0;
 }
 

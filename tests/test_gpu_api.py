@@ -1,0 +1,135 @@
+"""The rest of the GPU C-ABI surface against the plain step: per-game and per-range stepping
+(rl/csrc/rlenv.cu:247-267), the renderer's fused 6-bit output against rl_pack6 and the reference formula
+(rl/tests/test_host_obs_pack6.py:16-30), rl_unpack6, exact resume through save/load (rl/csrc/rlenv.cu:270-298), and
+the learner-side gathers rl_gather_rows / rl_gather_envs (rl/csrc/rlenv.cu:400-421)."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from rlenv import RlEnv
+from actions import random_legal
+
+COUNTS = {'synth00': 24, 'synth03': 16}
+OUTS = ['obs', 'emph', 'reward', 'done', 'masks', 'timeline', 'pads', 'events', 'parts']
+
+
+def _env(gpu_lib_path, seed=9):
+    e = RlEnv(COUNTS, device='cuda', lib_path=gpu_lib_path, seed=seed, sticky=True, idle_max=30, dropout=True)
+    e.start()
+    return e
+
+
+def _same(a, b, t, what=''):
+    for k in OUTS:
+        assert torch.equal(getattr(a, k), getattr(b, k)), f'step {t}: {k} differs {what}'
+
+
+def _pack6_formula(obs: np.ndarray) -> np.ndarray:
+    p = obs.reshape(-1, 4).astype(np.uint32) & 63
+    v = p[:, 0] | (p[:, 1] << 6) | (p[:, 2] << 12) | (p[:, 3] << 18)
+    return np.stack([v & 255, (v >> 8) & 255, (v >> 16) & 255], 1).astype(np.uint8).reshape(-1)
+
+
+@pytest.mark.gpu
+def test_step_game_and_range_match_step(gpu_lib_path):
+    a, b, c = _env(gpu_lib_path), _env(gpu_lib_path), _env(gpu_lib_path)
+    gen = torch.Generator().manual_seed(1)
+    sl = a.game_slices()
+    for t in range(30):
+        act = random_legal(a.masks.cpu(), gen).cuda()
+        for e in (a, b, c):
+            e.actions.copy_(act)
+        a.step()
+        for gi in range(len(b.games)):
+            b.step_game(gi, b.obs, b.emph)
+        for gi, s in enumerate(sl):
+            n = s.stop - s.start
+            c.step_range(gi, 0, n // 3, c.obs, c.emph)
+            c.step_range(gi, n // 3, n - n // 3, c.obs, c.emph)
+        torch.cuda.synchronize()
+        _same(a, b, t, 'step_game')
+        _same(a, c, t, 'step_range')
+
+
+@pytest.mark.gpu
+def test_fused_pack6_matches_rl_pack6_and_formula(gpu_lib_path):
+    a, b = _env(gpu_lib_path), _env(gpu_lib_path)
+    packed = torch.zeros(b.n, 4, 224, 180, dtype=torch.uint8, device='cuda')
+    b.bind_obs_pack6(packed)
+    ref = torch.empty_like(packed)
+    back = torch.empty_like(a.obs)
+    gen = torch.Generator().manual_seed(2)
+    stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    for t in range(12):
+        act = random_legal(a.masks.cpu(), gen).cuda()
+        a.actions.copy_(act)
+        b.actions.copy_(act)
+        a.step()
+        b.step()
+        assert a.lib.rl_pack6(ctypes.c_void_p(a.obs.data_ptr()), ctypes.c_void_p(ref.data_ptr()), a.obs.numel(), stream()) == 0
+        assert a.lib.rl_unpack6(ctypes.c_void_p(ref.data_ptr()), ctypes.c_void_p(back.data_ptr()), a.obs.numel(), stream()) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(packed, ref), f'step {t}: fused pack6 != rl_pack6(obs)'
+        assert torch.equal(back, a.obs & 63), f'step {t}: unpack6(pack6(obs)) != obs'
+        assert torch.equal(a.emph, b.emph)
+        if t == 11:
+            assert np.array_equal(ref.cpu().numpy().reshape(-1), _pack6_formula(a.obs.cpu().numpy()))
+    # ragged sizes (tail groups) through the codec
+    x = torch.randint(0, 64, (1_000_003,), dtype=torch.uint8, device='cuda')
+    n = x.numel() // 4 * 4
+    y = torch.zeros(n // 4 * 3, dtype=torch.uint8, device='cuda')
+    z = torch.zeros(n, dtype=torch.uint8, device='cuda')
+    assert a.lib.rl_pack6(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()), n, stream()) == 0
+    assert a.lib.rl_unpack6(ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(z.data_ptr()), n, stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(z, x[:n])
+    assert np.array_equal(y.cpu().numpy(), _pack6_formula(x[:n].cpu().numpy()))
+
+
+@pytest.mark.gpu
+def test_save_load_exact_resume(gpu_lib_path):
+    a = _env(gpu_lib_path)
+    gen = torch.Generator().manual_seed(3)
+    for _ in range(25):
+        a.actions.copy_(random_legal(a.masks.cpu(), gen).cuda())
+        a.step()
+    sd = a.state_dict()
+    acts = [None] * 30
+    rec = []
+    for t in range(30):
+        acts[t] = random_legal(a.masks.cpu(), gen).cuda()
+        a.actions.copy_(acts[t])
+        a.step()
+        rec.append({k: getattr(a, k).clone() for k in OUTS})
+    b = _env(gpu_lib_path, seed=77)       # another seed: everything must come from the saved state
+    b.load_state_dict(sd)
+    for t in range(30):
+        b.actions.copy_(acts[t])
+        b.step()
+        torch.cuda.synchronize()
+        for k in OUTS:
+            assert torch.equal(getattr(b, k), rec[t][k]), f'resumed step {t}: {k} differs'
+
+
+@pytest.mark.gpu
+def test_gathers(gpu_lib_path):
+    a = _env(gpu_lib_path)
+    lib = a.lib
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    T, N, row = 5, 40, 161_280
+    src = torch.randint(0, 256, (T, N, row), dtype=torch.uint8, device='cuda')
+    rows = torch.tensor([0, 7, 199, 3, 3, 120], dtype=torch.int64, device='cuda')
+    dst = torch.zeros(len(rows), row, dtype=torch.uint8, device='cuda')
+    assert lib.rl_gather_rows(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                              ctypes.c_void_p(rows.data_ptr()), len(rows), row, s) == 0
+    envs = np.array([39, 0, 17], dtype=np.int64)         # host array (copy-engine gather)
+    dst2 = torch.zeros(T, len(envs), row, dtype=torch.uint8, device='cuda')
+    assert lib.rl_gather_envs(ctypes.c_void_p(dst2.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                              envs.ctypes.data_as(ctypes.c_void_p), len(envs), T, N, row, s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src.reshape(T * N, row)[rows])
+    assert torch.equal(dst2, src[:, torch.from_numpy(envs).cuda()])
