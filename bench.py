@@ -51,6 +51,7 @@ def parse():
     ap.add_argument('--ring', type=int, default=4, help='pinned host rollout slots (decisions) for e2e')
     ap.add_argument('--cpu-leg', action='store_true', help=argparse.SUPPRESS)
     ap.add_argument('--cpu-seconds', type=float, default=15.0)
+    ap.add_argument('--cpu-steps', type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument('--no-cpu', action='store_true')
     return ap.parse_args()
 
@@ -58,35 +59,51 @@ def parse():
 # ------------------------------------------------------------------------------------------------ CPU leg
 
 def cpu_leg(args):
-    """Runs in its own process (OMP_NUM_THREADS fixed before the oracle's OpenMP starts). Prints a JSON dict."""
+    """Runs in its own process (OMP_NUM_THREADS fixed before the oracle's OpenMP starts). Prints a JSON dict.
+    --cpu-steps K: exactly W warm-up + K timed decisions (the reference arm); the env count is cut to a sample of the
+    workload when K + W full-size decisions would not fit in --cpu-seconds. Otherwise: as many decisions of the full
+    workload as fit in --cpu-seconds (the cpu_baseline leg)."""
     import torch
     from rlenv import RlEnv
     from actions import random_legal
     oracle = ROOT / 'oracle' / 'liboracle_rlenv.so'
     if not oracle.exists():
         subprocess.run(['make', '-C', str(ROOT / 'oracle'), 'all'], check=True, capture_output=True)
-    env = RlEnv({GAME: args.envs}, device='cpu', seed=args.seed * 7919, sticky=True, idle_max=30, dropout=True,
-                lib_path=oracle)
-    env.start()
+
+    def make(n):
+        e = RlEnv({GAME: n}, device='cpu', seed=args.seed * 7919, sticky=True, idle_max=30, dropout=True, lib_path=oracle)
+        e.start()
+        return e
+
+    E = args.envs
+    env = make(E)
     gen = torch.Generator().manual_seed(args.seed)
-    for _ in range(max(1, min(args.warmup, 2))):
-        env.actions.copy_(random_legal(env.masks, gen)); env.step()
+    env.actions.copy_(random_legal(env.masks, gen)); env.step()
     t0 = time.perf_counter()
     env.actions.copy_(random_legal(env.masks, gen)); env.step()
     one = time.perf_counter() - t0
-    steps = int(max(2, min(200, args.cpu_seconds / max(one, 1e-6))))
-    acts = [random_legal(env.masks, gen) for _ in range(1)]
+    if args.cpu_steps > 0:
+        K, W = args.cpu_steps, max(args.warmup, 0)
+        if (K + W) * one > args.cpu_seconds:
+            E = max(256, int(E * args.cpu_seconds / ((K + W) * one)) // 64 * 64)
+            env = make(E)
+        for _ in range(W):
+            env.actions.copy_(random_legal(env.masks, gen)); env.step()
+        steps = K
+    else:
+        steps = int(max(2, min(200, args.cpu_seconds / max(one, 1e-6))))
+    acts = [random_legal(env.masks, gen) for _ in range(4)]
     t0 = time.perf_counter()
-    for _ in range(steps):
-        env.actions.copy_(acts[0]); env.step()
+    for t in range(steps):
+        env.actions.copy_(acts[t % 4]); env.step()
     dt = time.perf_counter() - t0
     cores = int(os.environ.get('OMP_NUM_THREADS', os.cpu_count()))
-    print(json.dumps(dict(value=steps * args.envs / dt, steps=steps, seconds=dt, cores=cores)))
+    print(json.dumps(dict(value=steps * E / dt, steps=steps, seconds=dt, cores=cores, envs=E)))
 
 
-def run_cpu_leg(args, seconds):
+def run_cpu_leg(args, seconds, steps=0):
     cmd = [sys.executable, __file__, '--cpu-leg', '--envs', str(args.envs), '--seed', str(args.seed),
-           '--warmup', str(args.warmup), '--cpu-seconds', str(seconds)]
+           '--warmup', str(args.warmup), '--cpu-seconds', str(seconds), '--cpu-steps', str(steps)]
     envv = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count()), CUDA_VISIBLE_DEVICES='')
     out = subprocess.run(cmd, capture_output=True, text=True, env=envv, timeout=900)
     if out.returncode != 0:
@@ -183,6 +200,7 @@ def gpu_arm(args):
     import torch
     import torch.distributed as dist
     from rlenv import RlEnv, default_lib
+    from shard import EpisodeCounters, rank_seed
     import build as gbuild
 
     world = int(os.environ.get('WORLD_SIZE', '1'))
@@ -196,7 +214,7 @@ def gpu_arm(args):
     if not default_lib().exists():
         gbuild.build()
     E = args.envs
-    env = RlEnv({GAME: E}, device=dev, seed=args.seed * 7919 + rank, sticky=True, idle_max=30, dropout=True)
+    env = RlEnv({GAME: E}, device=dev, seed=rank_seed(args.seed, rank), sticky=True, idle_max=30, dropout=True)
     packed = [torch.empty(E * PACKED_ROW, dtype=torch.uint8, device=dev) for _ in range(2)]
     env.bind_obs_pack6(packed[0])
     env.start()
@@ -204,14 +222,10 @@ def gpu_arm(args):
     g = torch.Generator(device=dev).manual_seed(args.seed + rank)
     K, W = args.steps, args.warmup
     acts_dev = torch.randint(0, 81, (K + W, E), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
-    counters = torch.zeros(4, dtype=torch.float64, device=dev)   # finished episodes, deaths, return sum, clears
+    counters = EpisodeCounters(dev)
 
     def account():
-        d = env.done.bool()
-        counters[0] += d.sum()
-        counters[1] += torch.where(d, env.info[:, 3], 0).sum()
-        counters[2] += torch.where(d, env.info[:, 0], 0).sum()
-        counters[3] += (env.events & 2).ne(0).sum()
+        counters.account(env)
 
     stream = torch.cuda.current_stream(dev)
     for t in range(W):
@@ -234,10 +248,9 @@ def gpu_arm(args):
             env.actions.copy_(acts_dev[W + t])
             env.step()
             account()
-            if world > 1 and (t + 1) % 128 == 0:
-                dist.all_reduce(counters)
-        if world > 1:
-            dist.all_reduce(counters)
+            if (t + 1) % 128 == 0:
+                counters.rollout_end()
+        counters.rollout_end()
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:
@@ -275,8 +288,8 @@ def gpu_arm(args):
         h2d += E * 2
         env.step()
         account()
-        if world > 1 and (t + 1) % 128 == 0:
-            dist.all_reduce(counters)
+        if (t + 1) % 128 == 0:
+            counters.rollout_end()
         # small per-env results on the env's stream (the next step overwrites them), pictures on the copy stream
         sm = small[t % R]
         sm[:E * 4].copy_(env.reward.view(torch.uint8), non_blocking=True)
@@ -291,8 +304,7 @@ def gpu_arm(args):
             slot[E * PACKED_ROW:].copy_(emph_buf[b], non_blocking=True)
         d2h += E * (PACKED_ROW + EMPH_ROW + 4 + 1 + 19)
         done_ev[b].record(copy)
-    if world > 1:
-        dist.all_reduce(counters)
+    counters.rollout_end()
     stream.wait_stream(copy)
     e1.record(stream)
     torch.cuda.synchronize(dev)
@@ -342,8 +354,7 @@ def gpu_arm(args):
             kernel_ms_per_step={k: round(v / K, 4) for k, v in tm['ms'].items()},
             gpu_launches=tm['total_launches'],
             clocks=clk.summary(),
-            episodes=dict(finished=float(counters[0].item()), deaths=float(counters[1].item()),
-                          return_sum=float(counters[2].item()), level_events=float(counters[3].item())),
+            episodes=counters.as_dict(),
         )
     if world > 1:
         dist.barrier()
@@ -363,13 +374,17 @@ def main():
         # is not vendored), all host threads, a bounded sample of config 2
         if rank != 0:
             return
-        r = run_cpu_leg(args, seconds=30.0)
+        r = run_cpu_leg(args, seconds=150.0, steps=args.steps)
+        sample = f"{r['steps']} timed decisions x {r['envs']} envs" + (
+            f" (a sample of the {args.envs}-env workload, sized to end within minutes)" if r['envs'] < args.envs else '')
         line = dict(impl='reference', metric=METRIC, value=round(r['value'], 1), unit=UNIT, n_gpus=world,
-                    steps=r['steps'], warmup=min(args.warmup, 2), ms_per_step=round(1e3 * r['seconds'] / r['steps'], 3),
-                    higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8', data='synthetic',
-                    config=dict(workload='config 2: synthetic NROM, 8192 envs, 4 frames/decision', envs=args.envs),
+                    steps=r['steps'], warmup=args.warmup, ms_per_step=round(1e3 * r['seconds'] / r['steps'], 3),
+                    higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
+                    data='synthetic (seeded NROM cart synth00, random legal moves)',
+                    config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on',
+                                envs_per_gpu=args.envs, envs_timed=r['envs'], frames_per_decision=4),
                     cpu_baseline=dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
-                                      sample=f"{r['steps']} decisions x {args.envs} envs", cpu=cpu_model()),
+                                      sample=sample, cpu=cpu_model()),
                     e2e=dict(value=round(r['value'], 1), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
         print(json.dumps(line), flush=True)
         return
