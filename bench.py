@@ -6,7 +6,8 @@
 Workload (per GPU): E = 8192 envs of the seeded synthetic NROM cart 'synth00', 4 frames per
 decision, sticky moves, dropout and 0..30 idle frames at episode starts on, pictures packed to 6 bits by the
 renderer. Weak scaling: every GPU steps its own 8192 envs (seed * 7919 + rank); the per-rollout episode counters
-are all-reduced with NCCL every 128 decisions.
+are all-reduced with NCCL every 128 decisions. Every env starts its first episode at the same decision, so --age
+(1024) untimed decisions run before the W warm-up decisions: the timed steps see the steady-state restart rate.
   value   decisions/s with everything resident in HBM (env step only, CUDA events on the env's stream).
   e2e     the same through the public API with host buffers: each decision copies its actions host->device from
           pinned memory, steps, and copies the packed pictures (+ emphasis, reward, done, masks) device->host into a
@@ -48,6 +49,8 @@ def parse():
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--envs', type=int, default=8192)
     ap.add_argument('--seed', type=int, default=1)
+    ap.add_argument('--age', type=int, default=1024,
+                    help='untimed decisions before the warm-up, so that episode restarts run at their steady-state rate')
     ap.add_argument('--ring', type=int, default=4, help='pinned host rollout slots (decisions) for e2e')
     ap.add_argument('--cpu-leg', action='store_true', help=argparse.SUPPRESS)
     ap.add_argument('--cpu-seconds', type=float, default=15.0)
@@ -228,6 +231,10 @@ def gpu_arm(args):
         counters.account(env)
 
     stream = torch.cuda.current_stream(dev)
+    # every env starts its first episode at once; aging spreads the episode ends to the steady-state restart rate
+    for t in range(args.age):
+        env.actions.copy_(torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        env.step()
     for t in range(W):
         env.actions.copy_(acts_dev[t]); env.step(); account()
     torch.cuda.synchronize(dev)
@@ -342,6 +349,7 @@ def gpu_arm(args):
             data='synthetic (seeded NROM cart synth00, random moves)',
             config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on', envs_per_gpu=E,
                         frames_per_decision=4, parallelism=f'dp{world} (env shards, NCCL all-reduce of counters)',
+                        aged_decisions=args.age,
                         inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)'),
             frames_per_s=round(4 * value, 1),
             e2e=dict(value=round(e2e_value, 1), unit=UNIT, h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=d2h // K,

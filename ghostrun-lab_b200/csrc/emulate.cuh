@@ -141,12 +141,21 @@ __device__ __forceinline__ u32 v_inc_y(u32 v) {
 
 struct Hit0 { u32 dot; bool hit; };
 
-// Shared-memory staging of one warp's 32 consoles: register words, CPU RAM and OAM, each lane a column (word w of
+// Consoles per warp in the emulation kernels: lanes 0..kEnvsPerWarp-1 each run one console, the others idle. Fewer
+// consoles per warp mean fewer distinct program counters per min-PC round and a smaller shared-memory footprint, so
+// more warps are resident to hide the interpreter's dependent-instruction latency.
+#ifndef GR_ENVS_PER_WARP
+#define GR_ENVS_PER_WARP 32
+#endif
+constexpr u32 kEnvsPerWarp = GR_ENVS_PER_WARP;
+static_assert(kEnvsPerWarp == 4 || kEnvsPerWarp == 8 || kEnvsPerWarp == 16 || kEnvsPerWarp == 32, "envs per warp");
+
+// Shared-memory staging of one warp's consoles: register words, CPU RAM and OAM, each lane a column (word w of
 // lane l at [w][l]), so every lane touches its own bank whatever addresses the lanes use.
 struct EmuShared {
-    u32 regs[kRegWords][32];
-    u32 ram[kRamWords][32];
-    u32 oam[64][32];
+    u32 regs[kRegWords][kEnvsPerWarp];
+    u32 ram[kRamWords][kEnvsPerWarp];
+    u32 oam[64][kEnvsPerWarp];
 };
 
 template <u32 BOARD>
@@ -1069,7 +1078,7 @@ struct S0Ctx {
     const u32* bank;      // the writing log bank
     u32 count;
     const u8* nt;         // live nametable RAM of the env
-    const u32* soam;      // OAM word 0 of the env's shared column (stride 32 words)
+    const u32* soam;      // OAM word 0 of the env's shared column (stride kEnvsPerWarp words)
     const u8* chr;        // CHR ROM (nullptr: chr_ram)
     const u8* chr_ram;    // the env's CHR-RAM
     u32 chr_size, chr_page_mask, arrangement;
@@ -1227,7 +1236,7 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
     const u32* h = c.bank;
     const u32* ev = h + kLogHdr;
     const int kook = (h[15] & kLogKook) ? 1 : 0;
-    auto oamb = [&](u32 i) -> u32 { return reinterpret_cast<const u8*>(c.soam + (i >> 2) * 32)[i & 3u]; };
+    auto oamb = [&](u32 i) -> u32 { return reinterpret_cast<const u8*>(c.soam + (i >> 2) * kEnvsPerWarp)[i & 3u]; };
     const u32 oy = oamb(0), otile = oamb(1), oattr = oamb(2), ox = oamb(3);
     const int first = static_cast<int>(oy) + 1;
     if (first >= 240) return Hit0{0, false};

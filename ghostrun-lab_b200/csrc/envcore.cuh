@@ -286,19 +286,20 @@ struct EnvArgs {
 
 // ------------------------------------------------------------------------------------------------ records
 
-// env slot <- record (whole console state; the record's frozen frame goes to presentation slot 0)
-static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, bool chr_ram) {
+// env slot <- record (whole console state; the record's frozen frame goes to presentation slot 0); threads tid of
+// nt share the copy (one thread: 0 of 1)
+static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, bool chr_ram, u32 tid = 0, u32 nt = 1) {
     const u32* rr = reinterpret_cast<const u32*>(rec + kRecRegs);
-    for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = rr[w];
-    S.regs[static_cast<u64>(R_FSLOT) * S.Np + e] = 0;
+    for (u32 w = tid; w < static_cast<u32>(kRegWords); w += nt)
+        S.regs[static_cast<u64>(w) * S.Np + e] = w == static_cast<u32>(R_FSLOT) ? 0u : rr[w];
     const u32* ram = reinterpret_cast<const u32*>(rec + kRecRam);
-    for (u32 i = 0; i < kRamWords; ++i) S.ram[static_cast<u64>(i) * S.Np + e] = ram[i];
+    for (u32 i = tid; i < kRamWords; i += nt) S.ram[static_cast<u64>(i) * S.Np + e] = ram[i];
     const u32* pr = reinterpret_cast<const u32*>(rec + kRecPrgRam);
-    for (u32 i = 0; i < kPrgRamWords; ++i) S.prg_ram[static_cast<u64>(i) * S.Np + e] = pr[i];
-    auto cp = [](u8* d, const u8* s, u32 n) {
+    for (u32 i = tid; i < kPrgRamWords; i += nt) S.prg_ram[static_cast<u64>(i) * S.Np + e] = pr[i];
+    auto cp = [tid, nt](u8* d, const u8* s, u32 n) {
         uint4* dv = reinterpret_cast<uint4*>(d);
         const uint4* sv = reinterpret_cast<const uint4*>(s);
-        for (u32 i = 0; i < n / 16; ++i) dv[i] = sv[i];
+        for (u32 i = tid; i < n / 16; i += nt) dv[i] = sv[i];
     };
     cp(S.oam + static_cast<u64>(e) * kOamBytes, rec + kRecOam, kOamBytes);
     cp(S.nt + static_cast<u64>(e) * kNtBytes, rec + kRecNt, kNtBytes);
@@ -309,7 +310,16 @@ static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, 
     cp(S.snap_nt + sl * kNtBytes, rec + kRecSnapNt, kNtBytes);
     cp(S.snap_oam + sl * kOamBytes, rec + kRecSnapOam, kOamBytes);
     if (chr_ram && S.snap_chr) cp(S.snap_chr + sl * kChrRamBytes, rec + kRecChrRam, kChrRamBytes);
-    S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
+    if (tid == 0) S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
+}
+
+// The snapshot record an episode restarts from: a saved level start, the boot snapshot after k idle frames, or the
+// boot snapshot (rl/csrc/rlenv_core.cuh:236-243).
+__device__ __forceinline__ const u8* restart_record(const GameArgs& g, const EnvArgs& A, u32 ge) {
+    const int lv = A.ep_start ? A.ep_start[ge] : -1;
+    const int idle = A.ep_idle[ge];
+    const int k = lv < 0 && idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
+    return lv >= 0 ? g.lv_rec + static_cast<u64>(lv) * kRecBytes : g.recs + static_cast<u64>(k) * kRecBytes;
 }
 
 // record <- env slot; threads tid of nt share the copy (one thread: 0 of 1)
@@ -365,8 +375,8 @@ static __device__ void write_controls(const GameArgs& g, const EnvArgs& A, u32 g
     }
 }
 
-// rl/csrc/rlenv_core.cuh:208-263: idle count, level-start coin and pick (drawn only when level starts are on),
-// then the snapshot record: a saved level start, the boot snapshot after k idle frames, or the boot snapshot.
+// rl/csrc/rlenv_core.cuh:208-263: idle count, level-start coin and pick (drawn only when level starts are on), and
+// the episode's scalars from the chosen snapshot; the snapshot record itself is copied into the env by k_restore.
 static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) {
     const u32 ep = ++A.episode[ge];
     const u64 seed = splitmix64(splitmix64(A.run_seed ^ 0xD20F0D20F0ull) ^ (static_cast<u64>(ge) << 40) ^ static_cast<u64>(ep));
@@ -392,12 +402,10 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
     A.sticky_ctr[ge] = ctr;
     const int k = lv < 0 && idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
     if (lv >= 0) {
-        scatter_record(A.st, ge, g.lv_rec + static_cast<u64>(lv) * kRecBytes, g.cart.chr == nullptr);
         A.target[ge] = g.lv_target[lv];
         A.ep_frame[ge] = g.lv_frame[lv];
         A.trk[ge] = g.lv_st[lv];
     } else {
-        scatter_record(A.st, ge, g.recs + static_cast<u64>(k) * kRecBytes, g.cart.chr == nullptr);
         A.target[ge] = g.tmpl_target + static_cast<u64>(k) * kFrameDots;
         A.ep_frame[ge] = static_cast<u32>(k);
         Tracker t;
@@ -416,7 +424,7 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-// Emulation, one warp = 32 envs per block, consoles staged in shared memory for the whole launch.
+// Emulation, one warp = kEnvsPerWarp envs per block, consoles staged in shared memory for the whole launch.
 // `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for the listed envs.
 constexpr std::size_t kFramesSmem = sizeof(EmuShared) + 256 * sizeof(u32);
 
@@ -429,10 +437,10 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
     for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
     __syncwarp();
     const u32 total = restart ? *A.list_count : g.n;
-    for (u32 base = blockIdx.x * 32u; base < total; base += gridDim.x * 32u) {
+    for (u32 base = blockIdx.x * kEnvsPerWarp; base < total; base += gridDim.x * kEnvsPerWarp) {
         const u32 k = base + lane;
         u32 ge = 0;
-        bool valid = k < total;
+        bool valid = lane < kEnvsPerWarp && k < total;
         if (valid) {
             ge = restart ? A.list[k] : g.e0 + k;
             valid = ge >= g.e0 && ge < g.e0 + g.n;
@@ -575,6 +583,15 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
     }
 }
 
+// Restarting envs <- their snapshot records (after k_finish listed them): one block per listed env.
+static __global__ void __launch_bounds__(128) k_restore(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A) {
+    const u32 total = *A.list_count;
+    for (u32 k = blockIdx.x; k < total; k += gridDim.x) {
+        const u32 ge = A.list[k];
+        scatter_record(A.st, ge, restart_record(g, A, ge), g.cart.chr == nullptr, threadIdx.x, blockDim.x);
+    }
+}
+
 // Level-start saves after a decision's k_finish (rl/csrc/rlenv.cu:89-97, rl/csrc/rlenv_core.cuh:344-387): block s
 // takes slot s's claimed arrival when nothing is saved yet or it died no more often; the block copies the env's
 // state record, then thread 0 commits the tracker, frame target and deaths and clears the claim.
@@ -634,6 +651,7 @@ __global__ void __launch_bounds__(256, 4) k_render(const __grid_constant__ Rende
         const u32 k = it / R.frames, f = it % R.frames;
         const u32 ge = R.list ? R.list[k] : R.e0 + k;
         if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
+        if (R.skip && R.skip[ge]) continue;   // restarting: the restart pass draws its new episode's first frames
         u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)
                            : R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels;
         rd.draw(ge, f, out, R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH, R.packed != nullptr);

@@ -142,6 +142,7 @@ inline std::size_t render_smem(bool chrx_smem) { return 1024 + (chrx_smem ? 1638
 
 struct Game {
     int game_id = 0;
+    int index = 0;        // position in Env::games (its restart counter)
     GameArgs g{};
     bool chrx_smem = false;
 };
@@ -157,7 +158,15 @@ struct Env {
     KTimer* timer = nullptr;
     bool chr_ram_any = false;
     cudaEvent_t ev = nullptr;
-    ~Env() { if (ev) cudaEventDestroy(ev); delete timer; }
+    cudaStream_t side = nullptr;                  // restart work of a decision (highest priority)
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    ~Env() {
+        if (ev) cudaEventDestroy(ev);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_join) cudaEventDestroy(ev_join);
+        if (side) cudaStreamDestroy(side);
+        delete timer;
+    }
 };
 
 inline void check_launch(const char* what) {
@@ -165,6 +174,15 @@ inline void check_launch(const char* what) {
     if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+// One game slice's decision (or start) on the caller's stream `s`, with the restart work forked onto the env's
+// high-priority side stream so it overlaps the main render:
+//   s:    [list reset] k_frames -> k_finish --fork--> k_render (envs not restarting) ...... join (join_side)
+//   side:                                     k_restore -> [k_archive] -> k_frames(restart) -> k_render(restart)
+// The join comes after the last game's launch, so a game's restart work also overlaps the next game's decision.
+// k_finish decides the episode ends and lists the restarting envs; the main render leaves them out (their outputs
+// are the new episode's first frames, drawn by the restart pass), so the two branches touch disjoint envs. The level
+// archive reads the slots only in k_finish (the pick) and k_restore (the copy), so it saves after both, as the
+// reference's k_archive after k_finish (rl/csrc/rlenv.cu:165-166).
 template <u32 B>
 void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
     GameArgs g = gm.g;
@@ -172,6 +190,8 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     EnvArgs A = A0;
     if (rg.obs) { A.obs = rg.obs; A.emph = rg.emph; }
     if (rg.count >= 0) { g.e0 = gm.g.e0 + static_cast<u32>(rg.start); g.n = static_cast<u32>(rg.count); }
+    A.list = A0.list + gm.g.game_e0;              // this game's restart list and count
+    A.list_count = A0.list_count + gm.index;
     const u32 n = g.n;
     if (n == 0) return;
     const u32 tb = 128;
@@ -187,45 +207,62 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     R.chrx_smem = gm.chrx_smem ? 1u : 0u;
     const std::size_t smem = render_smem(gm.chrx_smem);
     KTimer& T = *env.timer;
+    cudaStream_t side = env.side;
+    ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
     if (!start) {
         T.begin(kKFrames, s);
-        k_frames<B><<<(n + 31) / 32, 32, kFramesSmem, s>>>(g, A, 0);
+        k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, kFramesSmem, s>>>(g, A, 0);
         T.end(kKFrames, s);
         check_launch("k_frames");
-        if (!A.no_render) {
-            R.list = nullptr;
-            const u32 items = n * kFramesPerDecision;
-            const u32 blocks = std::min<u32>((items + 7) / 8, 148u * 16u);
-            T.begin(kKRender, s);
-            k_render<B><<<blocks, 256, smem, s>>>(R);
-            T.end(kKRender, s);
-            check_launch("k_render");
-        }
     }
     T.begin(kKFinish, s);
     k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
     T.end(kKFinish, s);
     check_launch("k_finish");
-    if (!start && g.lv_cap > 0) {   // level-start saves: after every env's finish, before the restarts
-        T.begin(kKFinish, s);
-        k_archive<<<g.lv_levels, 128, 0, s>>>(g, A);
-        T.end(kKFinish, s);
+    ck(cudaEventRecord(env.ev_fork, s), "fork");
+    ck(cudaStreamWaitEvent(side, env.ev_fork, 0), "fork");
+    if (!start && !A.no_render) {
+        R.list = nullptr;
+        R.skip = A.done;
+        const u32 items = n * kFramesPerDecision;
+        const u32 blocks = std::min<u32>((items + 7) / 8, 148u * 16u);
+        T.begin(kKRender, s);
+        k_render<B><<<blocks, 256, smem, s>>>(R);
+        T.end(kKRender, s);
+        check_launch("k_render");
+    }
+    const u32 wb = (n + kEnvsPerWarp - 1) / kEnvsPerWarp;
+    T.begin(kKFinish, side);
+    k_restore<<<start ? std::min<u32>(n, 148u * 8u) : 148u, 128, 0, side>>>(g, A);
+    T.end(kKFinish, side);
+    check_launch("k_restore");
+    if (!start && g.lv_cap > 0) {   // level-start saves: after the pick and copy of every restarting env
+        T.begin(kKFinish, side);
+        k_archive<<<g.lv_levels, 128, 0, side>>>(g, A);
+        T.end(kKFinish, side);
         check_launch("k_archive");
     }
-    const u32 rb = start ? (n + 31) / 32 : std::min<u32>((n + 31) / 32, 148u);
-    T.begin(kKRestart, s);
-    k_frames<B><<<rb, 32, kFramesSmem, s>>>(g, A, 1);
-    T.end(kKRestart, s);
+    const u32 rb = start ? wb : std::min<u32>(wb, 148u * (32u / kEnvsPerWarp));
+    T.begin(kKRestart, side);
+    k_frames<B><<<rb, 32, kFramesSmem, side>>>(g, A, 1);
+    T.end(kKRestart, side);
     check_launch("k_frames restart");
     if (!A.no_render) {
         R.list = A.list;
         R.list_count = A.list_count;
+        R.skip = nullptr;
         const u32 blocks = start ? std::min<u32>((n * kFramesPerDecision + 7) / 8, 148u * 16u) : 148u;
-        T.begin(kKRestartRender, s);
-        k_render<B><<<blocks, 256, smem, s>>>(R);
-        T.end(kKRestartRender, s);
+        T.begin(kKRestartRender, side);
+        k_render<B><<<blocks, 256, smem, side>>>(R);
+        T.end(kKRestartRender, side);
         check_launch("k_render restart");
     }
+}
+
+// The caller's stream waits for the side stream's restart work (after the last game's launch_game).
+inline void join_side(const Env& env, cudaStream_t s) {
+    ck(cudaEventRecord(env.ev_join, env.side), "join");
+    ck(cudaStreamWaitEvent(s, env.ev_join, 0), "join");
 }
 
 template <u32 B>

@@ -48,6 +48,7 @@ struct RenderArgs {
     u8* emph;            // [N, 4, 224]
     const u32* list;     // env list (restart pass), nullptr = all envs [e0, e0 + count)
     const u32* list_count;
+    const u8* skip;      // envs to leave out (non-zero), nullptr = none
     u32 e0, count;       // global env range of this launch (game slice)
     u32 frames;          // frames per env to draw (4)
     u32 chrx_smem;       // 1: the cart's pattern table is staged in shared memory (8 KB CHR ROM boards)

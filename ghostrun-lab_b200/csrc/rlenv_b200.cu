@@ -40,8 +40,8 @@ void launch_one(Env& env, const Game& gm, bool start, cudaStream_t s, const Rang
 
 void launch_all(Env& env, bool start, cudaStream_t s) {
     if (!env.A.actions || !env.A.masks) throw std::runtime_error("rlenv_bind was not called");
-    ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
     for (const Game& gm : env.games) launch_one(env, gm, start, s, Range{});
+    join_side(env, s);
 }
 
 // 4 colour numbers (6 bits) -> 3 bytes, little-endian 24-bit groups (rl/csrc/rlenv.cu:126-134 layout); 16 pixels per
@@ -150,8 +150,8 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         A.ep_idle = M.allocn<i32>(N, true);
         A.fault = M.allocn<u32>(N, true);
         A.resetting = M.allocn<u8>(N);
-        A.list = M.allocn<u32>(N);
-        A.list_count = M.allocn<u32>(1);
+        A.list = M.allocn<u32>(N);                                    // per game: its slice [game_e0, game_e0 + n)
+        A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1);
         {
             std::vector<u32> init(N, 0xFFFFFFFFu);
             ck(cudaMemcpy(A.episode, init.data(), N * 4, cudaMemcpyHostToDevice), "episode init");
@@ -166,6 +166,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         for (int i = 0; i < ngames; ++i) {
             Game gm;
             gm.game_id = game_ids[i];
+            gm.index = i;
             {
                 std::lock_guard<std::mutex> lock(g_specs_mu);
                 auto it = g_specs.find(game_ids[i]);
@@ -223,6 +224,11 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             if (smem > 48 * 1024) throw std::logic_error("render shared memory exceeds the default limit");
         }
         ck(cudaEventCreateWithFlags(&env->ev, cudaEventDisableTiming), "event");
+        ck(cudaEventCreateWithFlags(&env->ev_fork, cudaEventDisableTiming), "event");
+        ck(cudaEventCreateWithFlags(&env->ev_join, cudaEventDisableTiming), "event");
+        int least = 0, greatest = 0;
+        ck(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+        ck(cudaStreamCreateWithPriority(&env->side, cudaStreamNonBlocking, greatest), "side stream");
         env->timer = new KTimer();
         ck(cudaDeviceSynchronize(), "create");
         return env;
@@ -427,10 +433,10 @@ int rlenv_step_game(void* h, int gi, std::uint8_t* obs, std::uint8_t* emph, void
         Env& env = *static_cast<Env*>(h);
         if (gi < 0 || gi >= static_cast<int>(env.games.size())) throw std::runtime_error("step_game: bad game index");
         auto s = static_cast<cudaStream_t>(stream);
-        ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
         Range rg;
         rg.obs = obs; rg.emph = emph;
         launch_one(env, env.games[gi], false, s, rg);
+        join_side(env, s);
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }
@@ -441,10 +447,10 @@ int rlenv_step_range(void* h, int gi, int start, int count, std::uint8_t* obs, s
         const Game& gm = env.games[gi];
         if (start < 0 || count <= 0 || start + count > static_cast<int>(gm.g.n)) throw std::runtime_error("step_range: bad range");
         auto s = static_cast<cudaStream_t>(stream);
-        ck(cudaMemsetAsync(env.A.list_count, 0, 4, s), "list reset");
         Range rg;
         rg.start = start; rg.count = count; rg.obs = obs; rg.emph = emph;
         launch_one(env, gm, false, s, rg);
+        join_side(env, s);
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }

@@ -42,9 +42,13 @@ def oracle_path():
 
 @pytest.fixture(scope='session')
 def gpu_lib_path():
+    """The in-tree GPU library (built on first use), or the build named by RL_CUDA_LIB (rl/rlenv.py:58-60)."""
+    import os
     import torch
     if not torch.cuda.is_available():
         pytest.skip('no CUDA device')
+    if os.environ.get('RL_CUDA_LIB'):
+        return Path(os.environ['RL_CUDA_LIB'])
     sys.path.insert(0, str(PKG))
     import build
     return build.build()
