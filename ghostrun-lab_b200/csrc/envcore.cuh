@@ -633,28 +633,45 @@ static __global__ void __launch_bounds__(128) k_place_save(const __grid_constant
     }
 }
 
-// Warp per (env, frame). Grid-stride over the work items of this game slice (or the restart list).
+// Warp per env: lanes 0-3 walk the env's 4 frame logs (phase 1), then the warp draws the frames from the walks, or
+// sequentially (Renderer::draw) a frame with a write inside a line's drawn part. Grid-stride over the envs of this
+// game slice (or the restart list).
+struct RenderWarp {
+    RWarp w;
+    FrameWalk fw[kFramesPerDecision];
+};
+constexpr u32 kRenderWarps = 8;
+inline std::size_t render_smem(bool chrx_smem) {
+    return 1024 + (chrx_smem ? 16384 : 0) + kRenderWarps * sizeof(RenderWarp);
+}
+
 template <u32 BOARD>
-__global__ void __launch_bounds__(256, 4) k_render(const __grid_constant__ RenderArgs R) {
+__global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_constant__ RenderArgs R) {
     extern __shared__ __align__(16) u8 smem[];
     u32* spread = reinterpret_cast<u32*>(smem);                 // 1 KB
     u32* chrx = spread + 256;                                   // 16 KB when staged
-    RWarp* warps = reinterpret_cast<RWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
+    RenderWarp* warps = reinterpret_cast<RenderWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
     for (u32 i = threadIdx.x; i < 256; i += blockDim.x) spread[i] = spread8(i);
     if (R.chrx_smem) for (u32 i = threadIdx.x; i < 4096; i += blockDim.x) chrx[i] = R.cart.chrx[i];
     __syncthreads();
     const u32 lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
-    Renderer<BOARD> rd(R, lane, R.chrx_smem ? chrx : R.cart.chrx, spread, warps[wid]);
-    const u32 items = (R.list ? *R.list_count : R.count) * R.frames;
-    const u32 wpb = blockDim.x >> 5;
-    for (u32 it = blockIdx.x * wpb + wid; it < items; it += gridDim.x * wpb) {
-        const u32 k = it / R.frames, f = it % R.frames;
+    RenderWarp& RW = warps[wid];
+    Renderer<BOARD> rd(R, lane, R.chrx_smem ? chrx : R.cart.chrx, spread, RW.w);
+    const u32 items = R.list ? *R.list_count : R.count;
+    for (u32 k = blockIdx.x * kRenderWarps + wid; k < items; k += gridDim.x * kRenderWarps) {
         const u32 ge = R.list ? R.list[k] : R.e0 + k;
         if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
         if (R.skip && R.skip[ge]) continue;   // restarting: the restart pass draws its new episode's first frames
-        u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)
-                           : R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels;
-        rd.draw(ge, f, out, R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH, R.packed != nullptr);
+        if (lane < R.frames) rd.walk(ge, lane, RW.fw[lane]);
+        __syncwarp();
+        for (u32 f = 0; f < R.frames; ++f) {
+            u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)
+                               : R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels;
+            u8* eo = R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH;
+            if (RW.fw[f].seq) rd.draw(ge, f, out, eo, R.packed != nullptr);
+            else rd.draw_fast(ge, f, RW.fw[f], out, eo, R.packed != nullptr);
+            __syncwarp();
+        }
     }
 }
 

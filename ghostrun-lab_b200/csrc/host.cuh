@@ -138,7 +138,6 @@ struct Range {
     u8* emph = nullptr;
 };
 
-inline std::size_t render_smem(bool chrx_smem) { return 1024 + (chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp); }
 
 struct Game {
     int game_id = 0;
@@ -224,10 +223,9 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     if (!start && !A.no_render) {
         R.list = nullptr;
         R.skip = A.done;
-        const u32 items = n * kFramesPerDecision;
-        const u32 blocks = std::min<u32>((items + 7) / 8, 148u * 16u);
+        const u32 blocks = std::min<u32>((n + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u);
         T.begin(kKRender, s);
-        k_render<B><<<blocks, 256, smem, s>>>(R);
+        k_render<B><<<blocks, 32 * kRenderWarps, smem, s>>>(R);
         T.end(kKRender, s);
         check_launch("k_render");
     }
@@ -251,9 +249,9 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
         R.list = A.list;
         R.list_count = A.list_count;
         R.skip = nullptr;
-        const u32 blocks = start ? std::min<u32>((n * kFramesPerDecision + 7) / 8, 148u * 16u) : 148u;
+        const u32 blocks = start ? std::min<u32>((n + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u) : 148u;
         T.begin(kKRestartRender, side);
-        k_render<B><<<blocks, 256, smem, side>>>(R);
+        k_render<B><<<blocks, 32 * kRenderWarps, smem, side>>>(R);
         T.end(kKRestartRender, side);
         check_launch("k_render restart");
     }
@@ -274,6 +272,8 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
     u8* recs = env.mem.allocn<u8>(static_cast<std::size_t>(idle + 1) * kRecBytes);
     ck(cudaFuncSetAttribute(k_frames<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
     ck(cudaFuncSetAttribute(k_boot<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
+    ck(cudaFuncSetAttribute(k_render<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(render_smem(gm.chrx_smem))),
+       "smem attr");
     k_boot<B><<<1, 32, kFramesSmem>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
     check_launch("k_boot");
     u32 hf[4] = {0, 0, 0, 0};

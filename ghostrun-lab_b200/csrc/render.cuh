@@ -23,21 +23,38 @@
 
 namespace gr {
 
-struct RSprites {   // per warp, shared memory: a sprite line (FetchSpriteData / RefreshSprites)
+struct RSprites {   // per warp, shared memory: a sprite line (FetchSpriteData / RefreshSprites); its count is in
+                    // the replay state (RState::nf / nd)
     u32 cw[8];      // colour nibbles of the 8 pixels left to right (flip applied), 0 = transparent
     u32 meta[8];    // palette attr (bits 0-1) | behind (bit 2) | x << 8
     u32 opq0;       // first fetched sprite: bit k = its pixel k (screen order) is opaque (sprite-0 hit data)
-    u32 n;
 };
 
 struct RWarp {      // per-warp shared scratch
     RSprites spr[2];     // fetched / drawn (double buffer)
     u32 pal[8];          // palette RAM of the replay (4 bytes per word)
+    uint4 bgp;           // background sub-palettes 0-3 as drawn: colour 0 = backdrop | 0x40, & 0x3F (from pal)
     u32 chr[8];          // 1 KB CHR page per slot (paged boards)
     u32 lzchr[8];        // CHR pages of the line whose shift registers are kept lazily
     alignas(16) u8 nt[2048];  // the frame's nametable snapshot
     alignas(16) u8 px[256];   // exact-path line buffer
     u8 emph[224];
+};
+
+// Two-phase drawing of a frame without mid-line writes: a walk of the frame log (one lane per frame) records each
+// line's replay state; the warp then draws the lines from the records with no per-line bookkeeping.
+constexpr u32 kWalkVers = 4;   // palette / CHR-page versions a frame may use; more take the sequential path
+
+struct FrameWalk {   // per frame, shared memory
+    // line l: x = v | fine x << 15 | ctrl bits 3-5 << 18 | page map << 21;
+    //         y = mask | palette version << 8 | CHR version << 12 | (mask & 0x10 at the line end) << 16 |
+    //             palette version at the line end << 20
+    uint2 rec[kObsY0 + kObsH];
+    u32 pal[kWalkVers][8];       // palette RAM per version
+    uint4 bgp[kWalkVers];        // background sub-palettes as drawn: colour 0 = backdrop | 0x40, & 0x3F
+    uint4 spal[kWalkVers];       // sprite sub-palettes & 0x3F
+    u32 chr[kWalkVers][8];       // CHR pages per version
+    u32 seq;                     // 1: the frame takes the sequential path (Renderer::draw)
 };
 
 struct RenderArgs {
@@ -97,7 +114,10 @@ struct RState {
     u32 fb;              // which of the two sprite buffers is `fetched`
     u32 spal[4];         // sprite palette taken at RefreshSprites (& 0x3F)
     u32 lazy, lz_v, lz_ctrl, lz_mir;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
+    u32 lz_saved;        // W.lzchr holds the lazy line's CHR pages (saved at the first CHR write after that line)
+    u32 nf, nd;          // sprites in the fetched / drawn buffer
     u32 cursor;
+    int next_t;          // FCEUmm time of event `cursor`, INT_MAX past the last
 };
 
 template <u32 BOARD>
@@ -119,6 +139,19 @@ struct Renderer {
         : A(a), lane(ln), chrx(cx), spread(sp), W(w) {}
 
     __device__ __forceinline__ int ev_time(u32 i) const { return fceumm_time(ev[2 * i] & 0x1FFFFu, kook); }
+    __device__ __forceinline__ int time_of(u32 i) const { return i < count ? ev_time(i) : 0x7FFFFFFF; }
+    // apply event `cursor` and move on
+    __device__ __forceinline__ void next_event(bool drawing) {
+        apply(s.cursor, drawing);
+        ++s.cursor;
+        s.next_t = time_of(s.cursor);
+    }
+    // background sub-palette words for the fast line path (after the header and every palette write)
+    __device__ __forceinline__ void make_bgp() {
+        const u32 bd = (W.pal[0] & 0x3Fu) | 0x40u;
+        W.bgp = make_uint4((W.pal[0] & 0x3F3F3F00u) | bd, (W.pal[1] & 0x3F3F3F00u) | bd,
+                           (W.pal[2] & 0x3F3F3F00u) | bd, (W.pal[3] & 0x3F3F3F00u) | bd);
+    }
     __device__ __forceinline__ u32 pal_byte(u32 i) const { return reinterpret_cast<const u8*>(W.pal)[i]; }
     __device__ __forceinline__ static constexpr bool paged() { return BOARD == kMmc1 || BOARD == kMmc3; }
 
@@ -156,6 +189,46 @@ struct Renderer {
         return chr_sel(pages, vadr) | (attr * 0x44444444u);
     }
 
+    // One line's background fetches with its uniform parts worked out once: the nametable page of the first and of
+    // the wrapped tiles, the row, the pattern row; tile(c) = fetch c of the line (the c-th coarse-x increment of v).
+    struct LineFetch {
+        u32 cx0, base_a, base_b, row, arow, ashift, rowsel, vrow;
+    };
+    __device__ __forceinline__ u32 line_tile(const LineFetch& f, u32 c) const {
+        const u32 cc = f.cx0 + c;
+        const u32 col = cc & 31u;
+        const u32 base = ((cc >> 5) & 1u) ? f.base_b : f.base_a;
+        const u32 t = W.nt[base | f.row | col];
+        const u32 ab = W.nt[base | f.arow | (col >> 2)];
+        const u32 attr = (ab >> (f.ashift | (col & 2u))) & 3u;
+        u32 sel;
+        if constexpr (BOARD == kNrom || BOARD == kUxrom) {
+            if (A.chrx_smem) sel = chrx[f.rowsel + t];
+            else sel = chr_sel(W.chr, (t << 4) + f.vrow);
+        } else {
+            sel = chr_sel(W.chr, (t << 4) + f.vrow);
+        }
+        return sel | (attr * 0x44444444u);
+    }
+    __device__ __forceinline__ u32 nt_page(u32 which) const {   // CIRAM page (0/1) << 10 of nametable `which`
+        if constexpr (paged()) return ((s.mirroring >> which) & 1u) << 10;
+        else return (A.cart.arrangement == 1 ? (which >> 1) : which) << 10 & 0x400u;
+    }
+    __device__ __forceinline__ LineFetch line_fetch(u32 v) const {
+        LineFetch f;
+        f.cx0 = v & 0x1Fu;
+        const u32 cy = (v >> 5) & 0x1Fu, which = (v >> 10) & 3u;
+        f.base_a = nt_page(which);
+        f.base_b = nt_page(which ^ 1u);
+        f.row = cy << 5;
+        f.arow = 0x3C0u | ((cy >> 2) << 3);
+        f.ashift = (cy & 2u) << 1;
+        const u32 fy = (v >> 12) & 7u;
+        f.rowsel = fy * 512u + ((s.ctrl & 0x10u) << 4);
+        f.vrow = ((s.ctrl & 0x10u) << 8) | fy;
+        return f;
+    }
+
     __device__ void apply(u32 i, bool drawing) {
         const u32 w1 = ev[2 * i + 1];
         const u32 value = w1 & 0xFFu, aux = (w1 >> 8) & 0xFFu;
@@ -178,12 +251,22 @@ struct Renderer {
                 break;
             case kEvPalette:
                 __syncwarp();
-                if (lane == 0) reinterpret_cast<u8*>(W.pal)[aux & 31u] = static_cast<u8>(value);
+                if (lane == 0) {
+                    reinterpret_cast<u8*>(W.pal)[aux & 31u] = static_cast<u8>(value);
+                    make_bgp();
+                }
                 __syncwarp();
                 s.v = (s.v + inc) & 0x7FFFu;
                 break;
             case kEvChr:
                 __syncwarp();
+                if constexpr (paged()) {
+                    if (s.lazy && !s.lz_saved) {   // the lazy line was fetched with the pages before this write
+                        if (lane < 8) W.lzchr[lane] = W.chr[lane];
+                        s.lz_saved = 1;
+                        __syncwarp();
+                    }
+                }
                 if (lane == 0) W.chr[aux & 7u] = value;
                 __syncwarp();
                 break;
@@ -196,8 +279,9 @@ struct Renderer {
     __device__ void materialize_shift() {
         if (!s.lazy) return;
         __syncwarp();
-        const u32 c32 = fetch(v_inc_x_n(s.lz_v, 32), s.lz_ctrl, s.lz_mir, W.lzchr);
-        const u32 c33 = fetch(v_inc_x_n(s.lz_v, 33), s.lz_ctrl, s.lz_mir, W.lzchr);
+        const u32* pages = s.lz_saved ? W.lzchr : W.chr;
+        const u32 c32 = fetch(v_inc_x_n(s.lz_v, 32), s.lz_ctrl, s.lz_mir, pages);
+        const u32 c33 = fetch(v_inc_x_n(s.lz_v, 33), s.lz_ctrl, s.lz_mir, pages);
         u32 lo32 = 0, hi32 = 0, lo33 = 0, hi33 = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -279,11 +363,11 @@ struct Renderer {
             if (pp >= 268 && tofix) { if (s.mask & 0x18u) s.v = v_inc_y(s.v); tofix = false; }
             check(pp);
         };
-        while (s.cursor < count && ev_time(s.cursor) < start + 272) {
+        while (s.next_t < start + 272) {
             const u32 kind = ev[2 * s.cursor] >> 24;
             if (kind != kEvDataWrite && kind != kEvPalette)
-                update(ev_time(s.cursor) + 3 * static_cast<int>((ev[2 * s.cursor] >> 17) & 0xFu) - start);
-            apply(s.cursor++, true);
+                update(s.next_t + 3 * static_cast<int>((ev[2 * s.cursor] >> 17) & 0xFu) - start);
+            next_event(true);
         }
         update(272);
         if (tofix) { if (s.mask & 0x18u) s.v = v_inc_y(s.v); tofix = false; }
@@ -305,6 +389,7 @@ struct Renderer {
             s.blurp = b0 & 1u;
             u32 n = 0;
             if (b0 | b1) {
+                __syncwarp();   // the previous line's readers of this buffer are done
                 const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
                 const u32 lt = (1u << lane) - 1u;
                 const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
@@ -327,18 +412,21 @@ struct Renderer {
                         if (r == 0) f.opq0 = nib_opaque8(cw);
                     }
                 }
+                __syncwarp();
             }
-            if (lane == 0) f.n = n;
-            __syncwarp();
+            s.nf = n;
         }
-        while (s.cursor < count && ev_time(s.cursor) < start + 278) apply(s.cursor++, true);
+        while (s.next_t < start + 278) next_event(true);
         if (s.mask & 0x18u) s.v = (s.v & 0xFBE0u) | (s.t & 0x041Fu);
-        while (s.cursor < count && ev_time(s.cursor) < start + 341) apply(s.cursor++, true);
+        while (s.next_t < start + 341) next_event(true);
         if (s.mask & 0x10u) {
             s.spork = 0;
             const RSprites& f = W.spr[s.fb];
-            if (f.n != 0) {
+            if (s.nf != 0) {
                 s.fb ^= 1u;    // drawn = fetched (the other buffer becomes the next fetch target)
+                const u32 t = s.nd;
+                s.nd = s.nf;
+                s.nf = t;
                 for (int q = 0; q < 4; ++q) s.spal[q] = W.pal[4 + q] & 0x3F3F3F3Fu;
                 if (s.blurp && !s.hit && f.opq0) {
                     s.sphitx = f.meta[0] >> 8;
@@ -346,6 +434,321 @@ struct Renderer {
                 }
                 s.spork = 1;
             }
+        }
+    }
+
+    // ================================================================ two-phase path
+    // ---- phase 1 (one lane per frame): replay the frame log's register state line by line (the same order of event
+    // application, v increments and line ends as draw / end_of_line) and record it; pixels, sprites and sprite-0
+    // bookkeeping are left to phase 2 (sprite-0 state only changes what a mid-line write sees, and such frames take
+    // the sequential path).
+    struct Walk {
+        u32 ctrl, mask, x, v, t, mir, pv, cv, cursor, count, seq;
+        bool pused, cused;
+        int kook, next_t;
+        const u32* ev;
+    };
+    __device__ __forceinline__ int walk_time(const Walk& w, u32 i) const {
+        return i < w.count ? fceumm_time(w.ev[2 * i] & 0x1FFFFu, w.kook) : 0x7FFFFFFF;
+    }
+    __device__ static void derive(FrameWalk& F, u32 pv) {
+        const u32* p = F.pal[pv];
+        const u32 bd = (p[0] & 0x3Fu) | 0x40u;
+        F.bgp[pv] = make_uint4((p[0] & 0x3F3F3F00u) | bd, (p[1] & 0x3F3F3F00u) | bd, (p[2] & 0x3F3F3F00u) | bd,
+                               (p[3] & 0x3F3F3F00u) | bd);
+        F.spal[pv] = make_uint4(p[4] & 0x3F3F3F3Fu, p[5] & 0x3F3F3F3Fu, p[6] & 0x3F3F3F3Fu, p[7] & 0x3F3F3F3Fu);
+    }
+    __device__ void walk_apply(Walk& w, FrameWalk& F, bool drawing) const {
+        const u32 w0 = w.ev[2 * w.cursor], w1 = w.ev[2 * w.cursor + 1];
+        const u32 value = w1 & 0xFFu, aux = (w1 >> 8) & 0xFFu;
+        const u32 inc = (w.ctrl & 4u) ? 32u : 1u;
+        switch (w0 >> 24) {
+            case kEvCtrl: w.ctrl = value; w.t = (w.t & 0xF3FFu) | ((value & 3u) << 10); break;
+            case kEvMask: w.mask = value; break;
+            case kEvScroll:
+                if (aux == 0) { w.t = (w.t & 0xFFE0u) | (value >> 3); w.x = value & 7u; }
+                else w.t = (w.t & 0x8C1Fu) | ((value & 0xF8u) << 2) | ((value & 7u) << 12);
+                break;
+            case kEvAddr:
+                if (aux == 0) w.t = (w.t & 0x00FFu) | ((value & 0x3Fu) << 8);
+                else { w.t = (w.t & 0xFF00u) | value; w.v = w.t; }
+                break;
+            case kEvDataWrite: w.v = (w.v + (aux + 1u) * inc) & 0x7FFFu; break;
+            case kEvDataRead:
+                if (drawing && (w.mask & 0x18u)) w.v = v_inc_y(w.v);
+                else w.v = (w.v + inc) & 0x7FFFu;
+                break;
+            case kEvPalette:
+                if (w.pused) {   // the current version is drawn with: the write starts a new one
+                    if (w.pv + 1 >= kWalkVers) { w.seq = 1; break; }
+                    for (int k = 0; k < 8; ++k) F.pal[w.pv + 1][k] = F.pal[w.pv][k];
+                    ++w.pv;
+                    w.pused = false;
+                }
+                reinterpret_cast<u8*>(F.pal[w.pv])[aux & 31u] = static_cast<u8>(value);
+                w.v = (w.v + inc) & 0x7FFFu;
+                break;
+            case kEvChr:
+                if (w.cused) {
+                    if (w.cv + 1 >= kWalkVers) { w.seq = 1; break; }
+                    for (int k = 0; k < 8; ++k) F.chr[w.cv + 1][k] = F.chr[w.cv][k];
+                    ++w.cv;
+                    w.cused = false;
+                }
+                F.chr[w.cv][aux & 7u] = value;
+                break;
+            case kEvMirror: w.mir = value; break;
+            default: break;
+        }
+        ++w.cursor;
+        w.next_t = walk_time(w, w.cursor);
+    }
+    __device__ void walk(u32 ge, u32 f, FrameWalk& F) const {
+        const u64 sl = static_cast<u64>(ge) * 4 + f;
+        const u32* hh = A.st.log + (static_cast<u64>(ge) * kLogBanks + A.st.slot_bank[sl]) * kLogBankWords;
+        Walk w;
+        w.ev = hh + kLogHdr;
+        w.count = min(hh[0] & ~kLogOverflow, kLogEv);
+        w.kook = (hh[15] & kLogKook) ? 1 : 0;
+        w.ctrl = hh[1] & 0xFFu; w.mask = (hh[1] >> 8) & 0xFFu; w.x = (hh[1] >> 16) & 7u;
+        w.v = hh[2] & 0x7FFFu; w.t = (hh[2] >> 16) & 0x7FFFu;
+        w.mir = hh[5] & 0xFu;
+        for (int k = 0; k < 8; ++k) {
+            F.pal[0][k] = hh[7 + k];
+            F.chr[0][k] = (hh[3 + (k >> 2)] >> ((k & 3) * 8)) & 0xFFu;
+        }
+        w.pv = 0; w.cv = 0; w.pused = false; w.cused = false; w.seq = 0;
+        w.cursor = 0;
+        w.next_t = walk_time(w, 0);
+        while (w.next_t < -16 && !w.seq) walk_apply(w, F, false);
+        if (w.mask & 0x18u) w.v = w.t;
+        for (int l = 0; l < kObsY0 + kObsH && !w.seq; ++l) {
+            const int start = l * 341 - 16;
+            if (w.next_t < start + 272) { w.seq = 1; break; }   // a write inside the drawn part of the line
+            if (!w.pused) { derive(F, w.pv); w.pused = true; }
+            w.cused = true;
+            const u32 rx = w.v | (w.x << 15) | (((w.ctrl >> 3) & 7u) << 18) | ((w.mir & 0xFu) << 21);
+            const u32 ry = w.mask | (w.pv << 8) | (w.cv << 12);
+            const u32 fetch_mask = w.mask;
+            if (w.mask & 0x18u) w.v = v_inc_y(v_inc_x_n(w.v, 34));
+            while (w.next_t < start + 278 && !w.seq) walk_apply(w, F, true);
+            if (w.mask & 0x18u) w.v = (w.v & 0xFBE0u) | (w.t & 0x041Fu);
+            while (w.next_t < start + 341 && !w.seq) walk_apply(w, F, true);
+            if (!w.pused) { derive(F, w.pv); w.pused = true; }
+            // sprites switched on during the hblank of a line drawn with rendering off would show an older line's
+            // sprite fetch (the buffer's count is stale): the sequential path keeps that
+            if (!(fetch_mask & 0x18u) && (w.mask & 0x10u)) w.seq = 1;
+            F.rec[l] = make_uint2(rx, ry | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20));
+        }
+        F.seq = w.seq;
+    }
+
+    // One line's background fetch from a record (v, control, page map given).
+    __device__ __forceinline__ LineFetch line_fetch_at(u32 v, u32 ctrl, u32 mir) const {
+        LineFetch f;
+        f.cx0 = v & 0x1Fu;
+        const u32 cy = (v >> 5) & 0x1Fu, which = (v >> 10) & 3u;
+        if constexpr (paged()) {
+            f.base_a = ((mir >> which) & 1u) << 10;
+            f.base_b = ((mir >> (which ^ 1u)) & 1u) << 10;
+        } else {
+            f.base_a = nt_page(which);
+            f.base_b = nt_page(which ^ 1u);
+        }
+        f.row = cy << 5;
+        f.arow = 0x3C0u | ((cy >> 2) << 3);
+        f.ashift = (cy & 2u) << 1;
+        const u32 fy = (v >> 12) & 7u;
+        f.rowsel = fy * 512u + ((ctrl & 0x10u) << 4);
+        f.vrow = ((ctrl & 0x10u) << 8) | fy;
+        return f;
+    }
+    __device__ __forceinline__ u32 line_tile_p(const LineFetch& f, u32 c, const u32* pages) const {
+        const u32 cc = f.cx0 + c;
+        const u32 col = cc & 31u;
+        const u32 base = ((cc >> 5) & 1u) ? f.base_b : f.base_a;
+        const u32 t = W.nt[base | f.row | col];
+        const u32 ab = W.nt[base | f.arow | (col >> 2)];
+        const u32 attr = (ab >> (f.ashift | (col & 2u))) & 3u;
+        u32 sel;
+        if constexpr (BOARD == kNrom || BOARD == kUxrom) {
+            if (A.chrx_smem) sel = chrx[f.rowsel + t];
+            else sel = chr_sel(pages, (t << 4) + f.vrow);
+        } else {
+            sel = chr_sel(pages, (t << 4) + f.vrow);
+        }
+        return sel | (attr * 0x44444444u);
+    }
+
+    // ---- phase 2 (the whole warp): draw frame f of env ge from its walk, 4 lines at a time: lane group g = lane / 8
+    // draws line l0 + g, lane j = lane % 8 its crop pixels 32j..32j+31 (screen x 8+32j..): fetches 4j+1..4j+5.
+    // The lines are independent given the records: the sprites drawn on line l are those fetched at the end of line
+    // l - 1 (FetchSpriteData with line l - 1's control, CHR pages and OAM) when line l - 1 fetched (rendering on)
+    // and the refresh at its end had sprites on (which is line l's mask); the walk sends the one case where an older
+    // fetch would show to the sequential path. Crop x starts at 8, so the left-column clips never show.
+    __device__ __forceinline__ static void put_sprite(u32 win, u32 m, u32 pw, bool beh, u32& sn, u32& sa, u32& sb) {
+        const u32 om = ((win | (win >> 1)) & 0x11111111u) * 0xFu;
+        sn = (sn & ~om) | ((win | pw) & om);
+        sa |= om;
+        sb = beh ? (sb | om) : (sb & ~om);
+        (void)m;
+    }
+    __device__ __forceinline__ static u32 sprite_mix(u32 bg, u32 sn16, u32 sa16, u32 sb16, const uint4& sp) {
+        const u32 c = pal_lookup4(sn16, sp.x, sp.y, sp.z, sp.w);
+        const u32 any = nib_to_bytes(sa16), beh = nib_to_bytes(sb16);
+        const u32 tr = ((bg & 0x40404040u) >> 6) * 0xFFu;
+        const u32 use = any & (~beh | tr);
+        return (bg & ~use) | (c & use);
+    }
+    __device__ void draw_fast(u32 ge, u32 f, const FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
+        const u64 sl = static_cast<u64>(ge) * 4 + f;
+        chr_ram = (A.cart.chr == nullptr && A.st.snap_chr) ? A.st.snap_chr + sl * kChrRamBytes : nullptr;
+        {   // the frame's nametable into shared memory, its OAM into registers (2 entries per lane)
+            const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
+            uint4* nts = reinterpret_cast<uint4*>(W.nt);
+            const uint4 q0 = ntg[lane], q1 = ntg[lane + 32], q2 = ntg[lane + 64], q3 = ntg[lane + 96];
+            const u32* oamw = reinterpret_cast<const u32*>(A.st.snap_oam + sl * kOamBytes);
+            spA = oamw[lane];
+            spB = oamw[lane + 32];
+            __syncwarp();
+            nts[lane] = q0; nts[lane + 32] = q1; nts[lane + 64] = q2; nts[lane + 96] = q3;
+            __syncwarp();
+        }
+        const u32 g = lane >> 3, j = lane & 7u;
+        const u32 lt = (1u << lane) - 1u;
+        uint2* sbuf = reinterpret_cast<uint2*>(W.px);   // [4 lines][8 sprites] (colour nibbles, meta)
+        for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
+            // ---- sprites of lines l0..l0+3 (fetched at the end of the line above each)
+            u32 nsp = 0;   // this lane group's sprite count
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int e = l0 + k - 1;
+                const uint2 re = F.rec[e];
+                const u32 ctrl = ((re.x >> 18) & 7u) << 3;
+                u32 n = 0;
+                if ((re.y & 0x18u) && (re.y & (1u << 16))) {
+                    const u32 hgt = (ctrl & 0x20u) ? 16u : 8u;
+                    const bool in0 = static_cast<u32>(e - static_cast<int>(spA & 0xFFu)) < hgt;
+                    const bool in1 = static_cast<u32>(e - static_cast<int>(spB & 0xFFu)) < hgt;
+                    const u32 b0 = __ballot_sync(0xFFFFFFFFu, in0), b1 = __ballot_sync(0xFFFFFFFFu, in1);
+                    if (b0 | b1) {
+                        const u32* pages = F.chr[(re.y >> 12) & 3u];
+                        const u32 vofs = ((ctrl & 0x08u) && !(ctrl & 0x20u)) ? 0x1000u : 0u;
+                        const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
+                        n = min(__popc(b0) + __popc(b1), 8);
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const bool in = half ? in1 : in0;
+                            const u32 rk = half ? r1 : r0;
+                            if (in && rk < 8) {
+                                const u32 spw = half ? spB : spA;
+                                const u32 tile = (spw >> 8) & 0xFFu, attr = (spw >> 16) & 0xFFu, xx = spw >> 24;
+                                const u32 t = static_cast<u32>(e - static_cast<int>(spw & 0xFFu));
+                                u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+                                if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (ctrl & 0x20u) >> 1; vadr -= t & 8u; }
+                                else { vadr += t; vadr += t & 8u; }
+                                u32 cw = chr_sel(pages, vadr & 0x1FFFu);
+                                if (attr & 0x40u) cw = nib_reverse(cw);
+                                sbuf[k * 8 + rk] = make_uint2(cw, (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8));
+                            }
+                        }
+                    }
+                }
+                if (g == static_cast<u32>(k)) nsp = n;
+            }
+            __syncwarp();
+            // ---- background of line l (this lane group's), 32 pixels per lane
+            const int l = l0 + static_cast<int>(g);
+            const uint2 r = F.rec[l];
+            const u32 mask = r.y & 0xFFu;
+            const uint4 P = F.bgp[(r.y >> 8) & 3u];
+            const u32 bdw = (P.x & 0xFFu) * 0x01010101u;
+            u32 s0 = 0, s1 = 0, s2 = 0, s3 = 0;   // pixel nibbles (colour | attribute << 2), 8 per word
+            const bool bg = (mask & 0x08u) != 0;
+            if (bg) {
+                const u32 ctrl = ((r.x >> 18) & 7u) << 3;
+                const u32* pages = F.chr[(r.y >> 12) & 3u];
+                const LineFetch lf = line_fetch_at(r.x & 0x7FFFu, ctrl, (r.x >> 21) & 0xFu);
+                const u32 x4 = 4u * ((r.x >> 15) & 7u);
+                const u32 c0 = line_tile_p(lf, 4 * j + 1, pages), c1 = line_tile_p(lf, 4 * j + 2, pages);
+                const u32 c2 = line_tile_p(lf, 4 * j + 3, pages), c3 = line_tile_p(lf, 4 * j + 4, pages);
+                const u32 c4 = line_tile_p(lf, 4 * j + 5, pages);
+                s0 = __funnelshift_r(c0, c1, x4); s1 = __funnelshift_r(c1, c2, x4);
+                s2 = __funnelshift_r(c2, c3, x4); s3 = __funnelshift_r(c3, c4, x4);
+            }
+            u32 px[8];   // colour bytes (0x40 = background colour 0), 4 pixels per word
+            if (bg) {
+                px[0] = pal_lookup4(s0, P.x, P.y, P.z, P.w); px[1] = pal_lookup4(s0 >> 16, P.x, P.y, P.z, P.w);
+                px[2] = pal_lookup4(s1, P.x, P.y, P.z, P.w); px[3] = pal_lookup4(s1 >> 16, P.x, P.y, P.z, P.w);
+                px[4] = pal_lookup4(s2, P.x, P.y, P.z, P.w); px[5] = pal_lookup4(s2 >> 16, P.x, P.y, P.z, P.w);
+                px[6] = pal_lookup4(s3, P.x, P.y, P.z, P.w); px[7] = pal_lookup4(s3 >> 16, P.x, P.y, P.z, P.w);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) px[q] = bdw;
+            }
+            // ---- sprites over this lane's 32 pixels (CopySprites, patch:1615-1640: the first in OAM order wins)
+            const u32 nmax = __reduce_max_sync(0xFFFFFFFFu, nsp);
+            if (nmax) {
+                u32 n0 = 0, n1 = 0, n2 = 0, n3 = 0, a0 = 0, a1 = 0, a2 = 0, a3 = 0, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
+                const int x0 = 8 + 32 * static_cast<int>(j);
+                for (int i = static_cast<int>(nmax) - 1; i >= 0; --i) {
+                    if (i >= static_cast<int>(nsp)) continue;
+                    const uint2 sd = sbuf[g * 8 + static_cast<u32>(i)];
+                    const int rel = static_cast<int>(sd.y >> 8) - x0;
+                    if (rel <= -8 || rel >= 32) continue;
+                    const int w = rel >> 3;                  // -1..3: word of the sprite's first pixel
+                    const u32 o = static_cast<u32>(rel) & 7u;
+                    const u32 lo = sd.x << (4 * o), hi = o ? (sd.x >> (32 - 4 * o)) : 0u;
+                    const u32 pw = (sd.y & 3u) * 0x44444444u;
+                    const bool beh = (sd.y & 4u) != 0;
+                    if (w == 0) put_sprite(lo, 0, pw, beh, n0, a0, b0);
+                    if (w == 1) put_sprite(lo, 1, pw, beh, n1, a1, b1);
+                    if (w == 2) put_sprite(lo, 2, pw, beh, n2, a2, b2);
+                    if (w == 3) put_sprite(lo, 3, pw, beh, n3, a3, b3);
+                    if (hi) {
+                        if (w == -1) put_sprite(hi, 0, pw, beh, n0, a0, b0);
+                        if (w == 0) put_sprite(hi, 1, pw, beh, n1, a1, b1);
+                        if (w == 1) put_sprite(hi, 2, pw, beh, n2, a2, b2);
+                        if (w == 2) put_sprite(hi, 3, pw, beh, n3, a3, b3);
+                    }
+                }
+                if (a0 | a1 | a2 | a3) {
+                    const uint4 sp = F.spal[(F.rec[l - 1].y >> 20) & 3u];
+                    if (a0) { px[0] = sprite_mix(px[0], n0, a0, b0, sp); px[1] = sprite_mix(px[1], n0 >> 16, a0 >> 16, b0 >> 16, sp); }
+                    if (a1) { px[2] = sprite_mix(px[2], n1, a1, b1, sp); px[3] = sprite_mix(px[3], n1 >> 16, a1 >> 16, b1 >> 16, sp); }
+                    if (a2) { px[4] = sprite_mix(px[4], n2, a2, b2, sp); px[5] = sprite_mix(px[5], n2 >> 16, a2 >> 16, b2 >> 16, sp); }
+                    if (a3) { px[6] = sprite_mix(px[6], n3, a3, b3, sp); px[7] = sprite_mix(px[7], n3 >> 16, a3 >> 16, b3 >> 16, sp); }
+                }
+            }
+            const u32 keep = ((mask & 1u) && (mask & 0x18u)) ? 0x30303030u : 0x3F3F3F3Fu;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) px[q] &= keep;
+            const int y = l - kObsY0;
+            if (!pack6) {
+                uint4* row = reinterpret_cast<uint4*>(obs_out + static_cast<u64>(y) * kObsW + 32u * j);
+                row[0] = make_uint4(px[0], px[1], px[2], px[3]);
+                if (j < 7) row[1] = make_uint4(px[4], px[5], px[6], px[7]);
+            } else {
+                u32 gq[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) gq[q] = pack_group6(px[q]);
+                u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3) + 24u * j);
+                row[0] = gq[0] | (gq[1] << 24);
+                row[1] = (gq[1] >> 8) | (gq[2] << 16);
+                row[2] = (gq[2] >> 16) | (gq[3] << 8);
+                if (j < 7) {
+                    row[3] = gq[4] | (gq[5] << 24);
+                    row[4] = (gq[5] >> 8) | (gq[6] << 16);
+                    row[5] = (gq[6] >> 16) | (gq[7] << 8);
+                }
+            }
+            __syncwarp();   // sbuf is rewritten by the next iteration
+        }
+        for (int i = lane; i < kObsH / 4; i += 32) {   // emphasis bits of the 224 drawn lines
+            u32 e4 = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) e4 |= ((F.rec[kObsY0 + 4 * i + k].y >> 5) & 7u) << (8 * k);
+            reinterpret_cast<u32*>(emph_out)[i] = e4;
         }
     }
 
@@ -374,44 +777,46 @@ struct Renderer {
             W.chr[lane] = (h[3 + (lane >> 2)] >> ((lane & 3) * 8)) & 0xFFu;
             W.pal[lane] = h[7 + lane];
         }
-        if (lane == 0) { W.spr[0].n = 0; W.spr[1].n = 0; }
+        __syncwarp();
+        if (lane == 0) make_bgp();
         __syncwarp();
         s.mirroring = h[5] & 0xFFu;
         s.sh0 = s.sh1 = s.at = 0;
         s.blurp = 0; s.spork = 0; s.hit = 0; s.sphitx = 0x100u; s.sphitmask = 0; s.hit_x = 0;
         s.fb = 0;
         s.spal[0] = s.spal[1] = s.spal[2] = s.spal[3] = 0;
-        s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mir = 0;
+        s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mir = 0; s.lz_saved = 0;
+        s.nf = 0; s.nd = 0;
         s.cursor = 0;
-        while (s.cursor < count && ev_time(s.cursor) < -16) apply(s.cursor++, false);
+        s.next_t = time_of(0);
+        while (s.next_t < -16) next_event(false);
         if (s.mask & 0x18u) s.v = s.t;
 
         for (int l = 0; l < kObsY0 + kObsH; ++l) {
             const int start = l * 341 - 16;
             u32 w0, w1;   // this lane's 8 background pixels (colour | 0x40 transparent), byte k = pixel 8L+k
-            if (s.cursor < count && ev_time(s.cursor) < start + 272) {
+            if (s.next_t < start + 272) {
                 exact_line(l);
                 const uint2 q = reinterpret_cast<const uint2*>(W.px)[lane];
                 w0 = q.x; w1 = q.y;
             } else {
-                const u32 bd = (pal_byte(0) & 0x3Fu) | 0x40u;
-                const u32 bdw = bd * 0x01010101u;
+                const uint4 P = W.bgp;   // byte 0 of each word: backdrop | 0x40
+                const u32 bdw = (P.x & 0xFFu) * 0x01010101u;
                 if (!(s.mask & 0x18u)) {
                     w0 = w1 = bdw;   // rendering off: backdrop, nothing fetched, v unchanged
                 } else {
                     const u32 v0 = s.v;
-                    const u32 ca = fetch(v_inc_x_n(v0, lane), s.ctrl, s.mirroring, W.chr);
+                    const LineFetch lf = line_fetch(v0);
+                    const u32 ca = line_tile(lf, lane);
                     u32 cn = __shfl_down_sync(0xFFFFFFFFu, ca, 1);
                     // fetch 32 only feeds pixels 248..255 (right of the crop): needed for a sprite-0 check there
                     const bool need32 = s.sphitx != 0x100u && s.sphitx >= 241u;
-                    if (need32 && lane == 31) cn = fetch(v_inc_x_n(v0, 32), s.ctrl, s.mirroring, W.chr);
+                    if (need32 && lane == 31) cn = line_tile(lf, 32);
                     const u32 sel = __funnelshift_r(ca, cn, 4 * s.x);
                     if (s.mask & 0x08u) {
                         // colour 0 of every sub-palette shows the backdrop
-                        const u32 P0 = (W.pal[0] & 0x3F3F3F00u) | bd, P1 = (W.pal[1] & 0x3F3F3F00u) | bd;
-                        const u32 P2 = (W.pal[2] & 0x3F3F3F00u) | bd, P3 = (W.pal[3] & 0x3F3F3F00u) | bd;
-                        w0 = pal_lookup4(sel, P0, P1, P2, P3);
-                        w1 = pal_lookup4(sel >> 16, P0, P1, P2, P3);
+                        w0 = pal_lookup4(sel, P.x, P.y, P.z, P.w);
+                        w1 = pal_lookup4(sel >> 16, P.x, P.y, P.z, P.w);
                         if (lane == 0 && !(s.mask & 0x02u)) { w0 = bdw; w1 = bdw; }
                     } else {
                         w0 = w1 = bdw;
@@ -431,8 +836,7 @@ struct Renderer {
                         const u32 hits = win & s.sphitmask & lim;
                         if (hits) { s.hit = 1; s.hit_x = sx + (__ffs(hits) - 1); s.sphitx = 0x100u; }
                     }
-                    s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mir = s.mirroring;
-                    if constexpr (paged()) { if (lane < 8) W.lzchr[lane] = W.chr[lane]; }
+                    s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mir = s.mirroring; s.lz_saved = 0;
                     s.v = v_inc_y(v_inc_x_n(v0, 34));
                 }
             }
@@ -442,7 +846,7 @@ struct Renderer {
                 const RSprites& d = W.spr[s.fb ^ 1u];
                 u32 snib = 0, sany = 0, sbeh = 0;
                 const int base = static_cast<int>(lane) * 8;
-                for (int i = static_cast<int>(d.n) - 1; i >= 0; --i) {
+                for (int i = static_cast<int>(s.nd) - 1; i >= 0; --i) {
                     const u32 meta = d.meta[i];
                     const int dx = static_cast<int>(meta >> 8) - base;
                     if (dx <= -8 || dx >= 8) continue;

@@ -219,10 +219,6 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             }
             env->games.push_back(gm);
         }
-        for (auto& gm : env->games) {
-            const std::size_t smem = 1024 + (gm.chrx_smem ? 16384 : 0) + 8 * sizeof(RWarp);
-            if (smem > 48 * 1024) throw std::logic_error("render shared memory exceeds the default limit");
-        }
         ck(cudaEventCreateWithFlags(&env->ev, cudaEventDisableTiming), "event");
         ck(cudaEventCreateWithFlags(&env->ev_fork, cudaEventDisableTiming), "event");
         ck(cudaEventCreateWithFlags(&env->ev_join, cudaEventDisableTiming), "event");
