@@ -92,3 +92,52 @@ def test_level_starts_parity(oracle_path, gpu_lib_path):
         torch.cuda.synchronize()
         _compare(g2, c, 481 + t)
         _compare_levels(g2, c, 481 + t)
+
+
+@pytest.mark.gpu
+def test_parity_config3(oracle_path, gpu_lib_path):
+    """BASELINE config 3 in small: the 12 synthetic game ids (4 boards round-robin: NROM, UxROM, MMC1 with CHR-RAM,
+    MMC3 with its line-32 IRQ split), each with its own seeded reward weights, 8 envs each; 16 level-entrance slots
+    per game filled by play, every new episode starting from a saved slot (P(level start) = 1), uniform first and
+    then with seeded Dirichlet(1) weights over the saved slots (rl/rlenv.py:251-254 CDF)."""
+    counts = {f'synth{k:02d}': 8 for k in range(12)}
+    kw = dict(seed=31, sticky=True, idle_max=30, dropout=True, level_cap=16)
+    g = RlEnv(counts, device='cuda', lib_path=gpu_lib_path, **kw)
+    c = RlEnv(counts, device='cpu', lib_path=oracle_path, **kw)
+    g.start()
+    c.start()
+    gen = torch.Generator().manual_seed(31)
+    right = torch.full((c.n,), 3, dtype=torch.int16)
+    rng = np.random.default_rng(31)
+    level_starts = 0
+    for t in range(501):
+        torch.cuda.synchronize()
+        _compare(g, c, t)
+        _compare_levels(g, c, t)
+        if t and c.done.any():
+            level_starts += int((c.start_level[c.done.bool()] > 0).sum())
+        if t % 100 == 0:
+            _compare_dumps(g, c, [0, 23, 42, 61, 90, c.n - 1], t)
+            for gi in range(len(c.games)):
+                assert np.array_equal(g.level_deaths(gi), c.level_deaths(gi)), f'step {t}: slot deaths of game {gi}'
+        if t == 20:
+            for e in (g, c):
+                e.set_level_prob(1.0)
+        if t == 250:
+            for gi, game in enumerate(c.games):
+                saved = sorted(c.saved_levels()[game])
+                if not saved:
+                    continue
+                w = np.zeros(16)
+                w[saved] = rng.dirichlet(np.ones(len(saved)))
+                for e in (g, c):
+                    e.set_level_plan(gi, 1.0, w)
+        if t == 500:
+            break
+        act = random_legal(c.masks, gen)
+        act = torch.where((torch.arange(c.n) % 2 == 0) | (t < 150), right, act)   # all hold Right at first
+        c.actions.copy_(act)
+        g.actions.copy_(act.cuda())
+        c.step()
+        g.step()
+    assert level_starts > 0, 'the run should finish episodes that began at a saved level'

@@ -74,6 +74,49 @@ def test_parity_nrom_short(oracle_path, gpu_lib_path):
 
 @pytest.mark.gpu
 def test_parity_nrom_config1(oracle_path, gpu_lib_path):
-    """one synthetic NROM cart, 64 envs, sticky/dropout/idle on; restarts included."""
-    dones = run_parity({'synth00': 64}, oracle_path, gpu_lib_path, steps=400, dump_every=50)
+    """one synthetic NROM cart, 64 envs, sticky/dropout/idle on, 2,000 decisions (every output
+    every decision, machine dumps every 100); restarts included."""
+    dones = run_parity({'synth00': 64}, oracle_path, gpu_lib_path, steps=2000, dump_every=100)
+    assert dones > 0, 'the run should cover episode restarts'
+
+
+@pytest.mark.gpu
+def test_parity_config2_subset(oracle_path, gpu_lib_path):
+    """BASELINE config 2's check: the 8,192-env GPU run (pictures packed by the renderer) against the CPU oracle on a
+    256-env subset. An env's trajectory depends only on its global index, the run seed and its actions, so envs
+    0..255 of the big run equal a 256-env run. Packed pictures are compared after rl_unpack6."""
+    import ctypes
+    N, S = 8192, 256
+    kw = dict(seed=5, sticky=True, idle_max=30, dropout=True)
+    g = RlEnv({'synth00': N}, device='cuda', lib_path=gpu_lib_path, **kw)
+    c = RlEnv({'synth00': S}, device='cpu', lib_path=oracle_path, **kw)
+    packed = torch.zeros(N, 4, 224, 180, dtype=torch.uint8, device='cuda')
+    g.bind_obs_pack6(packed)
+    un = torch.zeros(S, 4, 224, 240, dtype=torch.uint8, device='cuda')
+    g.start()
+    c.start()
+    gen = torch.Generator().manual_seed(5)
+    gen_rest = torch.Generator(device='cuda').manual_seed(6)
+    stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    dones = 0
+    for t in range(151):
+        assert g.lib.rl_unpack6(ctypes.c_void_p(packed.data_ptr()), ctypes.c_void_p(un.data_ptr()), un.numel(), stream()) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(un.cpu(), c.obs), f'step {t}: pictures differ'
+        for k in ('emph', 'reward', 'done', 'masks', 'timeline', 'pads', 'events', 'parts'):
+            assert torch.equal(getattr(g, k)[:S].cpu(), getattr(c, k)), f'step {t}: {k} differs'
+        d = c.done.bool()
+        if t and d.any():
+            dones += int(d.sum())
+            assert torch.equal(g.info[:S].cpu()[d], c.info[d]), f'step {t}: info differs'
+        if t == 150:
+            break
+        act = random_legal(c.masks, gen)
+        rest = torch.randint(0, 81, (N - S,), generator=gen_rest, device='cuda', dtype=torch.int32).to(torch.int16)
+        c.actions.copy_(act)
+        g.actions.copy_(torch.cat([act.cuda(), rest]))
+        c.step()
+        g.step()
+    for e in (0, 101, 255):
+        assert np.array_equal(g.dump(e), c.dump(e)), f'env {e}: machine dump differs'
     assert dones > 0, 'the run should cover episode restarts'
