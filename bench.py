@@ -30,6 +30,10 @@ import sys
 import threading
 import time
 
+# More hardware work queues than CUDA's default 8: a multi-game env runs a main and a side stream per game
+# (set before the CUDA context exists; a user of the library sets it the same way).
+os.environ.setdefault('CUDA_DEVICE_MAX_CONNECTIONS', '32')
+
 ROOT = Path(__file__).resolve().parent
 PKG = ROOT / 'ghostrun-lab_b200'
 sys.path.insert(0, str(PKG))
@@ -47,7 +51,9 @@ def parse():
     ap.add_argument('--steps', type=int, default=100)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--envs', type=int, default=8192)
+    ap.add_argument('--envs', type=int, default=None, help='envs per GPU (default 8192; 32768 for --workload config3)')
+    ap.add_argument('--workload', default='config2', choices=['config2', 'config3'],
+                    help='config2: synthetic NROM (the headline); config3: 12 synthetic games on 4 boards with level starts')
     ap.add_argument('--seed', type=int, default=1)
     ap.add_argument('--age', type=int, default=1024,
                     help='untimed decisions before the warm-up, so that episode restarts run at their steady-state rate')
@@ -217,7 +223,14 @@ def gpu_arm(args):
     if not default_lib().exists():
         gbuild.build()
     E = args.envs
-    env = RlEnv({GAME: E}, device=dev, seed=rank_seed(args.seed, rank), sticky=True, idle_max=30, dropout=True)
+    c3 = args.workload == 'config3'
+    if c3:   # 12 game ids round-robin over the 4 boards, 16 level-start slots per game
+        games = [f'synth{k:02d}' for k in range(12)]
+        counts = {gname: E // 12 + (1 if k < E % 12 else 0) for k, gname in enumerate(games)}
+        env = RlEnv(counts, device=dev, seed=rank_seed(args.seed, rank), sticky=True, idle_max=30, dropout=True,
+                    level_cap=16)
+    else:
+        env = RlEnv({GAME: E}, device=dev, seed=rank_seed(args.seed, rank), sticky=True, idle_max=30, dropout=True)
     packed = [torch.empty(E * PACKED_ROW, dtype=torch.uint8, device=dev) for _ in range(2)]
     env.bind_obs_pack6(packed[0])
     env.start()
@@ -232,9 +245,27 @@ def gpu_arm(args):
 
     stream = torch.cuda.current_stream(dev)
     # every env starts its first episode at once; aging spreads the episode ends to the steady-state restart rate
+    right = torch.full((E,), 3, dtype=torch.int16, device=dev)
     for t in range(args.age):
-        env.actions.copy_(torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        a = torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+        if c3:   # level-entrance slots fill by play: every env holds Right first, half of them throughout
+            if t == 20:
+                env.set_level_prob(1.0)
+            a = torch.where((torch.arange(E, device=dev) % 2 == 0) | (t < args.age // 2), right, a)
+        env.actions.copy_(a)
         env.step()
+    lv_info = None
+    if c3:   # every new episode starts from a saved slot, Dirichlet(1) weights over each game's saved slots
+        import numpy as np
+        rng = np.random.default_rng(args.seed + rank)
+        saved = env.saved_levels()
+        for gi, gname in enumerate(env.games):
+            lv = sorted(saved[gname])
+            if lv:
+                w = np.zeros(16)
+                w[lv] = rng.dirichlet(np.ones(len(lv)))
+                env.set_level_plan(gi, 1.0, w)
+        lv_info = {gname: len(v) for gname, v in saved.items()}
     for t in range(W):
         env.actions.copy_(acts_dev[t]); env.step(); account()
     torch.cuda.synchronize(dev)
@@ -337,17 +368,21 @@ def gpu_arm(args):
     result = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        launches_r = max(1, tm['launches']['render'])
-        render_ms = tm['ms']['render'] / launches_r
+        # the decision's main render launches (one per game) draw the E envs' 4 frames between them
+        render_ms = tm['ms']['render'] / K
         env_frames = E * 4
-        alg_bytes = env_frames * (PACKED_ROW // 4 + 224 + 2048 + 256 + 64)   # per launch: packed out, emph, NT, OAM, log header
+        alg_bytes = env_frames * (PACKED_ROW // 4 + 224 + 2048 + 256 + 64)   # per decision: packed out, emph, NT, OAM, log header
         achieved = alg_bytes / (render_ms / 1e3) / 1e9
         tr = render_traffic_per_env_frame()
         result = dict(
             metric=METRIC, value=round(value, 1), unit=UNIT, n_gpus=world, steps=K, warmup=W,
             ms_per_step=round(ms_max / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
-            data='synthetic (seeded NROM cart synth00, random moves)',
-            config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on', envs_per_gpu=E,
+            data='synthetic (seeded NROM cart synth00, random moves)' if not c3 else
+                 'synthetic (12 seeded games synth00-11 on NROM/UxROM/MMC1/MMC3, random moves, half holding Right)',
+            config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on' if not c3 else
+                        f'config 3: 12 synthetic games on 4 boards, {E} envs/GPU, 16 level-start slots per game, '
+                        'P(level start)=1 with Dirichlet(1) weights, pack6 on',
+                        level_slots_saved=lv_info, envs_per_gpu=E,
                         frames_per_decision=4, parallelism=f'dp{world} (env shards, NCCL all-reduce of counters)',
                         aged_decisions=args.age,
                         inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)'),
@@ -358,7 +393,8 @@ def gpu_arm(args):
             roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
                           traffic=round(tr * env_frames) if tr else None, kernel='k_render',
                           peak_source=f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured' else 'fallback',
-                          algorithmic_bytes_per_launch=alg_bytes, avg_launch_ms=round(render_ms, 4)),
+                          algorithmic_bytes_per_decision=alg_bytes, render_ms_per_decision=round(render_ms, 4),
+                          render_launches_per_decision=round(tm['launches']['render'] / K, 2)),
             kernel_ms_per_step={k: round(v / K, 4) for k, v in tm['ms'].items()},
             gpu_launches=tm['total_launches'],
             clocks=clk.summary(),
@@ -372,6 +408,8 @@ def gpu_arm(args):
 
 def main():
     args = parse()
+    if args.envs is None:
+        args.envs = 32768 if args.workload == 'config3' else 8192
     if args.cpu_leg:
         cpu_leg(args)
         return

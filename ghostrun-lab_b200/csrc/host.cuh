@@ -157,13 +157,20 @@ struct Env {
     KTimer* timer = nullptr;
     bool chr_ram_any = false;
     cudaEvent_t ev = nullptr;
-    cudaStream_t side = nullptr;                  // restart work of a decision (highest priority)
-    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    // Per game: a main stream (games run concurrently, as the reference's one stream per game, rl/csrc/rlenv.cu:
+    // 173-182) and a highest-priority side stream for its restart work; events to fork from the caller's stream and
+    // join back. A one-game env runs its main work on the caller's stream itself.
+    std::vector<cudaStream_t> gmain, gside;
+    std::vector<cudaEvent_t> gfork, gmain_done, gside_done;
+    cudaEvent_t ev_begin = nullptr;
     ~Env() {
         if (ev) cudaEventDestroy(ev);
-        if (ev_fork) cudaEventDestroy(ev_fork);
-        if (ev_join) cudaEventDestroy(ev_join);
-        if (side) cudaStreamDestroy(side);
+        if (ev_begin) cudaEventDestroy(ev_begin);
+        for (auto e : gfork) cudaEventDestroy(e);
+        for (auto e : gmain_done) cudaEventDestroy(e);
+        for (auto e : gside_done) cudaEventDestroy(e);
+        for (auto q : gmain) cudaStreamDestroy(q);
+        for (auto q : gside) cudaStreamDestroy(q);
         delete timer;
     }
 };
@@ -177,13 +184,18 @@ inline void check_launch(const char* what) {
 // high-priority side stream so it overlaps the main render:
 //   s:    [list reset] k_frames -> k_finish --fork--> k_render (envs not restarting) ...... join (join_side)
 //   side:                                     k_restore -> [k_archive] -> k_frames(restart) -> k_render(restart)
-// The join comes after the last game's launch, so a game's restart work also overlaps the next game's decision.
+// Games run on their own stream pairs, concurrently (launch_all).
 // k_finish decides the episode ends and lists the restarting envs; the main render leaves them out (their outputs
 // are the new episode's first frames, drawn by the restart pass), so the two branches touch disjoint envs. The level
 // archive reads the slots only in k_finish (the pick) and k_restore (the copy), so it saves after both, as the
 // reference's k_archive after k_finish (rl/csrc/rlenv.cu:165-166).
+// Launch phases (launch_all issues each phase for every game before the next, so kernels of different games that
+// share a hardware work queue queue up behind work they would wait for anyway).
+enum : u32 { kPhFrames = 1, kPhFinish = 2, kPhRender = 4, kPhRestart = 8, kPhAll = 15 };
+
 template <u32 B>
-void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
+void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cudaStream_t side, const Range& rg,
+                 u32 phases) {
     GameArgs g = gm.g;
     const EnvArgs& A0 = env.A;
     EnvArgs A = A0;
@@ -206,21 +218,23 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     R.chrx_smem = gm.chrx_smem ? 1u : 0u;
     const std::size_t smem = render_smem(gm.chrx_smem);
     KTimer& T = *env.timer;
-    cudaStream_t side = env.side;
-    ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
-    if (!start) {
-        T.begin(kKFrames, s);
-        k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, kFramesSmem, s>>>(g, A, 0);
-        T.end(kKFrames, s);
-        check_launch("k_frames");
+    if (phases & kPhFrames) {
+        ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
+        if (!start) {
+            T.begin(kKFrames, s);
+            k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, kFramesSmem, s>>>(g, A, 0);
+            T.end(kKFrames, s);
+            check_launch("k_frames");
+        }
     }
-    T.begin(kKFinish, s);
-    k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
-    T.end(kKFinish, s);
-    check_launch("k_finish");
-    ck(cudaEventRecord(env.ev_fork, s), "fork");
-    ck(cudaStreamWaitEvent(side, env.ev_fork, 0), "fork");
-    if (!start && !A.no_render) {
+    if (phases & kPhFinish) {
+        T.begin(kKFinish, s);
+        k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
+        T.end(kKFinish, s);
+        check_launch("k_finish");
+        ck(cudaEventRecord(env.gfork[gm.index], s), "fork");
+    }
+    if ((phases & kPhRender) && !start && !A.no_render) {
         R.list = nullptr;
         R.skip = A.done;
         const u32 blocks = std::min<u32>((n + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u);
@@ -229,6 +243,8 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
         T.end(kKRender, s);
         check_launch("k_render");
     }
+    if (!(phases & kPhRestart)) return;
+    ck(cudaStreamWaitEvent(side, env.gfork[gm.index], 0), "fork");
     const u32 wb = (n + kEnvsPerWarp - 1) / kEnvsPerWarp;
     T.begin(kKFinish, side);
     k_restore<<<start ? std::min<u32>(n, 148u * 8u) : 148u, 128, 0, side>>>(g, A);
@@ -257,10 +273,10 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     }
 }
 
-// The caller's stream waits for the side stream's restart work (after the last game's launch_game).
-inline void join_side(const Env& env, cudaStream_t s) {
-    ck(cudaEventRecord(env.ev_join, env.side), "join");
-    ck(cudaStreamWaitEvent(s, env.ev_join, 0), "join");
+// The caller's stream waits for game gi's side-stream restart work.
+inline void join_side(const Env& env, int gi, cudaStream_t s) {
+    ck(cudaEventRecord(env.gside_done[gi], env.gside[gi]), "join");
+    ck(cudaStreamWaitEvent(s, env.gside_done[gi], 0), "join");
 }
 
 template <u32 B>
@@ -290,7 +306,7 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
 
 
 #define GR_BOARD_TEMPLATES(EXT, B)                                                                   \
-    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t, const Range&);      \
+    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t, cudaStream_t, const Range&, u32); \
     EXT template void boot_game<B>(Env&, Game&, const u8*, std::size_t, int, u32);
 GR_BOARD_TEMPLATES(extern, kNrom)
 GR_BOARD_TEMPLATES(extern, kUxrom)

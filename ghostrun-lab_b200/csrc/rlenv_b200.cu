@@ -29,19 +29,40 @@ std::map<int, Spec> g_specs;   // rl10 game id -> reward parameters (rl10_regist
 
 int fail(const std::exception& ex) { g_error = ex.what(); return 1; }
 
-void launch_one(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
+// The given launch phases of one game: main work on stream `s`, restart work on the game's side stream.
+void launch_phases(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg, u32 phases) {
+    cudaStream_t side = env.gside[gm.index];
     switch (gm.g.cart.board) {
-        case kNrom: launch_game<kNrom>(env, gm, start, s, rg); break;
-        case kUxrom: launch_game<kUxrom>(env, gm, start, s, rg); break;
-        case kMmc1: launch_game<kMmc1>(env, gm, start, s, rg); break;
-        default: launch_game<kMmc3>(env, gm, start, s, rg); break;
+        case kNrom: launch_game<kNrom>(env, gm, start, s, side, rg, phases); break;
+        case kUxrom: launch_game<kUxrom>(env, gm, start, s, side, rg, phases); break;
+        case kMmc1: launch_game<kMmc1>(env, gm, start, s, side, rg, phases); break;
+        default: launch_game<kMmc3>(env, gm, start, s, side, rg, phases); break;
     }
 }
 
+// One game's decision on stream `s`, its restart work joined back into `s`.
+void launch_one(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
+    launch_phases(env, gm, start, s, rg, kPhAll);
+    join_side(env, gm.index, s);
+}
+
+// Every game: a one-game env on the caller's stream; several games each on their own stream pair, concurrently,
+// issued phase by phase across the games, joined back into the caller's stream.
 void launch_all(Env& env, bool start, cudaStream_t s) {
     if (!env.A.actions || !env.A.masks) throw std::runtime_error("rlenv_bind was not called");
-    for (const Game& gm : env.games) launch_one(env, gm, start, s, Range{});
-    join_side(env, s);
+    if (env.games.size() == 1) {
+        launch_one(env, env.games[0], start, s, Range{});
+        return;
+    }
+    ck(cudaEventRecord(env.ev_begin, s), "fork");
+    for (const Game& gm : env.games) ck(cudaStreamWaitEvent(env.gmain[gm.index], env.ev_begin, 0), "fork");
+    for (u32 ph : {kPhFrames, kPhFinish, kPhRestart, kPhRender})
+        for (const Game& gm : env.games) launch_phases(env, gm, start, env.gmain[gm.index], Range{}, ph);
+    for (const Game& gm : env.games) {
+        ck(cudaEventRecord(env.gmain_done[gm.index], env.gmain[gm.index]), "join");
+        ck(cudaStreamWaitEvent(s, env.gmain_done[gm.index], 0), "join");
+        join_side(env, gm.index, s);
+    }
 }
 
 // 4 colour numbers (6 bits) -> 3 bytes, little-endian 24-bit groups (rl/csrc/rlenv.cu:126-134 layout); 16 pixels per
@@ -220,11 +241,23 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             env->games.push_back(gm);
         }
         ck(cudaEventCreateWithFlags(&env->ev, cudaEventDisableTiming), "event");
-        ck(cudaEventCreateWithFlags(&env->ev_fork, cudaEventDisableTiming), "event");
-        ck(cudaEventCreateWithFlags(&env->ev_join, cudaEventDisableTiming), "event");
+        ck(cudaEventCreateWithFlags(&env->ev_begin, cudaEventDisableTiming), "event");
         int least = 0, greatest = 0;
         ck(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
-        ck(cudaStreamCreateWithPriority(&env->side, cudaStreamNonBlocking, greatest), "side stream");
+        for (std::size_t gi = 0; gi < env->games.size(); ++gi) {
+            cudaStream_t q = nullptr;
+            cudaEvent_t e = nullptr;
+            ck(cudaStreamCreateWithPriority(&q, cudaStreamNonBlocking, least), "game stream");
+            env->gmain.push_back(q);
+            ck(cudaStreamCreateWithPriority(&q, cudaStreamNonBlocking, greatest), "side stream");
+            env->gside.push_back(q);
+            ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+            env->gfork.push_back(e);
+            ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+            env->gmain_done.push_back(e);
+            ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+            env->gside_done.push_back(e);
+        }
         env->timer = new KTimer();
         ck(cudaDeviceSynchronize(), "create");
         return env;
@@ -432,7 +465,6 @@ int rlenv_step_game(void* h, int gi, std::uint8_t* obs, std::uint8_t* emph, void
         Range rg;
         rg.obs = obs; rg.emph = emph;
         launch_one(env, env.games[gi], false, s, rg);
-        join_side(env, s);
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }
@@ -446,7 +478,6 @@ int rlenv_step_range(void* h, int gi, int start, int count, std::uint8_t* obs, s
         Range rg;
         rg.start = start; rg.count = count; rg.obs = obs; rg.emph = emph;
         launch_one(env, gm, false, s, rg);
-        join_side(env, s);
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }
