@@ -177,6 +177,7 @@ struct Emu {
     u32 dma;
     u32 slot;     // presentation slot of the frame being emulated
     u32 prg_bank; // UxROM
+    u32 froze;    // the vblank froze slot `slot` during this step_until (its snapshot copy is still to be made)
 
     __device__ Emu(const StateView& s, const CartView& c, u32 env, u32 ln, EmuShared& shm, const u32* dt)
         : S(s), C(c), e(env), lane(ln), sh(shm), dtab(dt) {}
@@ -423,13 +424,37 @@ struct Emu {
         const u32 nb = (shown + 1u) & kLcBank;
         log_ctl = (log_ctl & ~kLcBank) | nb;
         const u64 sl = static_cast<u64>(e) * 4 + slot;
-        copy16(S.snap_nt + sl * kNtBytes, nt(), kNtBytes);
-        uint4* so = reinterpret_cast<uint4*>(S.snap_oam + sl * kOamBytes);
-        for (u32 i = 0; i < 16; ++i)
-            so[i] = make_uint4(sh.oam[4 * i][lane], sh.oam[4 * i + 1][lane], sh.oam[4 * i + 2][lane], sh.oam[4 * i + 3][lane]);
-        if (S.snap_chr && !C.chr) copy16(S.snap_chr + sl * kChrRamBytes, chr_ram(), kChrRamBytes);
+        froze = 1;    // the vblank ends the frame's step_until: snapshot_frozen copies the memories after it
         S.slot_bank[sl] = static_cast<u8>(nb);
         ww(R_FSLOT, slot);
+    }
+
+    // After step_until (all 32 lanes): the nametable RAM, OAM (and CHR-RAM) of every lane that froze a frame into
+    // presentation slot `slot`, copied by the whole warp. Nothing runs between the vblank and the end of the frame's
+    // step_until (the frame's target is the vblank dot), so the memories are still as frozen.
+    __device__ __forceinline__ void snapshot_frozen() {
+        u32 pend = __ballot_sync(0xFFFFFFFFu, froze != 0);
+        while (pend) {
+            const u32 L = __ffs(pend) - 1;
+            pend &= pend - 1;
+            const u32 eL = __shfl_sync(0xFFFFFFFFu, e, L);
+            const u32 sL = __shfl_sync(0xFFFFFFFFu, slot, L);
+            const u64 sl = static_cast<u64>(eL) * 4 + sL;
+            const uint4* ntv = reinterpret_cast<const uint4*>(S.nt + static_cast<u64>(eL) * kNtBytes);
+            uint4* dnt = reinterpret_cast<uint4*>(S.snap_nt + sl * kNtBytes);
+            const uint4 q0 = ntv[lane], q1 = ntv[lane + 32], q2 = ntv[lane + 64], q3 = ntv[lane + 96];
+            u32* doam = reinterpret_cast<u32*>(S.snap_oam + sl * kOamBytes);
+            const u32 o0 = sh.oam[lane][L], o1 = sh.oam[lane + 32][L];
+            dnt[lane] = q0; dnt[lane + 32] = q1; dnt[lane + 64] = q2; dnt[lane + 96] = q3;
+            doam[lane] = o0; doam[lane + 32] = o1;
+            if (S.snap_chr && !C.chr) {
+                const uint4* cv = reinterpret_cast<const uint4*>(S.chr_ram + static_cast<u64>(eL) * kChrRamBytes);
+                uint4* dc = reinterpret_cast<uint4*>(S.snap_chr + sl * kChrRamBytes);
+#pragma unroll 4
+                for (u32 i = lane; i < kChrRamBytes / 16; i += 32) dc[i] = cv[i];
+            }
+        }
+        froze = 0;
     }
 
     __device__ __forceinline__ Hit0 sprite0_eval() const;
@@ -875,14 +900,16 @@ struct Emu {
         // operand value for the reading operations
         const bool reads = (opn >= O_LDA && opn <= O_LDY) || (opn >= O_ADC && opn <= O_DEC);
         if (reads) val = mode == M_IMM ? b1 : mode == M_ACC ? a : rd(ea);
+        bool store = false;   // one store site for STA / STX / STY and read-modify-write results
+        u32 wv = 0;
         // ---- operation
         switch (opn) {
             case O_LDA: a = val; nz(a); break;
             case O_LDX: x = val; nz(x); break;
             case O_LDY: y = val; nz(y); break;
-            case O_STA: wr(ea, a); break;
-            case O_STX: wr(ea, x); break;
-            case O_STY: wr(ea, y); break;
+            case O_STA: store = true; wv = a; break;
+            case O_STX: store = true; wv = x; break;
+            case O_STY: store = true; wv = y; break;
             case O_SBC: val ^= 0xFFu; [[fallthrough]];
             case O_ADC: {
                 const u32 s = a + val + (p & FC);
@@ -913,7 +940,7 @@ struct Emu {
                     default: r = (val - 1) & 0xFFu; break;
                 }
                 nz(r);
-                if (mode == M_ACC) a = r; else wr(ea, r);
+                if (mode == M_ACC) a = r; else { store = true; wv = r; }
                 break;
             }
             case O_INX: x = (x + 1) & 0xFFu; nz(x); break;
@@ -977,6 +1004,7 @@ struct Emu {
                 break;
             }
         }
+        if (store) wr(ea, wv);
         cycles += cyc;
         return Step{cyc, op, pc0, false};
     }

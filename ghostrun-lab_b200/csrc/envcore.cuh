@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
             valid = ge >= g.e0 && ge < g.e0 + g.n;
         }
         Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab);
+        m.froze = 0;
         if (valid) { m.stage_in(); m.load(); }
         u32 fault = valid ? A.fault[ge] : 0u;
         u64 target = valid ? A.target[ge] : 0ull;
@@ -486,6 +487,7 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
                 m.slot = i < extra ? 0u : static_cast<u32>(i - extra);
             }
             const u32 fl = m.step_until(target, mine && fault == 0);
+            m.snapshot_frozen();
             if (mine) {
                 if (fl) fault = fl;
                 m.finish_slot();
@@ -704,6 +706,7 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
     }
     __syncwarp();
     Emu<BOARD> m(S, g.cart, e, lane, sh, dtab);
+    m.froze = 0;
     if (me) {
         m.stage_in();
         // paged boards keep a run-time page map (the others mirror by the header and have none); power-on registers
@@ -733,6 +736,7 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
     for (u32 k = 0; k < boot_n + idle_n; ++k) {
         if (me) { m.pad = k < boot_n ? boot_pads[k] : 0u; m.slot = k & 3u; }
         const u32 f = m.step_until(target, me);
+        m.snapshot_frozen();
         if (me) {
             m.finish_slot();
             target += kFrameDots;
