@@ -166,6 +166,7 @@ struct Emu {
     const u32 lane;       // column in the shared staging
     EmuShared& sh;
     const u32* __restrict__ dtab;   // decode table (shared memory)
+    const u8* __restrict__ prg_s;   // the cart's staged PRG window (shared memory)
     // hot state (registers for the whole frame loop)
     u32 pc, a, x, y, sp, p, pad;
     u64 cycles;
@@ -179,8 +180,8 @@ struct Emu {
     u32 prg_bank; // UxROM
     u32 froze;    // the vblank froze slot `slot` during this step_until (its snapshot copy is still to be made)
 
-    __device__ Emu(const StateView& s, const CartView& c, u32 env, u32 ln, EmuShared& shm, const u32* dt)
-        : S(s), C(c), e(env), lane(ln), sh(shm), dtab(dt) {}
+    __device__ Emu(const StateView& s, const CartView& c, u32 env, u32 ln, EmuShared& shm, const u32* dt, const u8* ps)
+        : S(s), C(c), e(env), lane(ln), sh(shm), dtab(dt), prg_s(ps) {}
 
     // -------- staging: global env-minor / env-major arrays <-> this lane's shared column
     __device__ __forceinline__ void stage_in() const {
@@ -268,15 +269,19 @@ struct Emu {
     __device__ __forceinline__ void set_mreg(u32 i, u32 v) const { set_field(R_MREG + (i >> 2), (i & 3) * 8, 0xFF, v); }
     __device__ __forceinline__ u32 mirroring() const { return rw(R_PPU2) >> 24; }
 
+    __device__ __forceinline__ u32 prg_byte(u32 off) const {   // PRG byte at physical offset off
+        const u32 k = off - C.prg_stage_base;
+        return k < C.prg_stage_bytes ? static_cast<u32>(prg_s[k]) : static_cast<u32>(__ldg(C.prg + off));
+    }
     __device__ __forceinline__ u32 prg_rd(u32 addr) const {
         if constexpr (BOARD == kNrom) {
-            return __ldg(C.prg + ((addr - 0x8000u) & C.prg_mask));
+            return prg_s[(addr - 0x8000u) & C.prg_mask];   // the whole PRG is staged
         } else if constexpr (BOARD == kUxrom) {
             const u32 off = addr < 0xC000u ? (((prg_bank & C.bank_mask) << 14) | (addr & 0x3FFFu))
                                            : (C.fixed_base + (addr & 0x3FFFu));
-            return __ldg(C.prg + off);
+            return prg_byte(off);
         } else {
-            return __ldg(C.prg + rw(R_PRGPG + ((addr >> 13) & 3u)) + (addr & 0x1FFFu));
+            return prg_byte(rw(R_PRGPG + ((addr >> 13) & 3u)) + (addr & 0x1FFFu));
         }
     }
 

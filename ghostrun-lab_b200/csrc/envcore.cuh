@@ -426,15 +426,25 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
 
 // Emulation, one warp = kEnvsPerWarp envs per block, consoles staged in shared memory for the whole launch.
 // `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for the listed envs.
-constexpr std::size_t kFramesSmem = sizeof(EmuShared) + 256 * sizeof(u32);
+constexpr std::size_t kFramesSmem = sizeof(EmuShared) + 256 * sizeof(u32);   // + the cart's staged PRG window
+inline std::size_t frames_smem(const CartView& c) { return kFramesSmem + c.prg_stage_bytes; }
+
+// The cart's PRG window into shared memory (whole warp, 16-byte vectors).
+__device__ __forceinline__ void stage_prg(const CartView& c, u8* dst, u32 lane) {
+    const uint4* src = reinterpret_cast<const uint4*>(c.prg + c.prg_stage_base);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (u32 i = lane; i < c.prg_stage_bytes / 16; i += 32) d[i] = __ldg(src + i);
+}
 
 template <u32 BOARD>
 __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
     extern __shared__ __align__(16) u8 smem_raw[];
     EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
     u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    u8* prg_s = smem_raw + kFramesSmem;
     const u32 lane = threadIdx.x;
     for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
+    stage_prg(g.cart, prg_s, lane);
     __syncwarp();
     const u32 total = restart ? *A.list_count : g.n;
     for (u32 base = blockIdx.x * kEnvsPerWarp; base < total; base += gridDim.x * kEnvsPerWarp) {
@@ -445,7 +455,7 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
             ge = restart ? A.list[k] : g.e0 + k;
             valid = ge >= g.e0 && ge < g.e0 + g.n;
         }
-        Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab);
+        Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab, prg_s);
         m.froze = 0;
         if (valid) { m.stage_in(); m.load(); }
         u32 fault = valid ? A.fault[ge] : 0u;
@@ -688,8 +698,11 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
     extern __shared__ __align__(16) u8 smem_raw[];
     EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
     u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    u8* prg_s = smem_raw + kFramesSmem;
     const u32 lane = threadIdx.x;
     for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
+    stage_prg(g.cart, prg_s, lane);
+    __syncwarp();
     const bool me = lane == 0;
     if (me) {
         for (int w = 0; w < kRegWords; ++w) S.regs[static_cast<u64>(w) * S.Np + e] = 0;
@@ -705,7 +718,7 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
         S.slot_bank[static_cast<u64>(e) * 4] = 0;
     }
     __syncwarp();
-    Emu<BOARD> m(S, g.cart, e, lane, sh, dtab);
+    Emu<BOARD> m(S, g.cart, e, lane, sh, dtab, prg_s);
     m.froze = 0;
     if (me) {
         m.stage_in();

@@ -222,7 +222,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
         ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
         if (!start) {
             T.begin(kKFrames, s);
-            k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, kFramesSmem, s>>>(g, A, 0);
+            k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, frames_smem(g.cart), s>>>(g, A, 0);
             T.end(kKFrames, s);
             check_launch("k_frames");
         }
@@ -258,7 +258,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
     }
     const u32 rb = start ? wb : std::min<u32>(wb, 148u * (32u / kEnvsPerWarp));
     T.begin(kKRestart, side);
-    k_frames<B><<<rb, 32, kFramesSmem, side>>>(g, A, 1);
+    k_frames<B><<<rb, 32, frames_smem(g.cart), side>>>(g, A, 1);
     T.end(kKRestart, side);
     check_launch("k_frames restart");
     if (!A.no_render) {
@@ -286,11 +286,13 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
     u32* fault = env.mem.allocn<u32>(4);
     const u32 idle = idle_max > 0 ? static_cast<u32>(idle_max) : 0u;
     u8* recs = env.mem.allocn<u8>(static_cast<std::size_t>(idle + 1) * kRecBytes);
-    ck(cudaFuncSetAttribute(k_frames<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
-    ck(cudaFuncSetAttribute(k_boot<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem)), "smem attr");
+    ck(cudaFuncSetAttribute(k_frames<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
+       "smem attr");
+    ck(cudaFuncSetAttribute(k_boot<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
+       "smem attr");
     ck(cudaFuncSetAttribute(k_render<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(render_smem(gm.chrx_smem))),
        "smem attr");
-    k_boot<B><<<1, 32, kFramesSmem>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
+    k_boot<B><<<1, 32, frames_smem(gm.g.cart)>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);
     check_launch("k_boot");
     u32 hf[4] = {0, 0, 0, 0};
     ck(cudaMemcpy(hf, fault, 16, cudaMemcpyDeviceToHost), "boot");

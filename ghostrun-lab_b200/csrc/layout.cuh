@@ -116,7 +116,11 @@ struct CartView {
     u32 chr_tiles;
     u32 board, arrangement;
     u32 bank_mask, fixed_base, prg_page_mask, chr_page_mask;
+    // PRG window staged in each emulation block's shared memory: bytes [prg_stage_base, + prg_stage_bytes) of prg
+    // (the whole PRG on NROM, the last 16 KB - the fixed bank the reset / NMI code runs from - on the paged boards)
+    u32 prg_stage_base, prg_stage_bytes;
 };
+constexpr u32 kPrgStageMax = 32768;
 
 struct StateView {
     u32 Np;

@@ -220,6 +220,9 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
                 C.chrx = nullptr;
             }
             C.board = hc.board;
+            // PRG staged in the emulation blocks' shared memory: all of it on NROM (16 / 32 KB), else the last 16 KB
+            C.prg_stage_bytes = hc.board == kNrom ? static_cast<u32>(hc.prg.size()) : std::min<u32>(16384u, static_cast<u32>(hc.prg.size()));
+            C.prg_stage_base = static_cast<u32>(hc.prg.size()) - C.prg_stage_bytes;
             C.arrangement = hc.arrangement;
             C.bank_mask = hc.bank_mask;
             C.fixed_base = hc.fixed_base;
