@@ -52,8 +52,9 @@ def parse():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--envs', type=int, default=None, help='envs per GPU (default 8192; 32768 for --workload config3)')
-    ap.add_argument('--workload', default='config2', choices=['config2', 'config3'],
-                    help='config2: synthetic NROM (the headline); config3: 12 synthetic games on 4 boards with level starts')
+    ap.add_argument('--workload', default='config2', choices=['config2', 'config3', 'stem'],
+                    help='config2: synthetic NROM (the headline); config3: 12 synthetic games on 4 boards with level '
+                         'starts; stem: the policy input stem (colour lookup + 2x2 conv, tcgen05) on packed pictures')
     ap.add_argument('--seed', type=int, default=1)
     ap.add_argument('--age', type=int, default=1024,
                     help='untimed decisions before the warm-up, so that episode restarts run at their steady-state rate')
@@ -202,6 +203,64 @@ def render_traffic_per_env_frame():
         if m:
             return float(m.group(1))
     return None
+
+
+def stem_arm(args):
+    """The policy's input stem (rl_stem_fwd, tcgen05) on B = --envs samples of 6-bit packed pictures: samples/s.
+    Roofline: HBM bytes (packed pictures + emphasis in, bf16 features out) per call / its CUDA-event time."""
+    import torch
+    from stem import fused_stem
+    B, K, W = args.envs, args.steps, args.warmup
+    dev = torch.device('cuda', 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    obs6 = torch.randint(0, 256, (B, 4, 224, 180), generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+    emph = torch.randint(0, 8, (B, 4, 224), generator=g, device=dev, dtype=torch.int32).to(torch.uint8)
+    pal = torch.rand(512, 3, generator=g, device=dev)
+    w = torch.randn(16, 12, 2, 2, generator=g, device=dev) * 0.2
+    b = torch.randn(16, generator=g, device=dev) * 0.1
+    for _ in range(W):
+        fused_stem(obs6, emph, pal, w, b, packed=True, check=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(0)
+    with clk:
+        e0.record()
+        for _ in range(K):
+            out = fused_stem(obs6, emph, pal, w, b, packed=True, check=False)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    in_bytes = obs6.numel() + emph.numel()
+    out_bytes = out.numel() * 2
+    peak, kind = measured_peaks()
+    achieved = (in_bytes + out_bytes) / (ms / 1e3) / 1e9
+    # e2e: the learner's view - the packed rollout slice from pinned host memory, the stem, a per-channel mean back
+    host6 = obs6.cpu().pin_memory()
+    hoste = emph.cpu().pin_memory()
+    d6, de = torch.empty_like(obs6), torch.empty_like(emph)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(K):
+        d6.copy_(host6, non_blocking=True)
+        de.copy_(hoste, non_blocking=True)
+        o = fused_stem(d6, de, pal, w, b, packed=True, check=False)
+        m = o.float().mean(dim=(0, 2, 3)).cpu()
+    f1.record()
+    torch.cuda.synchronize()
+    ems = f0.elapsed_time(f1) / K
+    return dict(metric='stem samples/s (4-frame pictures -> 16x112x120 bf16 features)', value=round(B / (ms / 1e3), 1),
+                unit='samples/s', n_gpus=1, steps=K, warmup=W, ms_per_step=round(ms, 4), higher_is_better=True,
+                scaling='weak', vs_baseline=None, dtype='bf16', data='synthetic (random packed pictures, palette, weights)',
+                config=dict(workload=f'policy input stem, {B} samples of 6-bit packed pictures', batch=B,
+                            inputs_exceed_l2=True),
+                e2e=dict(value=round(B / (ems / 1e3), 1), unit='samples/s', h2d_bytes_per_step=in_bytes,
+                         d2h_bytes_per_step=16 * 4),
+                roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
+                              traffic=None, kernel='k_stem_fwd<packed>', bytes_per_call=in_bytes + out_bytes,
+                              peak_source=f'{kind} (MEASURED_PEAKS.json hbm_gbs)' if kind == 'measured' else 'fallback'),
+                gpu_launches=K, clocks=clk.summary(), cpu_baseline=None,
+                checksum=[round(float(x), 5) for x in m[:4]])
 
 
 def gpu_arm(args):
@@ -433,6 +492,9 @@ def main():
                                       sample=sample, cpu=cpu_model()),
                     e2e=dict(value=round(r['value'], 1), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
         print(json.dumps(line), flush=True)
+        return
+    if args.workload == 'stem':
+        print(json.dumps(stem_arm(args)), flush=True)
         return
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

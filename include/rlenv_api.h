@@ -117,6 +117,19 @@ int rlenv_env_scalars(void* h, int ge, uint64_t* host_out, void* stream);
 #define RLENV_DUMP_NOALLOC_MAX_ENVS 8
 int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, uint8_t* host_out, void* stream);
 
+// ---------------------------------------------------------------- policy input stem (rl/fused.py:163-169)
+
+// Fused colour lookup + 2x2 stride-2 stem convolution of the policy (the reference's Triton fused_stem forward,
+// rl/fused.py:36-96 and 163-169; no counterpart in the reference C-ABI): obs [B,4,224,240] colour numbers
+// (packed = 0) or [B,4,224,180] 6-bit packed pictures (packed = 1, the rl_pack6 layout); emph [B,4,224]; pal4
+// [512][4] bf16 = R, G, B, 0 of palette index colour | emphasis << 6; weight [16][48] bf16 (conv weight [16,12,2,2]
+// flattened, k = (frame * 3 + RGB) * 4 + dy * 2 + dx); bias [16] bf16; out [B,112,120,16] bf16 channels-last.
+// bf16 products, fp32 sums on the tensor cores (tcgen05). err: device int set to 1 if a tile's MMA did not complete.
+// Device pointers, asynchronous on `stream`; returns non-zero on a launch error (message: rl_stem_error).
+int rl_stem_fwd(const void* obs, const void* emph, const void* pal4, const void* weight, const void* bias, void* out,
+                long long batch, int packed, int* err, void* stream);
+const char* rl_stem_error(void);
+
 // Per-kernel device time (CUDA events on the launching stream) and launch counts, for benchmarks.
 void rlenv_set_timing(void* h, int on);
 int rlenv_timing(void* h, double* out13, int reset);
