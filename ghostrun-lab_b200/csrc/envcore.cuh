@@ -249,6 +249,13 @@ struct GameArgs {   // one game slice
     i32* lv_deaths;
     unsigned long long* lv_claim;
     const u32* lv_cdf;         // [lv_cap] level pick CDF (lv_weighted)
+    // Idle-frame chains of the saved slots: the state after k = 1..lv_idle_n idle frames (pad 0) from slot s, a pure
+    // function of the slot (as the boot snapshot's idle records), made by k_chain when a slot's contents change.
+    u32 lv_idle_n;             // idle_max
+    u8* lv_idle_rec;           // [lv_cap][lv_idle_n][kRecBytes]
+    u32* lv_idle_fault;        // [lv_cap][lv_idle_n] fault code after those frames
+    u32* lv_chain_ok;          // [lv_cap] 1: the chain matches the slot
+    StateView lv_scratch;      // emulation space of k_chain, env index = slot
 };
 
 struct EnvArgs {
@@ -277,6 +284,7 @@ struct EnvArgs {
     float* parts;
     u8* packed;     // optional [N, 4, 224, 180] packed 6-bit pictures (replaces obs when set)
     i32* ep_start;      // [N] slot the episode started from, -1 = power-on; nullptr = level starts off
+    u8* lv_chained;     // [N] 1: k_restore copied the level start's state after its idle frames (none left to run)
     i32* start_out;     // optional [N]: ep_start of the episode that just ended (where done)
     i32* level_out;     // optional [N]: level after the decision's update, -1 = not known yet
     float* progress_out;   // optional [N]: within-level progress / progress_unit, NaN = not valid now
@@ -315,11 +323,20 @@ static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, 
 
 // The snapshot record an episode restarts from: a saved level start, the boot snapshot after k idle frames, or the
 // boot snapshot (rl/csrc/rlenv_core.cuh:236-243).
-__device__ __forceinline__ const u8* restart_record(const GameArgs& g, const EnvArgs& A, u32 ge) {
+// A level start with idle frames takes its slot's idle chain record when the chain is made (`chained`).
+__device__ __forceinline__ const u8* restart_record(const GameArgs& g, const EnvArgs& A, u32 ge, bool& chained) {
     const int lv = A.ep_start ? A.ep_start[ge] : -1;
     const int idle = A.ep_idle[ge];
-    const int k = lv < 0 && idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
-    return lv >= 0 ? g.lv_rec + static_cast<u64>(lv) * kRecBytes : g.recs + static_cast<u64>(k) * kRecBytes;
+    chained = false;
+    if (lv >= 0) {
+        if (idle > 0 && g.lv_idle_rec && static_cast<u32>(idle) <= g.lv_idle_n && g.lv_chain_ok[lv]) {
+            chained = true;
+            return g.lv_idle_rec + (static_cast<u64>(lv) * g.lv_idle_n + static_cast<u64>(idle - 1)) * kRecBytes;
+        }
+        return g.lv_rec + static_cast<u64>(lv) * kRecBytes;
+    }
+    const int k = idle <= static_cast<int>(g.idle_tmpl) ? idle : 0;
+    return g.recs + static_cast<u64>(k) * kRecBytes;
 }
 
 // record <- env slot; threads tid of nt share the copy (one thread: 0 of 1)
@@ -474,8 +491,10 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
                 act = A.actions[ge];
             } else {
                 const int idle = A.ep_idle[ge];
-                const bool lv = A.ep_start && A.ep_start[ge] >= 0;   // a level start emulates every idle frame
-                extra = !lv && idle <= static_cast<int>(g.idle_tmpl) ? 0 : idle;
+                // a level start emulates every idle frame unless its slot's chain supplied them
+                const bool lv = A.ep_start && A.ep_start[ge] >= 0;
+                const bool chained = lv && A.lv_chained && A.lv_chained[ge];
+                extra = lv ? (chained ? 0 : idle) : (idle <= static_cast<int>(g.idle_tmpl) ? 0 : idle);
             }
         }
         const int nfr = extra + kFramesPerDecision;
@@ -600,7 +619,18 @@ static __global__ void __launch_bounds__(128) k_restore(const __grid_constant__ 
     const u32 total = *A.list_count;
     for (u32 k = blockIdx.x; k < total; k += gridDim.x) {
         const u32 ge = A.list[k];
-        scatter_record(A.st, ge, restart_record(g, A, ge), g.cart.chr == nullptr, threadIdx.x, blockDim.x);
+        bool chained;
+        const u8* rec = restart_record(g, A, ge, chained);
+        scatter_record(A.st, ge, rec, g.cart.chr == nullptr, threadIdx.x, blockDim.x);
+        if (threadIdx.x == 0 && A.lv_chained) {
+            A.lv_chained[ge] = chained ? 1 : 0;
+            if (chained) {   // the idle frames are in the record: the episode's clock and fault move on with them
+                const int lv = A.ep_start[ge], idle = A.ep_idle[ge];
+                A.target[ge] += static_cast<u64>(idle) * kFrameDots;
+                A.ep_frame[ge] += static_cast<u32>(idle);
+                A.fault[ge] = g.lv_idle_fault[static_cast<u64>(lv) * g.lv_idle_n + static_cast<u64>(idle - 1)];
+            }
+        }
     }
 }
 
@@ -621,6 +651,7 @@ static __global__ void __launch_bounds__(128) k_archive(const __grid_constant__ 
             g.lv_target[s] = A.target[ge];
             g.lv_frame[s] = A.ep_frame[ge];
             g.lv_deaths[s] = static_cast<i32>(cl >> 32);
+            if (g.lv_chain_ok) g.lv_chain_ok[s] = 0;   // new contents: the next decision's k_chain remakes the chain
         }
         g.lv_claim[s] = ~0ull;
     }
@@ -642,6 +673,7 @@ static __global__ void __launch_bounds__(128) k_place_save(const __grid_constant
         g.lv_target[s] = A.target[ge];
         g.lv_frame[s] = A.ep_frame[ge];
         g.lv_deaths[s] = 0;
+        if (g.lv_chain_ok) g.lv_chain_ok[s] = 0;
     }
 }
 
@@ -684,6 +716,52 @@ __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_co
             else rd.draw_fast(ge, f, RW.fw[f], out, eo, R.packed != nullptr);
             __syncwarp();
         }
+    }
+}
+
+// Idle-frame chains of the saved slots whose contents changed (block s = slot s, lane 0 emulates in the scratch
+// space): the state after each of idle_max idle frames (pad 0, the reference's ph_reset_idle frames,
+// rl/csrc/rlenv_core.cuh:311-317) from the slot, with the fault code so far. Runs before k_restore; a restart whose
+// slot has its chain copies the record after its idle count instead of emulating the frames.
+template <u32 BOARD>
+__global__ void __launch_bounds__(32, 1) k_chain(const __grid_constant__ GameArgs g) {
+    const u32 s = blockIdx.x;
+    if (g.lv_chain_ok[s] || g.lv_deaths[s] < 0 || g.lv_idle_n == 0) return;   // same for the whole block
+    extern __shared__ __align__(16) u8 smem_raw[];
+    EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    u8* prg_s = smem_raw + kFramesSmem;
+    const u32 lane = threadIdx.x;
+    for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
+    stage_prg(g.cart, prg_s, lane);
+    const StateView& S = g.lv_scratch;
+    scatter_record(S, s, g.lv_rec + static_cast<u64>(s) * kRecBytes, g.cart.chr == nullptr, lane, 32);
+    __syncwarp();
+    const bool me = lane == 0;
+    Emu<BOARD> m(S, g.cart, s, lane, sh, dtab, prg_s);
+    m.froze = 0;
+    if (me) { m.stage_in(); m.load(); }
+    u64 target = g.lv_target[s];
+    u32 fault = 0;
+    for (u32 k = 0; k < g.lv_idle_n; ++k) {
+        if (me) { m.pad = 0; m.slot = 0; }
+        const u32 f = m.step_until(target, me && fault == 0);
+        m.snapshot_frozen();
+        if (me) {
+            m.finish_slot();
+            if (f && !fault) fault = f;
+            target += kFrameDots;
+            m.store();
+            m.stage_out();
+        }
+        __syncwarp();
+        gather_record(S, s, g.lv_idle_rec + (static_cast<u64>(s) * g.lv_idle_n + k) * kRecBytes, g.cart.chr == nullptr, lane, 32);
+        if (me) g.lv_idle_fault[static_cast<u64>(s) * g.lv_idle_n + k] = fault;
+        __syncwarp();
+    }
+    if (me) {
+        __threadfence();
+        g.lv_chain_ok[s] = 1;
     }
 }
 

@@ -34,6 +34,25 @@ struct DevMem {
     ~DevMem() { for (void* p : blocks) cudaFree(p); }
 };
 
+// Device arrays of a StateView for Np env slots (env-minor words, env-major bytes, 4 presentation slots each).
+inline StateView alloc_state_view(DevMem& M, u32 Np, bool chr_ram, bool saved) {
+    StateView S{};
+    S.Np = Np;
+    S.regs = M.allocn<u32>(static_cast<std::size_t>(kRegWords) * Np, saved);
+    S.ram = M.allocn<u32>(static_cast<std::size_t>(kRamWords) * Np, saved);
+    S.prg_ram = M.allocn<u32>(static_cast<std::size_t>(kPrgRamWords) * Np, saved);
+    S.oam = M.allocn<u8>(static_cast<std::size_t>(kOamBytes) * Np, saved);
+    S.nt = M.allocn<u8>(static_cast<std::size_t>(kNtBytes) * Np, saved);
+    S.pal = M.allocn<u8>(static_cast<std::size_t>(kPalBytes) * Np, saved);
+    S.chr_ram = chr_ram ? M.allocn<u8>(static_cast<std::size_t>(kChrRamBytes) * Np, saved) : nullptr;
+    S.log = M.allocn<u32>(static_cast<std::size_t>(kLogBanks) * kLogBankWords * Np, saved);
+    S.snap_nt = M.allocn<u8>(static_cast<std::size_t>(4) * kNtBytes * Np, saved);
+    S.snap_oam = M.allocn<u8>(static_cast<std::size_t>(4) * kOamBytes * Np, saved);
+    S.snap_chr = chr_ram ? M.allocn<u8>(static_cast<std::size_t>(4) * kChrRamBytes * Np, saved) : nullptr;
+    S.slot_bank = M.allocn<u8>(static_cast<std::size_t>(4) * Np, saved);
+    return S;
+}
+
 // iNES 1.0 header -> board description (the product's own parser; rl/csrc/rlenv_build.hpp:36-84 uses NeSLE's).
 struct HostCart {
     std::vector<u8> prg, chr;
@@ -246,6 +265,12 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
     if (!(phases & kPhRestart)) return;
     ck(cudaStreamWaitEvent(side, env.gfork[gm.index], 0), "fork");
     const u32 wb = (n + kEnvsPerWarp - 1) / kEnvsPerWarp;
+    if (g.lv_cap > 0 && g.lv_idle_n > 0) {   // idle chains of the slots that changed, before the restores use them
+        T.begin(kKFinish, side);
+        k_chain<B><<<g.lv_cap, 32, frames_smem(g.cart), side>>>(g);
+        T.end(kKFinish, side);
+        check_launch("k_chain");
+    }
     T.begin(kKFinish, side);
     k_restore<<<start ? std::min<u32>(n, 148u * 8u) : 148u, 128, 0, side>>>(g, A);
     T.end(kKFinish, side);
@@ -289,6 +314,8 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
     ck(cudaFuncSetAttribute(k_frames<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
        "smem attr");
     ck(cudaFuncSetAttribute(k_boot<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
+       "smem attr");
+    ck(cudaFuncSetAttribute(k_chain<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
        "smem attr");
     ck(cudaFuncSetAttribute(k_render<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(render_smem(gm.chrx_smem))),
        "smem attr");

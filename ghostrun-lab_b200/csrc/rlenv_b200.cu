@@ -141,20 +141,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             if (carts.back().chr.empty()) env->chr_ram_any = true;
         }
         DevMem& M = env->mem;
-        StateView& S = env->A.st;
-        S.Np = Np;
-        S.regs = M.allocn<u32>(static_cast<std::size_t>(kRegWords) * Np, true);
-        S.ram = M.allocn<u32>(static_cast<std::size_t>(kRamWords) * Np, true);
-        S.prg_ram = M.allocn<u32>(static_cast<std::size_t>(kPrgRamWords) * Np, true);
-        S.oam = M.allocn<u8>(static_cast<std::size_t>(kOamBytes) * Np, true);
-        S.nt = M.allocn<u8>(static_cast<std::size_t>(kNtBytes) * Np, true);
-        S.pal = M.allocn<u8>(static_cast<std::size_t>(kPalBytes) * Np, true);
-        S.chr_ram = env->chr_ram_any ? M.allocn<u8>(static_cast<std::size_t>(kChrRamBytes) * Np, true) : nullptr;
-        S.log = M.allocn<u32>(static_cast<std::size_t>(kLogBanks) * kLogBankWords * Np, true);
-        S.snap_nt = M.allocn<u8>(static_cast<std::size_t>(4) * kNtBytes * Np, true);
-        S.snap_oam = M.allocn<u8>(static_cast<std::size_t>(4) * kOamBytes * Np, true);
-        S.snap_chr = env->chr_ram_any ? M.allocn<u8>(static_cast<std::size_t>(4) * kChrRamBytes * Np, true) : nullptr;
-        S.slot_bank = M.allocn<u8>(static_cast<std::size_t>(4) * Np, true);
+        env->A.st = alloc_state_view(M, Np, env->chr_ram_any, true);
         EnvArgs& A = env->A;
         const std::size_t N = static_cast<std::size_t>(total) + 1;
         A.trk = M.allocn<Tracker>(N, true);
@@ -325,10 +312,13 @@ int rlenv_save(void* h, std::uint8_t* out, void* stream) {
 int rlenv_load(void* h, const std::uint8_t* in, void* stream) {
     try {
         auto s = static_cast<cudaStream_t>(stream);
-        for (const auto& pb : static_cast<Env*>(h)->mem.state) {
+        Env& env = *static_cast<Env*>(h);
+        for (const auto& pb : env.mem.state) {
             ck(cudaMemcpyAsync(pb.first, in, pb.second, cudaMemcpyHostToDevice, s), "load");
             in += pb.second;
         }
+        for (const Game& gm : env.games)   // level-start slots may have changed: their idle chains are remade
+            if (gm.g.lv_chain_ok) ck(cudaMemsetAsync(gm.g.lv_chain_ok, 0, static_cast<std::size_t>(gm.g.lv_cap) * 4, s), "load");
         ck(cudaStreamSynchronize(s), "load");
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
@@ -350,6 +340,7 @@ int rlenv_enable_places(void* h, int cap, int levels) {
         DevMem& M = env.mem;
         const std::size_t N = static_cast<std::size_t>(env.total) + 1;
         env.A.ep_start = M.allocn<i32>(N, true);
+        env.A.lv_chained = M.allocn<u8>(N);
         {
             std::vector<i32> none(N, -1);
             ck(cudaMemcpy(env.A.ep_start, none.data(), N * 4, cudaMemcpyHostToDevice), "level starts");
@@ -371,6 +362,14 @@ int rlenv_enable_places(void* h, int cap, int levels) {
             ck(cudaMemcpy(g.lv_deaths, none.data(), C * 4, cudaMemcpyHostToDevice), "level starts");
             std::vector<unsigned long long> free_(C, ~0ull);
             ck(cudaMemcpy(g.lv_claim, free_.data(), C * 8, cudaMemcpyHostToDevice), "level starts");
+            // idle chains (derived data, not saved): records after 1..idle_max idle frames of each slot
+            g.lv_idle_n = env.A.idle_max > 0 ? static_cast<u32>(env.A.idle_max) : 0u;
+            g.lv_chain_ok = M.allocn<u32>(C);
+            if (g.lv_idle_n > 0) {
+                g.lv_idle_rec = M.allocn<u8>(C * g.lv_idle_n * kRecBytes);
+                g.lv_idle_fault = M.allocn<u32>(C * g.lv_idle_n);
+                g.lv_scratch = alloc_state_view(M, static_cast<u32>((C + 31) / 32 * 32), g.cart.chr == nullptr, false);
+            }
         }
         env.lv_cap = cap;
         env.lv_levels = levels;
@@ -437,6 +436,7 @@ int rlenv_place_copy(void* h, int gi, const std::int32_t* src, const std::int32_
         auto s = static_cast<cudaStream_t>(stream);
         for (int i = 0; i < count; ++i) {
             const std::size_t a = static_cast<std::size_t>(src[i]), b = static_cast<std::size_t>(dst[i]);
+            if (g.lv_chain_ok) ck(cudaMemsetAsync(g.lv_chain_ok + b, 0, 4, s), "place_copy");   // remade next decision
             ck(cudaMemcpyAsync(g.lv_rec + b * kRecBytes, g.lv_rec + a * kRecBytes, kRecBytes, cudaMemcpyDeviceToDevice, s), "place_copy");
             ck(cudaMemcpyAsync(g.lv_st + b, g.lv_st + a, sizeof(Tracker), cudaMemcpyDeviceToDevice, s), "place_copy");
             ck(cudaMemcpyAsync(g.lv_target + b, g.lv_target + a, 8, cudaMemcpyDeviceToDevice, s), "place_copy");
