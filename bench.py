@@ -448,6 +448,8 @@ def gpu_arm(args):
             frames_per_s=round(4 * value, 1),
             e2e=dict(value=round(e2e_value, 1), unit=UNIT, h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=d2h // K,
                      pinned_ring_slots=R, host_link_gbs=round(link, 1) if link else None,
+                     link_achieved_gbs=round(d2h / K * e2e_value / E / world / 1e9, 1),
+                     link_frac=round(d2h / K * e2e_value / E / world / 1e9 / link, 3) if link else None,
                      note='packed 6-bit pictures + emphasis + reward/done/masks to a pinned host ring every decision'),
             roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
                           traffic=round(tr * env_frames) if tr else None, kernel='k_render',
