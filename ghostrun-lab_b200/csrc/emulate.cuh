@@ -274,7 +274,7 @@ struct Emu {
         return k < C.prg_stage_bytes ? static_cast<u32>(prg_s[k]) : static_cast<u32>(__ldg(C.prg + off));
     }
     __device__ __forceinline__ u32 prg_rd(u32 addr) const {
-        if constexpr (BOARD == kNrom) {
+        if constexpr (BOARD == kNrom || BOARD == kCnrom) {   // 16 / 32 KB fixed (CNROM's PRG pages are 0-3)
             return prg_s[(addr - 0x8000u) & C.prg_mask];   // the whole PRG is staged
         } else if constexpr (BOARD == kUxrom) {
             const u32 off = addr < 0xC000u ? (((prg_bank & C.bank_mask) << 14) | (addr & 0x3FFFu))
@@ -287,7 +287,7 @@ struct Emu {
 
     __device__ __forceinline__ u32 chr_rd(u32 addr) const {
         addr &= 0x1FFFu;
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
+        if constexpr (board_paged(BOARD)) {
             const u32 off = rw(R_CHRPG + (addr >> 10)) + (addr & 0x3FFu);
             return C.chr ? __ldg(C.chr + off) : chr_ram()[off & 0x1FFFu];
         } else {
@@ -297,11 +297,11 @@ struct Emu {
     __device__ __forceinline__ void chr_wr(u32 addr, u32 v) const {
         if (C.chr) return;
         addr &= 0x1FFFu;
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) addr = (rw(R_CHRPG + (addr >> 10)) + (addr & 0x3FFu)) & 0x1FFFu;
+        if constexpr (board_paged(BOARD)) addr = (rw(R_CHRPG + (addr >> 10)) + (addr & 0x3FFu)) & 0x1FFFu;
         chr_ram()[addr] = static_cast<u8>(v);
     }
     __device__ __forceinline__ u32 nt_off(u32 addr) const {
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return nt_off_map(mirroring(), addr);
+        if constexpr (board_paged(BOARD)) return nt_off_map(mirroring(), addr);
         else return nt_off_header(C.arrangement, addr);
     }
     __device__ __forceinline__ static u32 pal_index(u32 addr) {
@@ -348,7 +348,7 @@ struct Emu {
         w0.z = (vt & 0xFFFFu) | ((vt >> 16) << 16);
         w0.w = 0;
         w1.x = 0; w1.y = 0; w1.z = 0;
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
+        if constexpr (board_paged(BOARD)) {
             u32 c0 = 0, c1 = 0;
             for (u32 i = 0; i < 4; ++i) c0 |= ((rw(R_CHRPG + i) >> 10) & 0xFFu) << (i * 8);
             for (u32 i = 0; i < 4; ++i) c1 |= ((rw(R_CHRPG + 4 + i) >> 10) & 0xFFu) << (i * 8);
@@ -641,8 +641,19 @@ struct Emu {
         if (C.arrangement != 2) set_field(R_PPU2, 24, 0xFF, (mreg(9) & 1u) ? kPageHorizontal : kPageVertical);
     }
 
+    // CNROM (patch:2982-2990 paged::sync): PRG 8 KB pages 0-3 (a 16 KB image mirrors through the mask), CHR 1 KB
+    // pages of the 8 KB bank in register 0.
+    __device__ __forceinline__ void cnrom_sync() {
+        for (u32 s = 0; s < 4; ++s) ww(R_PRGPG + s, (s & C.prg_page_mask) << 13);
+        for (u32 s = 0; s < 8; ++s) ww(R_CHRPG + s, ((mreg(0) * 8u + s) & C.chr_page_mask) << 10);
+    }
+
     __device__ __forceinline__ void board_write(u32 addr, u32 v) {
-        if constexpr (BOARD == kMmc1) {
+        if constexpr (BOARD == kCnrom) {
+            (void)addr;   // the bank latch (no bus conflicts: an iNES 1.0 image declares none)
+            set_mreg(0, v);
+            cnrom_sync();
+        } else if constexpr (BOARD == kMmc1) {
             if (v & 0x80u) { set_mreg(0, mreg(0) | 0x0Cu); set_mreg(4, 0); set_mreg(5, 0); mmc1_sync(); return; }
             const u32 cnt = mreg(5);
             const u32 sh = mreg(4) | ((v & 1u) << cnt);
@@ -669,7 +680,7 @@ struct Emu {
     __device__ __forceinline__ void mapper_write(u32 addr, u32 v) {
         if constexpr (BOARD == kUxrom) {
             prg_bank = v & C.bank_mask;
-        } else if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
+        } else if constexpr (board_paged(BOARD)) {
             if (log_active()) {
                 u32 before[8];
                 for (int i = 0; i < 8; ++i) before[i] = rw(R_CHRPG + i);
@@ -1131,7 +1142,7 @@ struct S0State {
 template <u32 BOARD>
 __device__ __forceinline__ u32 s0_chr(const S0Ctx& c, const u32* chr_pages, u32 addr) {
     addr &= 0x1FFFu;
-    if constexpr (BOARD == kMmc1 || BOARD == kMmc3) {
+    if constexpr (board_paged(BOARD)) {
         const u32 off = ((chr_pages[addr >> 10] & c.chr_page_mask) << 10) | (addr & 0x3FFu);
         return c.chr ? __ldg(c.chr + off) : c.chr_ram[off & 0x1FFFu];
     } else {
@@ -1143,7 +1154,7 @@ __device__ __forceinline__ u32 s0_chr(const S0Ctx& c, const u32* chr_pages, u32 
 template <u32 BOARD>
 __device__ __forceinline__ u32 s0_fetch(const S0Ctx& c, u32 ctrl, const u32* chr_pages, u32 mirroring, u32 v) {
     auto ntrd = [&](u32 addr) -> u32 {
-        if constexpr (BOARD == kMmc1 || BOARD == kMmc3) return c.nt[nt_off_map(mirroring, addr)];
+        if constexpr (board_paged(BOARD)) return c.nt[nt_off_map(mirroring, addr)];
         else return c.nt[nt_off_header(c.arrangement, addr)];
     };
     const u32 base = 0x2000u | (v & 0x0C00u);

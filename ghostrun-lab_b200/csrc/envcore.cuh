@@ -803,7 +803,8 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
         // paged boards keep a run-time page map (the others mirror by the header and have none); power-on registers
         // (patch:3057-3085)
         const u32 hmap = g.cart.arrangement == 1 ? kPageHorizontal : kPageVertical;
-        m.ww(R_PPU2, (BOARD == kMmc1 || BOARD == kMmc3) ? (hmap << 24) : 0u);
+        m.ww(R_PPU2, board_paged(BOARD) ? (hmap << 24) : 0u);
+        if constexpr (BOARD == kCnrom) m.cnrom_sync();
         if constexpr (BOARD == kMmc1) { m.set_mreg(0, 0x0C); m.mmc1_sync(); }
         if constexpr (BOARD == kMmc3) {
             m.set_mreg(1, 2); m.set_mreg(2, 4); m.set_mreg(3, 5); m.set_mreg(4, 6); m.set_mreg(5, 7); m.set_mreg(7, 1);

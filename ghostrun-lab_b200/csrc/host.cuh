@@ -81,6 +81,13 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.board = kUxrom;
         c.bank_mask = static_cast<u32>(prg_bytes / 16384 - 1);
         c.fixed_base = static_cast<u32>(prg_bytes - 16384);
+    } else if (mapper == 3) {   // CNROM: 16 / 32 KB PRG fixed, CHR ROM in 8 KB banks
+        if ((prg_bytes != 16384 && prg_bytes != 32768) || chr_bytes == 0 || (chr_bytes & (chr_bytes - 1)) ||
+            chr_bytes > 256 * 1024)
+            throw std::runtime_error("CNROM needs 16 / 32 KB PRG and a power-of-two CHR ROM up to 256 KB");
+        c.board = kCnrom;
+        c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
+        c.chr_page_mask = static_cast<u32>(chr_bytes / 1024 - 1);
     } else if (mapper == 1 || mapper == 4) {
         const std::size_t cb = chr_bytes ? chr_bytes : 8192;
         if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || (cb & (cb - 1)))
@@ -89,7 +96,7 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
         c.chr_page_mask = static_cast<u32>(cb / 1024 - 1);
     } else {
-        throw std::runtime_error("unsupported mapper " + std::to_string(mapper) + " (supported: 0 NROM, 1 MMC1, 2 UxROM, 4 MMC3)");
+        throw std::runtime_error("unsupported mapper " + std::to_string(mapper) + " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3)");
     }
     return c;
 }
@@ -341,5 +348,6 @@ GR_BOARD_TEMPLATES(extern, kNrom)
 GR_BOARD_TEMPLATES(extern, kUxrom)
 GR_BOARD_TEMPLATES(extern, kMmc1)
 GR_BOARD_TEMPLATES(extern, kMmc3)
+GR_BOARD_TEMPLATES(extern, kCnrom)
 
 }  // namespace gr

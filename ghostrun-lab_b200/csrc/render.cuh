@@ -153,7 +153,7 @@ struct Renderer {
                            (W.pal[2] & 0x3F3F3F00u) | bd, (W.pal[3] & 0x3F3F3F00u) | bd);
     }
     __device__ __forceinline__ u32 pal_byte(u32 i) const { return reinterpret_cast<const u8*>(W.pal)[i]; }
-    __device__ __forceinline__ static constexpr bool paged() { return BOARD == kMmc1 || BOARD == kMmc3; }
+    __device__ __forceinline__ static constexpr bool paged() { return board_paged(BOARD); }
 
     __device__ __forceinline__ u32 nt_rd(u32 mir, u32 addr) const {
         if constexpr (paged()) return W.nt[nt_off_map(mir, addr)];

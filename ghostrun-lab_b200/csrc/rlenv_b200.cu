@@ -36,6 +36,7 @@ void launch_phases(Env& env, const Game& gm, bool start, cudaStream_t s, const R
         case kNrom: launch_game<kNrom>(env, gm, start, s, side, rg, phases); break;
         case kUxrom: launch_game<kUxrom>(env, gm, start, s, side, rg, phases); break;
         case kMmc1: launch_game<kMmc1>(env, gm, start, s, side, rg, phases); break;
+        case kCnrom: launch_game<kCnrom>(env, gm, start, s, side, rg, phases); break;
         default: launch_game<kMmc3>(env, gm, start, s, side, rg, phases); break;
     }
 }
@@ -208,7 +209,8 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             }
             C.board = hc.board;
             // PRG staged in the emulation blocks' shared memory: all of it on NROM (16 / 32 KB), else the last 16 KB
-            C.prg_stage_bytes = hc.board == kNrom ? static_cast<u32>(hc.prg.size()) : std::min<u32>(16384u, static_cast<u32>(hc.prg.size()));
+            C.prg_stage_bytes = (hc.board == kNrom || hc.board == kCnrom) ? static_cast<u32>(hc.prg.size())
+                                                                           : std::min<u32>(16384u, static_cast<u32>(hc.prg.size()));
             C.prg_stage_base = static_cast<u32>(hc.prg.size()) - C.prg_stage_bytes;
             C.arrangement = hc.arrangement;
             C.bank_mask = hc.bank_mask;
@@ -226,6 +228,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
                 case kNrom: boot_game<kNrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 case kUxrom: boot_game<kUxrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 case kMmc1: boot_game<kMmc1>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+                case kCnrom: boot_game<kCnrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 default: boot_game<kMmc3>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
             }
             env->games.push_back(gm);

@@ -10,8 +10,9 @@ Everything stays on the device; nothing is copied to the host per step. The libr
 CPU fallback. `lib_path` selects another library with the same C-ABI (the tests point it at the CPU oracle).
 
 Games: the reference's 12 commercial slugs keep their rl10 ids 0..11 (their ROMs and RAM readers are not part of this
-build), and 12 seeded synthetic games 'synth00'..'synth11' (ids 12..23) run on the synthetic cartridges of synth.py:
-game k uses board ('nrom', 'uxrom', 'mmc1', 'mmc3')[k % 4] and its own seeded reward weights.
+build), and 13 seeded synthetic games 'synth00'..'synth12' (ids 12..24) run on the synthetic cartridges of synth.py:
+game k < 12 uses board ('nrom', 'uxrom', 'mmc1', 'mmc3')[k % 4], synth12 the CNROM board, each with its own seeded
+reward weights.
 """
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ import synth
 PKG = Path(__file__).resolve().parent
 REF_GAMES = ['smb', 'pacman', 'excitebike', 'contra', 'castlevania', 'gradius', 'zelda', 'tetris', 'tecmobowl', 'kage',
              'finalmission', 'punchout']   # rl/games_manifest.json order = rl10 game ids 0..11
-SYNTH_GAMES = [f'synth{k:02d}' for k in range(12)]
+SYNTH_GAMES = [f'synth{k:02d}' for k in range(13)]   # synth12: the CNROM cart
 GAMES = REF_GAMES + SYNTH_GAMES
 BOARDS = ('nrom', 'uxrom', 'mmc1', 'mmc3')
 CART_SEED, REWARD_SEED = 1000, 2000
@@ -46,6 +47,8 @@ def default_lib() -> Path:
 
 def synth_cart(slug: str) -> synth.Cart:
     k = SYNTH_GAMES.index(slug)
+    if k == 12:
+        return synth.make_cart(CART_SEED + 4, 'cnrom')
     return synth.make_cart(CART_SEED + k % 4, BOARDS[k % 4])
 
 

@@ -152,7 +152,7 @@ class Asm:
 
 # ------------------------------------------------------------------------------------------------- cartridges
 
-MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'mmc3': 4}
+MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'cnrom': 3, 'mmc3': 4}
 
 # zero page / RAM map of the template (the synthetic reward reader reads these)
 ZP_BUTTONS, ZP_TMP, ZP_LFSR, ZP_FRAME = 0x00, 0x01, 0x02, 0x04
@@ -279,6 +279,9 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     # level: progress high byte reaches the threshold
     i('LDA', 'zp', ZP_PROGRESS + 1); i('CMP', 'imm', p['thresh']); i('BCC', 'rel', 'nolevel')
     i('SBC', 'imm', p['thresh']); i('STA', 'zp', ZP_PROGRESS + 1); i('INC', 'zp', ZP_LEVEL)
+    if board == 'cnrom':   # CHR bank = level & 3 (written over an equal ROM byte, as a bus-conflict-safe game would)
+        i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x03); i('TAX')
+        i('LDA', 'absx', 'banktab'); i('STA', 'absx', 'banktab')
     if board == 'uxrom':
         i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x07); i('TAX')
         i('LDA', 'absx', 'banktab'); i('STA', 'absx', 'banktab')
@@ -380,10 +383,12 @@ def make_cart(seed: int, board: str = 'nrom') -> Cart:
     for k in range(8):
         y = int(r.integers(0, 224)) if k != 1 else 150
         spr += bytes([y, int(r.integers(0, 256)), int(r.integers(0, 256)) & 0xE3, int(r.integers(0, 248))])
-    prg_size = {'nrom': 32768, 'uxrom': 131072, 'mmc1': 131072, 'mmc3': 262144}[board]
+    prg_size = {'nrom': 32768, 'cnrom': 32768, 'uxrom': 131072, 'mmc1': 131072, 'mmc3': 262144}[board]
     data = dict(paltab=pal, nttab=nt, sprtab=bytes(spr))
     if board == 'uxrom':
         data['banktab'] = bytes(range(8))
+    if board == 'cnrom':
+        data['banktab'] = bytes(range(4))
     if board == 'mmc1':
         data['chrtab'] = chr_bytes
     # program in the last 16 KB (fixed bank on every board), vectors at $FFFA
@@ -404,6 +409,8 @@ def make_cart(seed: int, board: str = 'nrom') -> Cart:
                                              r.integers(0, 256, 131072, dtype=np.uint8).tobytes()[:0] + chr_bytes * 16)
     if board == 'mmc3':
         chr_rom = bytes(chr_bytes) + r.integers(0, 256, 131072 - 8192, dtype=np.uint8).tobytes()
+    if board == 'cnrom':   # 4 CHR banks of 8 KB
+        chr_rom = bytes(chr_bytes) + r.integers(0, 256, 32768 - 8192, dtype=np.uint8).tobytes()
     flags6 = ((mapper & 0x0F) << 4) | 0x01          # vertical mirroring
     flags7 = mapper & 0xF0
     header = b'NES\x1a' + bytes([prg_size // 16384, len(chr_rom) // 8192, flags6, flags7]) + bytes(8)

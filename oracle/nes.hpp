@@ -45,8 +45,8 @@ constexpr u32 kS0Evaluate = 0x80000000u, kS0Known = 0x40000000u, kS0Hit = 0x2000
 constexpr u64 kDmcIdle = ~0ull;
 constexpr u8 kPageVertical = 0x0A, kPageHorizontal = 0x0C, kPageSingleLow = 0x00, kPageSingleHigh = 0x0F;
 
-enum Board : u8 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3 };
-inline bool board_paged(Board b) { return b == kMmc1 || b == kMmc3; }
+enum Board : u8 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3, kCnrom = 4 };
+inline bool board_paged(Board b) { return b == kMmc1 || b == kMmc3 || b == kCnrom; }
 
 // ------------------------------------------------------------------------------------------------ cartridge
 
@@ -91,6 +91,13 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
             c.bank_mask = prg / 16384 - 1;
             c.fixed_base = prg - 16384;
             break;
+        case 3:   // CNROM (patch:3995-4027 describe_mapper: 16 / 32 KB PRG, CHR ROM in 8 KB banks)
+            if ((prg != 16384 && prg != 32768) || chr == 0 || (chr & (chr - 1)) || chr > 256 * 1024)
+                throw std::runtime_error("unsupported CNROM image size");
+            c.board = kCnrom;
+            c.prg_page_mask = prg / 8192 - 1;
+            c.chr_page_mask = chr / 1024 - 1;
+            break;
         case 1:
         case 4: {
             c.board = mapper == 1 ? kMmc1 : kMmc3;
@@ -103,7 +110,7 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
         }
         default:
             throw std::runtime_error("unsupported mapper " + std::to_string(mapper) +
-                                     " (supported: 0 NROM, 1 MMC1, 2 UxROM, 4 MMC3)");
+                                     " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3)");
     }
     return c;
 }
@@ -171,7 +178,10 @@ inline u8 header_map(const Cart& c) { return c.arrangement == 1 ? kPageHorizonta
 // Page tables and mirroring from the registers (patch:2962-3054, mapper.cuh paged::sync).
 inline void sync(const Cart& c, Console& m) {
     const u8* r = m.regs;
-    if (c.board == kMmc1) {
+    if (c.board == kCnrom) {   // PRG pages 0-3 (mirrored through the mask), CHR 8 KB bank r[0] (patch:2982-2990)
+        for (u32 s = 0; s < 4; ++s) prg8(c, m, s, s);
+        for (u32 s = 0; s < 8; ++s) chr1(c, m, s, r[0] * 8u + s);
+    } else if (c.board == kMmc1) {
         const u32 ctl = r[kMmc1Control], offs = r[kMmc1Chr0] & 0x10u, prg = r[kMmc1Prg];
         if ((ctl & 0x0C) == 0x0C) { prg16(c, m, 0, prg + offs); prg16(c, m, 1, 0x0F + offs); }
         else if ((ctl & 0x0C) == 0x08) { prg16(c, m, 1, prg + offs); prg16(c, m, 0, offs); }
@@ -209,6 +219,11 @@ inline void power_on(const Cart& c, Console& m) {
 // CPU write to $8000-$FFFF on a paged board (patch:3099-3160).
 inline void write(const Cart& c, Console& m, u16 addr, u8 value) {
     u8* r = m.regs;
+    if (c.board == kCnrom) {   // the bank latch; an iNES 1.0 image declares no bus conflicts (patch:3124-3127)
+        r[0] = value;
+        sync(c, m);
+        return;
+    }
     if (c.board == kMmc1) {
         if (value & 0x80) { r[kMmc1Control] |= 0x0C; r[kMmc1Shift] = 0; r[kMmc1Count] = 0; sync(c, m); return; }
         r[kMmc1Shift] = static_cast<u8>(r[kMmc1Shift] | ((value & 1u) << r[kMmc1Count]));
