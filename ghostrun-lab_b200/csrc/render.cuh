@@ -617,11 +617,31 @@ struct Renderer {
         const u32 g = lane >> 3, j = lane & 7u;
         const u32 lt = (1u << lane) - 1u;
         uint2* sbuf = reinterpret_cast<uint2*>(W.px);   // [4 lines][8 sprites] (colour nibbles, meta)
+        // Lines that can show a sprite: one at y is found by the evaluation at the end of lines y..y+15 (height <= 16)
+        // and drawn on lines y+1..y+16. A superset; iterations whose 4 lines have none skip the sprite work.
+        u32* may = reinterpret_cast<u32*>(W.emph);   // 8 words: bit l of the 256-line mask
+        {
+            auto span = [](u32 sp, u32 base) -> u32 {
+                const int lo = static_cast<int>(sp & 0xFFu) + 1 - static_cast<int>(base);
+                const int hi = lo + 15;
+                if (hi < 0 || lo > 31) return 0u;
+                const u32 a = lo < 0 ? 0u : static_cast<u32>(lo), b = hi > 31 ? 31u : static_cast<u32>(hi);
+                return (0xFFFFFFFFu >> (31u - b)) & (0xFFFFFFFFu << a);
+            };
+#pragma unroll
+            for (u32 b = 0; b < 8; ++b) {
+                const u32 m = __reduce_or_sync(0xFFFFFFFFu, span(spA, 32u * b) | span(spB, 32u * b));
+                if (lane == 0) may[b] = m;
+            }
+            __syncwarp();
+        }
         for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
             // ---- sprites of lines l0..l0+3 (fetched at the end of the line above each)
             u32 nsp = 0;   // this lane group's sprite count
+            const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
+                if (!any) break;
                 const int e = l0 + k - 1;
                 const uint2 re = F.rec[e];
                 const u32 ctrl = ((re.x >> 18) & 7u) << 3;
@@ -672,7 +692,8 @@ struct Renderer {
                 const u32 x4 = 4u * ((r.x >> 15) & 7u);
                 const u32 c0 = line_tile_p(lf, 4 * j + 1, pages), c1 = line_tile_p(lf, 4 * j + 2, pages);
                 const u32 c2 = line_tile_p(lf, 4 * j + 3, pages), c3 = line_tile_p(lf, 4 * j + 4, pages);
-                const u32 c4 = line_tile_p(lf, 4 * j + 5, pages);
+                // fetch 4j + 5 is the next lane's first; lane 7's last 16 pixels (screen x 248-263) are not drawn
+                const u32 c4 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
                 s0 = __funnelshift_r(c0, c1, x4); s1 = __funnelshift_r(c1, c2, x4);
                 s2 = __funnelshift_r(c2, c3, x4); s3 = __funnelshift_r(c3, c4, x4);
             }
