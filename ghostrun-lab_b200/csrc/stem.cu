@@ -7,15 +7,18 @@
 // are bf16 x bf16 summed in fp32 (tcgen05.mma kind::f16, fp32 accumulator in tensor memory); only the order of the
 // fp32 additions can differ from another implementation of the same GEMM.
 //
-// Mapping: a CTA of 128 threads takes 128 output pixels (one M=128 tile) at a time. Each thread builds its pixel's
-// 48 inputs (8 colour-number pairs + their emphasis, 24 palette lookups in shared memory) straight into the A tile in
-// shared memory, laid out as 8x16-byte core matrices without swizzle (K-major: element (m, k) at
-// (m / 8) * 768 + (m % 8) * 16 + (k / 8) * 128 + (k % 8) * 2); the weights (B, 16 x 48, same layout) stay in shared
-// memory. One thread issues the three K=16 MMAs into 16 fp32 columns of tensor memory and commits them to an
-// mbarrier; then warp w reads accumulator rows 32w..32w+31 (tcgen05.ld 32x32b), adds the bias and stores 16 bf16 per
-// pixel (channels-last, 32 contiguous bytes). A tiles and accumulators are double-buffered, so one tile's MMAs run
-// while the next is built. The kernel is HBM-bound (12-16 input bytes and 32 output bytes per output pixel against
-// 1,536 flops); several persistent CTAs per SM keep loads in flight.
+// Mapping: a CTA of 128 threads takes one output row (120 pixels; an M=128 tile whose rows 120..127 idle) at a time.
+// The row's input is exactly 8 picture rows (4 frames x 2 rows); the whole CTA loads them with coalesced 4-byte loads
+// one tile ahead (held in registers, then staged in shared memory). The K order of the GEMM is permuted so that a
+// palette lookup lands in the A operand unchanged: k' = pos * 4 + c, pos = frame * 4 + dy * 2 + dx (16 input pixels),
+// c = R, G, B, 1 (64 inputs); the weights are permuted the same way, the constant-1 input of position 0 carries the
+// bias and the others weigh 0. Thread m looks up its pixel's 16 palette entries (8 bytes each, shared memory) and
+// writes them as its row of A in tensor memory (tcgen05.st 32x32b: warp w owns lanes 32w..32w+31). One thread issues
+// the four K=16 MMAs (A from tensor memory, weights from shared memory as no-swizzle K-major core matrices: element
+// (n, k') at (n / 8) * 1024 + (n % 8) * 16 + (k' / 8) * 128 + (k' % 8) * 2) into 16 fp32 columns and commits them to
+// an mbarrier. The next iteration waits for them (bounded), reads the accumulator (tcgen05.ld 32x32b), writes the
+// next tile's A, and the row's 120 x 16 bf16 outputs (channels-last, 3,840 contiguous bytes) are stored while the
+// tensor core works. The kernel moves 12-16 input bytes and 32 output bytes per output pixel against 2,048 flops.
 //
 // The input is either the byte pictures [B, 4, 224, 240] or their 6-bit packed form [B, 4, 224, 180] (the rollout
 // storage format, rl/csrc/rlenv.cu:126-134): the packed variant unpacks in the kernel.
@@ -28,8 +31,12 @@
 namespace {
 
 constexpr int kH = 224, kW = 240, kOH = 112, kOW = 120, kFrames = 4;
-constexpr int kTileM = 128, kK = 48, kN = 16;
+constexpr int kTileM = 128, kK = 48, kKp = 64, kN = 16;   // kKp: the permuted K (16 input pixels x R, G, B, 1)
+constexpr uint32_t kAccCol = 32;                          // accumulator columns 32..47; A rows in columns 0..31
+constexpr uint32_t kOneBf16 = 0x3F80u;                    // 1.0 in bf16
 constexpr int kThreads = 128;
+constexpr int kCtasPerSm = 8;
+constexpr size_t kPadSmem = 16 * 1024;   // with ~10.3 KB static: 26.5 KB per CTA, at most 8 CTAs per SM
 constexpr unsigned kSpinLimit = 1u << 24;   // mbarrier polls before a tile is given up (error flag set)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -48,8 +55,9 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kN >> 3) << 17) |
                             (static_cast<uint32_t>(kTileM >> 4) << 24);
 
-__device__ __forceinline__ uint32_t bf16_bits(float v) {
-    return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 struct StemArgs {
@@ -63,181 +71,219 @@ struct StemArgs {
     long long n_out;            // B * 112 * 120
 };
 
-// The raw inputs of one output pixel: for each (frame, dy) the two colour numbers (c0 | c1 << 8) and the emphasis.
-struct Raw { uint32_t c[8]; uint32_t e[8]; };
+// The 8 picture rows of one output row, loaded by the whole CTA one tile ahead: 4-byte words in registers, then
+// shared memory (rows at a 256-byte stride), and the rows' emphasis bits (as palette offsets, emphasis << 6).
+template <bool PACKED>
+struct RowLoad {
+    static constexpr int kRowBytes = PACKED ? kW / 4 * 3 : kW;   // 180 or 240
+    static constexpr int kWords = kRowBytes / 4;                  // 45 or 60 per picture row
+    static constexpr int kPer = (8 * kWords + kThreads - 1) / kThreads;   // words per thread (3 or 4)
+    uint32_t w[kPer];
+    uint32_t e;   // thread q < 8: picture row q = frame * 2 + dy
+};
 
 template <bool PACKED>
-__device__ __forceinline__ void load_raw(const StemArgs& a, long long p, Raw& r) {
-    if (p >= a.n_out) {
+__device__ __forceinline__ void rows_load(const StemArgs& a, long long r, long long rows, int tid, RowLoad<PACKED>& L) {
+    using R = RowLoad<PACKED>;
+    if (r >= rows) return;
+    const uint32_t r32 = static_cast<uint32_t>(r);   // rows < 2^31 / 120 (checked at launch)
+    const uint32_t b = r32 / kOH, oy = r32 - b * kOH;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) { r.c[q] = 0; r.e[q] = 0; }
-        return;
-    }
-    const uint32_t p32 = static_cast<uint32_t>(p);   // n_out < 2^31 (checked at launch): 32-bit constant divisions
-    const uint32_t b = p32 / static_cast<uint32_t>(kOH * kOW);
-    const uint32_t rr = p32 - b * static_cast<uint32_t>(kOH * kOW);
-    const int oy = static_cast<int>(rr / kOW), ox = static_cast<int>(rr - (rr / kOW) * kOW);
-#pragma unroll
-    for (int f = 0; f < kFrames; ++f) {
-#pragma unroll
-        for (int dy = 0; dy < 2; ++dy) {
-            const int q = f * 2 + dy;
-            const long long plane_row = (static_cast<long long>(b) * kFrames + f) * kH + 2 * oy + dy;
-            if constexpr (PACKED) {
-                // the 3 bytes of 4-pixel group ox / 2 (rows are 4-byte aligned: 180 bytes); a second word only when the
-                // group straddles two (then both lie inside the row)
-                const long long off = plane_row * (kW / 4 * 3) + 3 * (ox >> 1);
-                const uint32_t* wp = reinterpret_cast<const uint32_t*>(a.obs + (off & ~3ll));
-                const uint32_t lo = __ldg(wp), sh = static_cast<uint32_t>(off & 3) * 8u;
-                const uint32_t hi = sh >= 16u ? __ldg(wp + 1) : 0u;
-                const uint32_t v = __funnelshift_r(lo, hi, sh);
-                const uint32_t s2 = (ox & 1) ? 12u : 0u;
-                r.c[q] = ((v >> s2) & 63u) | (((v >> (s2 + 6)) & 63u) << 8);
-            } else {
-                const uint32_t two = __ldg(reinterpret_cast<const uint16_t*>(a.obs + plane_row * kW + 2 * ox));
-                r.c[q] = two & 0x3F3Fu;
-            }
-            r.e[q] = static_cast<uint32_t>(__ldg(a.emph + plane_row)) << 6;
+    for (int k = 0; k < R::kPer; ++k) {
+        const int wi = tid + k * kThreads;
+        if (wi < 8 * R::kWords) {
+            const int q = wi / R::kWords, c = wi - q * R::kWords;
+            const long long row = (static_cast<long long>(b) * kFrames + (q >> 1)) * kH + 2 * oy + (q & 1);
+            L.w[k] = __ldg(reinterpret_cast<const uint32_t*>(a.obs + row * R::kRowBytes) + c);
         }
+    }
+    if (tid < 8) {
+        const long long row = (static_cast<long long>(b) * kFrames + (tid >> 1)) * kH + 2 * oy + (tid & 1);
+        L.e = static_cast<uint32_t>(__ldg(a.emph + row)) << 6;
     }
 }
 
 template <bool PACKED>
-__global__ void __launch_bounds__(kThreads) k_stem_fwd(const __grid_constant__ StemArgs a) {
-    __shared__ __align__(1024) uint8_t sA[2][kTileM * kK * 2];   // 2 x 12 KB (double-buffered A tiles)
-    __shared__ __align__(128) uint8_t sB[kN * kK * 2];           // 1.5 KB
-    __shared__ __align__(16) uint2 sPal[512];                    // 4 KB
-    __shared__ float sBias[kN];
-    __shared__ __align__(8) uint64_t mbar[2];
+__device__ __forceinline__ void rows_store(const RowLoad<PACKED>& L, uint32_t* rowbuf, uint32_t* ebuf, int tid) {
+    using R = RowLoad<PACKED>;
+#pragma unroll
+    for (int k = 0; k < R::kPer; ++k) {
+        const int wi = tid + k * kThreads;
+        if (wi < 8 * R::kWords) {
+            const int q = wi / R::kWords, c = wi - q * R::kWords;
+            rowbuf[q * 64 + c] = L.w[k];
+        }
+    }
+    if (tid < 8) ebuf[tid] = L.e;
+}
+
+// Half of a pixel's A row (picture rows q0..q0+3: 8 input pixels, 16 words) from the staged rows: two palette
+// lookups per picture row, each (R | G << 16, B | 1.0 << 16).
+template <bool PACKED>
+__device__ __forceinline__ void build_half(const uint32_t* rb, const uint32_t* eb, const uint2* pal, int q0,
+                                           uint32_t wi, uint32_t sh, uint32_t* x) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int q = q0 + j;
+        uint32_t c0, c1;
+        if constexpr (PACKED) {   // the pair's 12 bits at bit 12 * ox of the row (a little-endian 6-bit stream)
+            const uint32_t v = __funnelshift_r(rb[q * 64 + wi], rb[q * 64 + wi + 1], sh);
+            c0 = v & 63u;
+            c1 = (v >> 6) & 63u;
+        } else {                  // bytes 2 * ox, 2 * ox + 1
+            const uint32_t v = rb[q * 64 + wi] >> sh;
+            c0 = v & 63u;
+            c1 = (v >> 8) & 63u;
+        }
+        const uint32_t e = eb[q];
+        const uint2 p0 = pal[c0 | e], p1 = pal[c1 | e];
+        x[4 * j] = p0.x;
+        x[4 * j + 1] = p0.y;
+        x[4 * j + 2] = p1.x;
+        x[4 * j + 3] = p1.y;
+    }
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* x) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                 "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+                 :: "r"(taddr), "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7]),
+                    "r"(x[8]), "r"(x[9]), "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]), "r"(x[15])
+                 : "memory");
+}
+
+// Bounded wait for phase `parity` of the mbarrier: 1 when it completed.
+__device__ __forceinline__ uint32_t mbar_wait(uint32_t addr, uint32_t parity) {
+    uint32_t done = 0;
+    for (unsigned spin = 0; spin < kSpinLimit && !done; ++spin) {
+        asm volatile("{\n\t.reg .pred q;\n\t"
+                     "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, q;\n\t}"
+                     : "=r"(done) : "r"(addr), "r"(parity) : "memory");
+    }
+    return done;
+}
+
+template <bool PACKED>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stem_fwd(const __grid_constant__ StemArgs a) {
+    __shared__ __align__(128) uint8_t sB[kN * kKp * 2];   // 2 KB: permuted weights + bias
+    __shared__ __align__(16) uint2 sPal[512];             // 4 KB
+    __shared__ __align__(16) uint32_t sRow[2][8 * 64];    // 2 x 2 KB: a tile's 8 picture rows
+    __shared__ __align__(16) uint32_t sEmph[2][8];
+    __shared__ __align__(8) uint64_t mbar;
     __shared__ uint32_t tmem_base;
-    __shared__ int bail;
     const int tid = threadIdx.x, warp = tid >> 5;
 
-    for (int i = tid; i < 512; i += kThreads) sPal[i] = reinterpret_cast<const uint2*>(a.pal)[i];
-    for (int i = tid; i < kN * kK; i += kThreads) {   // weights into the core-matrix layout (row n = output channel)
-        const int n = i / kK, k = i % kK;
-        const uint32_t off = (n / 8) * 768 + (n % 8) * 16 + (k / 8) * 128 + (k % 8) * 2;
-        *reinterpret_cast<uint16_t*>(sB + off) = a.w[i];
+    for (int i = tid; i < 512; i += kThreads) {
+        const uint2 v = reinterpret_cast<const uint2*>(a.pal)[i];
+        sPal[i] = make_uint2(v.x, (v.y & 0xFFFFu) | (kOneBf16 << 16));   // R | G << 16, B | 1.0 << 16
     }
-    if (tid < kN) sBias[tid] = __bfloat162float(__ushort_as_bfloat16(a.bias[tid]));
+    for (int i = tid; i < kN * kKp; i += kThreads) {   // permuted weights into the core-matrix layout (row n = channel)
+        const int n = i / kKp, kp = i % kKp, pos = kp >> 2, c = kp & 3;
+        const int f = pos >> 2, dy = (pos >> 1) & 1, dx = pos & 1;
+        const uint16_t v = c < 3 ? a.w[n * kK + (f * 3 + c) * 4 + dy * 2 + dx] : (pos == 0 ? a.bias[n] : uint16_t(0));
+        *reinterpret_cast<uint16_t*>(sB + (n / 8) * 1024 + (n % 8) * 16 + (kp / 8) * 128 + (kp % 8) * 2) = v;
+    }
     if (tid == 0) {
-        bail = 0;
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar[1])));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar)));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {   // 32 columns of tensor memory: two 16-column fp32 accumulators
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" :: "r"(smem_u32(&tmem_base)));
+    if (warp == 0) {   // 64 columns of tensor memory: A rows (32 columns of bf16 pairs) and the fp32 accumulator (16)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" :: "r"(smem_u32(&tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
+    const long long rows = a.n_out / kOW;   // tiles: output rows
+    const long long step = gridDim.x;
+    RowLoad<PACKED> L;
+    rows_load<PACKED>(a, blockIdx.x, rows, tid, L);          // tile 0's rows
+    rows_store<PACKED>(L, sRow[0], sEmph[0], tid);
+    rows_load<PACKED>(a, blockIdx.x + step, rows, tid, L);   // tile 1's rows, in flight
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base;
-    const uint32_t b_base = smem_u32(sB);
-    uint32_t phase[2] = {0u, 0u};
+    const uint32_t lane_a = tmem + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's lanes, column 0
+    const uint32_t b_base = smem_u32(&sB[0]);
+    const uint32_t bar = smem_u32(&mbar);
+    // where this thread's pixel pair sits in a staged picture row
+    const int ox = tid < kOW ? tid : kOW - 1;
+    const uint32_t bit = PACKED ? 12u * static_cast<uint32_t>(ox) : 16u * static_cast<uint32_t>(ox);
+    const uint32_t wi = bit >> 5, sh = bit & 31u;
+    uint32_t phase = 0;
 
-    // Pipeline: iteration i builds tile i's A rows and issues its MMAs (buffer i % 2), then drains tile i - 1's
-    // accumulator, so a tile's MMAs run while the next tile is built. Buffer reuse two iterations later is safe: its
-    // MMAs were waited for (before the A rows are rewritten) and its accumulator reads finished (before the MMAs
-    // that overwrite it, ordered by the barrier at the top of the iteration).
-    const long long tiles = (a.n_out + kTileM - 1) / kTileM;
-    long long prev_p = -1;
+    // Iteration i (tile r, row buffer i % 2): wait for tile i-1's MMAs; look up tile i's inputs and write them as
+    // A rows; read tile i-1's accumulator; stage tile i+1's rows; barrier; MMAs of tile i; store tile i-1's outputs;
+    // issue the loads of tile i+2. Row buffer i % 2 is rewritten (iteration i+1) only after the barrier that follows
+    // its reads; A and the accumulator are rewritten only after the MMAs that read or wrote them completed.
+    long long prev_r = -1;
     int it = 0;
-    for (long long tile = blockIdx.x;; tile += gridDim.x, ++it) {
-        const bool have = tile < tiles;
+    for (long long r = blockIdx.x;; r += step, ++it) {
+        const bool have = r < rows;
         const int buf = it & 1;
-        const long long p = tile * kTileM + tid;
-        if (have) {
-            Raw raw;
-            load_raw<PACKED>(a, p, raw);
-            uint32_t x[24];   // 48 bf16, two per word, k order
-#pragma unroll
-            for (int f = 0; f < kFrames; ++f) {
-#pragma unroll
-                for (int dy = 0; dy < 2; ++dy) {
-                    const int q = f * 2 + dy;
-                    const uint2 q0 = sPal[(raw.c[q] & 63u) | raw.e[q]], q1 = sPal[(raw.c[q] >> 8) | raw.e[q]];   // (R | G << 16, B)
-                    // k = (f * 3 + ch) * 4 + dy * 2 + dx: the pair (dx = 0, 1) of channel ch is one 32-bit word
-                    const int w0 = ((f * 3 + 0) * 4 + dy * 2) >> 1;
-                    x[w0] = (q0.x & 0xFFFFu) | ((q1.x & 0xFFFFu) << 16);
-                    x[w0 + 2] = (q0.x >> 16) | (q1.x & 0xFFFF0000u);
-                    x[w0 + 4] = (q0.y & 0xFFFFu) | ((q1.y & 0xFFFFu) << 16);
-                }
-            }
-            uint8_t* rowbase = sA[buf] + (tid / 8) * 768 + (tid % 8) * 16;   // 6 core-matrix rows of 16 bytes
-#pragma unroll
-            for (int j = 0; j < 6; ++j)
-                *reinterpret_cast<uint4*>(rowbase + j * 128) = make_uint4(x[4 * j], x[4 * j + 1], x[4 * j + 2], x[4 * j + 3]);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic-proxy stores -> tensor core reads
+        uint32_t ok = 1, d[16];
+        if (it > 0) ok = mbar_wait(bar, phase);   // tile i-1's MMAs (they read A and wrote the accumulator)
+        if (have && ok) {
+            uint32_t x[16];
+            build_half<PACKED>(sRow[buf], sEmph[buf], sPal, 0, wi, sh, x);
+            tmem_st16(lane_a, x);
+            build_half<PACKED>(sRow[buf], sEmph[buf], sPal, 4, wi, sh, x);
+            tmem_st16(lane_a + 16, x);
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
-        if (have && tid == 0) {
+        if (it > 0) {
+            phase ^= 1u;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_base = smem_u32(sA[buf]);
-            const uint32_t acc_cols = tmem + static_cast<uint32_t>(buf * kN);
-#pragma unroll
-            for (int kk = 0; kk < 3; ++kk) {   // K = 48 in three K = 16 steps (two 8-element core matrices each)
-                const uint64_t da = smem_desc(a_base + kk * 256, 128, 768);
-                const uint64_t db = smem_desc(b_base + kk * 256, 128, 768);
-                const uint32_t acc = kk > 0 ? 1u : 0u;
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\t"
-                    "setp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-                    :: "r"(acc_cols), "l"(da), "l"(db), "r"(kIdesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         :: "r"(smem_u32(&mbar[buf])) : "memory");
-        }
-        if (it > 0) {   // ---- the previous tile: wait for its MMAs (bounded), bias, bf16, store
-            const int pb = buf ^ 1;
-            uint32_t done = 0;
-            for (unsigned spin = 0; spin < kSpinLimit && !done; ++spin) {
-                asm volatile("{\n\t.reg .pred q;\n\t"
-                             "mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n\t"
-                             "selp.u32 %0, 1, 0, q;\n\t}"
-                             : "=r"(done) : "r"(smem_u32(&mbar[pb])), "r"(phase[pb]) : "memory");
-            }
-            phase[pb] ^= 1u;
-            if (!done) bail = 1;
-            __syncthreads();
-            if (bail) {   // the tensor core did not answer: report and stop (tensor memory is freed below)
-                if (tid == 0) atomicExch(a.err, 1);
-                break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            uint32_t d[16];
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(pb * kN);
             asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
                          "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
                          : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]),
                            "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
-                         : "r"(taddr));
+                         : "r"(lane_a + kAccCol));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (prev_p >= 0 && prev_p < a.n_out) {
-                uint32_t o[8];
+        }
+        if (have && ok) {
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            if (r + step < rows) rows_store<PACKED>(L, sRow[buf ^ 1], sEmph[buf ^ 1], tid);   // tile i+1's rows
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        const int fail = __syncthreads_or(ok == 0u);
+        if (fail) {   // the tensor core did not answer: report, wait (bounded) for the MMAs in flight, stop
+            if (tid == 0) atomicExch(a.err, 1);
+            mbar_wait(bar, phase ^ 1u);
+            break;    // tensor memory is freed below
+        }
+        if (have && tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int n = 0; n < 8; ++n) {
-                    const float lo = __uint_as_float(d[2 * n]) + sBias[2 * n];
-                    const float hi = __uint_as_float(d[2 * n + 1]) + sBias[2 * n + 1];
-                    o[n] = bf16_bits(lo) | (bf16_bits(hi) << 16);
-                }
-                uint4* dst = reinterpret_cast<uint4*>(a.out + prev_p * kN);
-                dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            for (int kk = 0; kk < kKp / 16; ++kk) {   // K' = 64 in four K = 16 steps (8 columns of A each)
+                const uint64_t db = smem_desc(b_base + kk * 256, 128, 1024);
+                const uint32_t acc = kk > 0 ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\t"
+                    "setp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+                    :: "r"(tmem + kAccCol), "r"(tmem + static_cast<uint32_t>(kk * 8)), "l"(db), "r"(kIdesc), "r"(acc),
+                       "r"(0u), "r"(0u), "r"(0u), "r"(0u));
             }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         :: "r"(bar) : "memory");
+        }
+        if (it > 0 && tid < kOW) {   // tile i-1: bf16 outputs (the bias is in the sum)
+            uint32_t o[8];
+#pragma unroll
+            for (int n = 0; n < 8; ++n) o[n] = bf16x2_bits(__uint_as_float(d[2 * n]), __uint_as_float(d[2 * n + 1]));
+            uint4* dst = reinterpret_cast<uint4*>(a.out + (prev_r * kOW + tid) * kN);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
         if (!have) break;
-        prev_p = p;
+        rows_load<PACKED>(a, r + 2 * step, rows, tid, L);   // tile i+2's rows in flight
+        prev_r = r;
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" :: "r"(tmem));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" :: "r"(tmem));
     }
 }
 
@@ -269,12 +315,18 @@ int rl_stem_fwd(const void* obs, const void* emph, const void* pal4, const void*
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long tiles = (a.n_out + kTileM - 1) / kTileM;
-    const long long want = static_cast<long long>(sms) * 6;   // persistent CTAs, 6 per SM (30 KB shared each)
+    if ((reinterpret_cast<uintptr_t>(obs) & 3) || (reinterpret_cast<uintptr_t>(out) & 15)) {
+        g_stem_error = "rl_stem_fwd: obs must be 4-byte and out 16-byte aligned";
+        return 1;
+    }
+    const long long tiles = batch * kOH;   // output rows
+    // persistent CTAs, 8 per SM: 8 x 64 columns fill the SM's tensor memory; the unused dynamic shared memory keeps a
+    // ninth CTA off the SM (its allocation would wait for a CTA to finish)
+    const long long want = static_cast<long long>(sms) * kCtasPerSm;
     const unsigned grid = static_cast<unsigned>(tiles < want ? tiles : want);
     auto s = static_cast<cudaStream_t>(stream);
-    if (packed) k_stem_fwd<true><<<grid, kThreads, 0, s>>>(a);
-    else k_stem_fwd<false><<<grid, kThreads, 0, s>>>(a);
+    if (packed) k_stem_fwd<true><<<grid, kThreads, kPadSmem, s>>>(a);
+    else k_stem_fwd<false><<<grid, kThreads, kPadSmem, s>>>(a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { g_stem_error = cudaGetErrorString(e); return 1; }
     return 0;
