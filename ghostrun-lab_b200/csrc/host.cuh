@@ -164,6 +164,13 @@ struct Range {
     u8* emph = nullptr;
 };
 
+// Where a launch forks its restart work: a side stream, the event it waits for on the caller's stream, and the event
+// the caller's stream waits for at the join.
+struct Side {
+    cudaStream_t stream;
+    cudaEvent_t fork, done;
+};
+
 
 struct Game {
     int game_id = 0;
@@ -189,7 +196,14 @@ struct Env {
     std::vector<cudaStream_t> gmain, gside;
     std::vector<cudaEvent_t> gfork, gmain_done, gside_done;
     cudaEvent_t ev_begin = nullptr;
+    // Ranges (rlenv_step_range) fork their restart work onto a side stream of the CALLER's stream, created on first
+    // use, so that parts of one game stepped on different caller streams overlap instead of meeting on the game's
+    // side stream. Each range lists its restarting envs in its own slice of the list, with its own counter.
+    struct CallerSide { cudaStream_t caller, side; cudaEvent_t fork, done; };
+    std::vector<CallerSide> range_sides;
+    int side_priority = 0;
     ~Env() {
+        for (auto& c : range_sides) { cudaEventDestroy(c.fork); cudaEventDestroy(c.done); cudaStreamDestroy(c.side); }
         if (ev) cudaEventDestroy(ev);
         if (ev_begin) cudaEventDestroy(ev_begin);
         for (auto e : gfork) cudaEventDestroy(e);
@@ -220,15 +234,19 @@ inline void check_launch(const char* what) {
 enum : u32 { kPhFrames = 1, kPhFinish = 2, kPhRender = 4, kPhRestart = 8, kPhAll = 15 };
 
 template <u32 B>
-void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cudaStream_t side, const Range& rg,
+void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, const Side& sd, const Range& rg,
                  u32 phases) {
+    cudaStream_t side = sd.stream;
     GameArgs g = gm.g;
     const EnvArgs& A0 = env.A;
     EnvArgs A = A0;
     if (rg.obs) { A.obs = rg.obs; A.emph = rg.emph; }
     if (rg.count >= 0) { g.e0 = gm.g.e0 + static_cast<u32>(rg.start); g.n = static_cast<u32>(rg.count); }
-    A.list = A0.list + gm.g.game_e0;              // this game's restart list and count
-    A.list_count = A0.list_count + gm.index;
+    // this game's (or this range's) restart list and count: a range lists into its own slice, counter after the games'
+    const bool ranged = rg.count >= 0;
+    A.list = A0.list + gm.g.game_e0 + (ranged ? static_cast<u32>(rg.start) : 0u);
+    A.list_count = A0.list_count + (ranged ? env.games.size() + 1 + gm.g.game_e0 + static_cast<u32>(rg.start)
+                                           : static_cast<std::size_t>(gm.index));
     const u32 n = g.n;
     if (n == 0) return;
     const u32 tb = 128;
@@ -258,7 +276,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
         k_finish<<<(n + tb - 1) / tb, tb, 0, s>>>(g, A, start ? 1 : 0);
         T.end(kKFinish, s);
         check_launch("k_finish");
-        ck(cudaEventRecord(env.gfork[gm.index], s), "fork");
+        ck(cudaEventRecord(sd.fork, s), "fork");
     }
     if ((phases & kPhRender) && !start && !A.no_render) {
         R.list = nullptr;
@@ -270,7 +288,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
         check_launch("k_render");
     }
     if (!(phases & kPhRestart)) return;
-    ck(cudaStreamWaitEvent(side, env.gfork[gm.index], 0), "fork");
+    ck(cudaStreamWaitEvent(side, sd.fork, 0), "fork");
     const u32 wb = (n + kEnvsPerWarp - 1) / kEnvsPerWarp;
     if (g.lv_cap > 0 && g.lv_idle_n > 0) {   // idle chains of the slots that changed, before the restores use them
         T.begin(kKFinish, side);
@@ -305,10 +323,13 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, cud
     }
 }
 
-// The caller's stream waits for game gi's side-stream restart work.
-inline void join_side(const Env& env, int gi, cudaStream_t s) {
-    ck(cudaEventRecord(env.gside_done[gi], env.gside[gi]), "join");
-    ck(cudaStreamWaitEvent(s, env.gside_done[gi], 0), "join");
+// Game gi's own side stream (whole-game launches).
+inline Side game_side(const Env& env, int gi) { return Side{env.gside[gi], env.gfork[gi], env.gside_done[gi]}; }
+
+// The caller's stream waits for the side stream's restart work.
+inline void join_side(const Side& sd, cudaStream_t s) {
+    ck(cudaEventRecord(sd.done, sd.stream), "join");
+    ck(cudaStreamWaitEvent(s, sd.done, 0), "join");
 }
 
 template <u32 B>
@@ -342,7 +363,7 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
 
 
 #define GR_BOARD_TEMPLATES(EXT, B)                                                                   \
-    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t, cudaStream_t, const Range&, u32); \
+    EXT template void launch_game<B>(const Env&, const Game&, bool, cudaStream_t, const Side&, const Range&, u32); \
     EXT template void boot_game<B>(Env&, Game&, const u8*, std::size_t, int, u32);
 GR_BOARD_TEMPLATES(extern, kNrom)
 GR_BOARD_TEMPLATES(extern, kUxrom)

@@ -30,21 +30,35 @@ std::map<int, Spec> g_specs;   // rl10 game id -> reward parameters (rl10_regist
 int fail(const std::exception& ex) { g_error = ex.what(); return 1; }
 
 // The given launch phases of one game: main work on stream `s`, restart work on the game's side stream.
-void launch_phases(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg, u32 phases) {
-    cudaStream_t side = env.gside[gm.index];
+void launch_phases(Env& env, const Game& gm, bool start, cudaStream_t s, const Side& sd, const Range& rg, u32 phases) {
     switch (gm.g.cart.board) {
-        case kNrom: launch_game<kNrom>(env, gm, start, s, side, rg, phases); break;
-        case kUxrom: launch_game<kUxrom>(env, gm, start, s, side, rg, phases); break;
-        case kMmc1: launch_game<kMmc1>(env, gm, start, s, side, rg, phases); break;
-        case kCnrom: launch_game<kCnrom>(env, gm, start, s, side, rg, phases); break;
-        default: launch_game<kMmc3>(env, gm, start, s, side, rg, phases); break;
+        case kNrom: launch_game<kNrom>(env, gm, start, s, sd, rg, phases); break;
+        case kUxrom: launch_game<kUxrom>(env, gm, start, s, sd, rg, phases); break;
+        case kMmc1: launch_game<kMmc1>(env, gm, start, s, sd, rg, phases); break;
+        case kCnrom: launch_game<kCnrom>(env, gm, start, s, sd, rg, phases); break;
+        default: launch_game<kMmc3>(env, gm, start, s, sd, rg, phases); break;
     }
 }
 
-// One game's decision on stream `s`, its restart work joined back into `s`.
+// The side stream of a range stepped on caller stream `s`: the game's own while level starts are on (the level
+// archive and its idle chains are per game, so their kernels stay in one stream), otherwise one per caller stream.
+Side range_side(Env& env, const Game& gm, cudaStream_t s) {
+    if (gm.g.lv_cap > 0) return game_side(env, gm.index);
+    for (const auto& c : env.range_sides)
+        if (c.caller == s) return Side{c.side, c.fork, c.done};
+    Env::CallerSide c{s, nullptr, nullptr, nullptr};
+    ck(cudaStreamCreateWithPriority(&c.side, cudaStreamNonBlocking, env.side_priority), "range side stream");
+    ck(cudaEventCreateWithFlags(&c.fork, cudaEventDisableTiming), "event");
+    ck(cudaEventCreateWithFlags(&c.done, cudaEventDisableTiming), "event");
+    env.range_sides.push_back(c);
+    return Side{c.side, c.fork, c.done};
+}
+
+// One game's decision (or a range of its envs) on stream `s`, its restart work joined back into `s`.
 void launch_one(Env& env, const Game& gm, bool start, cudaStream_t s, const Range& rg) {
-    launch_phases(env, gm, start, s, rg, kPhAll);
-    join_side(env, gm.index, s);
+    const Side sd = rg.count >= 0 ? range_side(env, gm, s) : game_side(env, gm.index);
+    launch_phases(env, gm, start, s, sd, rg, kPhAll);
+    join_side(sd, s);
 }
 
 // Every game: a one-game env on the caller's stream; several games each on their own stream pair, concurrently,
@@ -58,11 +72,12 @@ void launch_all(Env& env, bool start, cudaStream_t s) {
     ck(cudaEventRecord(env.ev_begin, s), "fork");
     for (const Game& gm : env.games) ck(cudaStreamWaitEvent(env.gmain[gm.index], env.ev_begin, 0), "fork");
     for (u32 ph : {kPhFrames, kPhFinish, kPhRestart, kPhRender})
-        for (const Game& gm : env.games) launch_phases(env, gm, start, env.gmain[gm.index], Range{}, ph);
+        for (const Game& gm : env.games)
+            launch_phases(env, gm, start, env.gmain[gm.index], game_side(env, gm.index), Range{}, ph);
     for (const Game& gm : env.games) {
         ck(cudaEventRecord(env.gmain_done[gm.index], env.gmain[gm.index]), "join");
         ck(cudaStreamWaitEvent(s, env.gmain_done[gm.index], 0), "join");
-        join_side(env, gm.index, s);
+        join_side(game_side(env, gm.index), s);
     }
 }
 
@@ -160,7 +175,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         A.fault = M.allocn<u32>(N, true);
         A.resetting = M.allocn<u8>(N);
         A.list = M.allocn<u32>(N);                                    // per game: its slice [game_e0, game_e0 + n)
-        A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1);
+        A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1 + N);   // per game, then per range start
         {
             std::vector<u32> init(N, 0xFFFFFFFFu);
             ck(cudaMemcpy(A.episode, init.data(), N * 4, cudaMemcpyHostToDevice), "episode init");
@@ -237,6 +252,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         ck(cudaEventCreateWithFlags(&env->ev_begin, cudaEventDisableTiming), "event");
         int least = 0, greatest = 0;
         ck(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+        env->side_priority = greatest;
         for (std::size_t gi = 0; gi < env->games.size(); ++gi) {
             cudaStream_t q = nullptr;
             cudaEvent_t e = nullptr;

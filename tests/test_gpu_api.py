@@ -56,6 +56,40 @@ def test_step_game_and_range_match_step(gpu_lib_path):
 
 
 @pytest.mark.gpu
+def test_step_range_on_concurrent_streams_matches_step(gpu_lib_path):
+    """Parts of one game stepped at the same time on different streams (the reference's rollout_split units,
+    rl/train.py:569-652) equal the plain step, through episode ends (restarts listed per part)."""
+    counts = {'synth00': 256, 'synth03': 128}
+    mk = lambda: RlEnv(counts, device='cuda', lib_path=gpu_lib_path, seed=9, sticky=True, idle_max=30, dropout=True)  # noqa: E731
+    a, c = mk(), mk()
+    a.start(); c.start()
+    streams = [torch.cuda.Stream() for _ in range(3)]
+    parts = []   # (game, start, count): each game in uneven parts, spread over the streams
+    for gi, s in enumerate(c.game_slices()):
+        n = s.stop - s.start
+        cuts = [0, n // 4, n // 2 + 8, n]
+        parts += [(gi, cuts[j], cuts[j + 1] - cuts[j]) for j in range(3)]
+    gen = torch.Generator().manual_seed(1)
+    ends = 0
+    for t in range(150):
+        act = random_legal(a.masks.cpu(), gen).cuda()
+        a.actions.copy_(act); c.actions.copy_(act)
+        a.step()
+        main = torch.cuda.current_stream()
+        for j, (gi, st, n) in enumerate(parts):
+            q = streams[j % len(streams)]
+            q.wait_stream(main)
+            with torch.cuda.stream(q):
+                c.step_range(gi, st, n, c.obs, c.emph)
+        for q in streams:
+            main.wait_stream(q)
+        torch.cuda.synchronize()
+        _same(a, c, t, 'step_range on concurrent streams')
+        ends += int(a.done.sum())
+    assert ends > 0   # restarts were exercised (12 episode ends with these seeds)
+
+
+@pytest.mark.gpu
 def test_fused_pack6_matches_rl_pack6_and_formula(gpu_lib_path):
     a, b = _env(gpu_lib_path), _env(gpu_lib_path)
     packed = torch.zeros(b.n, 4, 224, 180, dtype=torch.uint8, device='cuda')
