@@ -52,9 +52,11 @@ def parse():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--envs', type=int, default=None, help='envs per GPU (default 8192; 32768 for --workload config3)')
-    ap.add_argument('--workload', default='config2', choices=['config2', 'config3', 'stem'],
+    ap.add_argument('--workload', default='config2', choices=['config2', 'config3', 'config5', 'stem'],
                     help='config2: synthetic NROM (the headline); config3: 12 synthetic games on 4 boards with level '
-                         'starts; stem: the policy input stem (colour lookup + 2x2 conv, tcgen05) on packed pictures')
+                         'starts; config5: config 2 with the reference policy network choosing the moves; stem: the '
+                         'policy input stem (colour lookup + 2x2 conv, tcgen05) on packed pictures')
+    ap.add_argument('--units', type=int, default=4, help='config5: parts of the envs, each on its own stream')
     ap.add_argument('--seed', type=int, default=1)
     ap.add_argument('--age', type=int, default=1024,
                     help='untimed decisions before the warm-up, so that episode restarts run at their steady-state rate')
@@ -261,6 +263,177 @@ def stem_arm(args):
                               peak_source=f'{kind} (MEASURED_PEAKS.json hbm_gbs)' if kind == 'measured' else 'fallback'),
                 gpu_launches=K, clocks=clk.summary(), cpu_baseline=None,
                 checksum=[round(float(x), 5) for x in m[:4]])
+
+
+def config5_arm(args):
+    """E envs per GPU of config 2's cart with the reference's policy network (random init, bf16)
+    choosing every move, as the reference's per-unit rollout (rl/train.py:569-652): the envs are split into --units
+    parts, each running its own chain (stem + CNN + MLP + GRU + ordered heads -> moves -> its env step_range) on its
+    own CUDA stream, so one part's inference overlaps another's emulation. decisions/s.
+      value  the rollout with everything on the device (moves sampled on the device: no host inputs).
+      e2e    the same, plus each decision's rollout storage read back to pinned host memory on the part's stream:
+             packed pictures, emphasis, reward, done, log-probability.
+    Also measured alone in the same process: the env (plain step, random moves) and the policy (one unit)."""
+    import torch
+    import torch.distributed as dist
+    from rlenv import RlEnv, default_lib
+    from shard import rank_seed
+    from policy import Policy
+    import build as gbuild
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if not default_lib().exists():
+        gbuild.build()
+    E, K, W, U = args.envs, args.steps, args.warmup, max(1, args.units)
+    # the reference rollout's settings (rl/train.py:342-345): cuDNN picks its fastest algorithms, TF32 allowed
+    torch.backends.cudnn.benchmark = True
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    env = RlEnv({GAME: E}, device=dev, seed=rank_seed(args.seed, rank), sticky=True, idle_max=30, dropout=True)
+    packed = torch.empty(E, 4, 224, 180, dtype=torch.uint8, device=dev)
+    env.bind_obs_pack6(packed)
+    env.start()
+    g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    for _ in range(args.age):   # spread the first episodes' ends to the steady-state restart rate
+        env.actions.copy_(torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        env.step()
+    torch.manual_seed(args.seed)
+    palette = torch.rand(512, 3, generator=torch.Generator().manual_seed(args.seed))   # a seeded stand-in colour table
+    pol = Policy(palette).to(dev).to(memory_format=torch.channels_last).eval()
+    n_params = sum(p.numel() for p in pol.parameters())
+    cuts = [E * j // U for j in range(U + 1)]
+    units = [slice(cuts[j], cuts[j + 1]) for j in range(U)]
+    streams = [torch.cuda.Stream(dev) for _ in range(U)]
+    gens = [torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank * 16 + j) for j in range(U)]
+    h = torch.zeros(E, 512, device=dev)
+    prev = [torch.zeros(E, dtype=torch.long, device=dev) for _ in range(5)]
+    starts = torch.ones(E, dtype=torch.bool, device=dev)
+    ends = torch.zeros(U, dtype=torch.float64, device=dev)
+    R = max(2, args.ring)
+    row = PACKED_ROW + EMPH_ROW + 4 + 1 + 4
+    ring = torch.empty((R, E * row), dtype=torch.uint8).pin_memory()
+
+    def unit_step(j, t, store):
+        sl, n = units[j], units[j].stop - units[j].start
+        mv, parts, logp, _, hj = pol.decide(packed[sl], env.emph[sl], env.timeline[sl], [p[sl] for p in prev],
+                                            env.masks[sl], h[sl], starts[sl], gens[j])
+        h[sl] = hj
+        env.actions[sl] = mv
+        env.step_range(0, sl.start, n, env.obs, env.emph)
+        done = env.done[sl].bool()
+        starts[sl] = done
+        for k in range(5):
+            prev[k][sl] = parts[k] * (~done).long()
+        ends[j] += done.sum()
+        if store:   # this part's rollout rows into the pinned ring slot of step t
+            slot = ring[t % R]
+            a = sl.start
+            slot[a * PACKED_ROW:sl.stop * PACKED_ROW].copy_(packed[sl].view(-1), non_blocking=True)
+            b0 = E * PACKED_ROW
+            slot[b0 + a * EMPH_ROW:b0 + sl.stop * EMPH_ROW].copy_(env.emph[sl].view(-1), non_blocking=True)
+            b1 = b0 + E * EMPH_ROW
+            slot[b1 + a * 4:b1 + sl.stop * 4].copy_(env.reward[sl].view(torch.uint8), non_blocking=True)
+            b2 = b1 + E * 4
+            slot[b2 + a:b2 + sl.stop].copy_(env.done[sl], non_blocking=True)
+            b3 = b2 + E
+            slot[b3 + a * 4:b3 + sl.stop * 4].copy_(logp.view(torch.uint8), non_blocking=True)
+
+    def rollout(steps, t0, store):
+        main = torch.cuda.current_stream(dev)
+        for q in streams:
+            q.wait_stream(main)
+        for t in range(steps):
+            for j in range(U):
+                with torch.cuda.stream(streams[j]):
+                    unit_step(j, t0 + t, store)
+        for q in streams:
+            main.wait_stream(q)
+
+    def timed(fn):
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    rollout(W, 0, False)
+    env.set_timing(True)
+    env.timing(reset=True)
+    clk = ClockSampler(local)
+    with clk:
+        ms = timed(lambda: rollout(K, 0, False))
+    tm = env.timing(reset=True)
+    env.set_timing(False)
+    rollout(1, 0, True)   # warm the copy path
+    ms_e2e = timed(lambda: rollout(K, 0, True))
+
+    # the two halves alone, same process: the env with random moves, the policy on all envs as one unit
+    acts = torch.randint(0, 81, (K, E), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+
+    def env_only():
+        for t in range(K):
+            env.actions.copy_(acts[t])
+            env.step()
+
+    def policy_only():
+        hh = h.clone()
+        for _ in range(K):
+            pol.decide(packed, env.emph, env.timeline, prev, env.masks, hh, starts, gens[0])
+
+    ms_env = timed(env_only)
+    ms_pol = timed(policy_only)
+    tot = ends.sum()
+    if world > 1:
+        dist.all_reduce(tot)
+    res = None
+    if rank == 0:
+        value = K * E * world / (ms / 1e3)
+        peak, peak_kind = measured_peaks()
+        render_ms = tm['ms']['render'] / K
+        alg_bytes = E * 4 * (PACKED_ROW // 4 + 224 + 2048 + 256 + 64)
+        achieved = alg_bytes / (render_ms / 1e3) / 1e9
+        res = dict(
+            metric=METRIC, value=round(value, 1), unit=UNIT, n_gpus=world, steps=K, warmup=W,
+            ms_per_step=round(ms / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8+bf16',
+            data='synthetic (seeded NROM cart synth00; random-init policy, seeded stand-in palette)',
+            config=dict(workload=f'config 5: config 2 cart, {E} envs/GPU + the reference policy network '
+                                 f'({n_params} parameters, bf16) choosing every move, {U} parts on their own streams',
+                        envs_per_gpu=E, units=U, policy_parameters=n_params, frames_per_decision=4,
+                        parallelism=f'dp{world} (env + policy shards)', aged_decisions=args.age,
+                        inputs_exceed_l2=True),
+            frames_per_s=round(4 * value, 1),
+            e2e=dict(value=round(K * E * world / (ms_e2e / 1e3), 1), unit=UNIT, h2d_bytes_per_step=0,
+                     d2h_bytes_per_step=E * row,
+                     note='moves come from the policy on the device; each decision\'s packed pictures, emphasis, '
+                          'reward, done and log-probability go to a pinned host ring on the part\'s stream'),
+            alone=dict(env_ms_per_step=round(ms_env / K, 4), policy_ms_per_step=round(ms_pol / K, 4),
+                       env_decisions_per_s=round(K * E / (ms_env / 1e3), 1),
+                       policy_decisions_per_s=round(K * E / (ms_pol / 1e3), 1)),
+            roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
+                          traffic=None, kernel='k_render',
+                          peak_source=f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured' else 'fallback',
+                          render_ms_per_decision=round(render_ms, 4)),
+            kernel_ms_per_step={k: round(v / K, 4) for k, v in tm['ms'].items()},
+            gpu_launches=tm['total_launches'] + K * U,   # env kernels + one stem launch per part and decision
+            clocks=clk.summary(), episodes_ended=int(tot.item()), cpu_baseline=None)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
 
 
 def gpu_arm(args):
@@ -497,6 +670,11 @@ def main():
         return
     if args.workload == 'stem':
         print(json.dumps(stem_arm(args)), flush=True)
+        return
+    if args.workload == 'config5':
+        res = config5_arm(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
