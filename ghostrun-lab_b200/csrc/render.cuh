@@ -620,6 +620,8 @@ struct Renderer {
         // Lines that can show a sprite: one at y is found by the evaluation at the end of lines y..y+15 (height <= 16)
         // and drawn on lines y+1..y+16. A superset; iterations whose 4 lines have none skip the sprite work.
         u32* may = reinterpret_cast<u32*>(W.emph);   // 8 words: bit l of the 256-line mask
+        u8* vis = W.emph + 32;                       // OAM indices of the sprites that can show, in OAM order
+        u32 nv;
         {
             auto span = [](u32 sp, u32 base) -> u32 {
                 const int lo = static_cast<int>(sp & 0xFFu) + 1 - static_cast<int>(base);
@@ -633,48 +635,48 @@ struct Renderer {
                 const u32 m = __reduce_or_sync(0xFFFFFFFFu, span(spA, 32u * b) | span(spB, 32u * b));
                 if (lane == 0) may[b] = m;
             }
+            // a sprite at y is evaluated on lines y..y+15 at most; the evaluations that draw are on lines 7..230
+            const bool va = (spA & 0xFFu) <= 230u, vb = (spB & 0xFFu) <= 230u;
+            const u32 ba = __ballot_sync(0xFFFFFFFFu, va), bb = __ballot_sync(0xFFFFFFFFu, vb);
+            if (va) vis[__popc(ba & lt)] = static_cast<u8>(lane);
+            if (vb) vis[__popc(ba) + __popc(bb & lt)] = static_cast<u8>(lane + 32u);
+            nv = __popc(ba) + __popc(bb);
             __syncwarp();
         }
         for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
-            // ---- sprites of lines l0..l0+3 (fetched at the end of the line above each)
+            // ---- sprites of lines l0..l0+3: lane group g evaluates the end of line l0 + g - 1 (the fetch its line
+            // draws) over the visible sprites in OAM order, 8 candidates per round; the first 8 in range are fetched
             u32 nsp = 0;   // this lane group's sprite count
             const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                if (!any) break;
-                const int e = l0 + k - 1;
+            if (any) {
+                const int e = l0 + static_cast<int>(g) - 1;
                 const uint2 re = F.rec[e];
                 const u32 ctrl = ((re.x >> 18) & 7u) << 3;
-                u32 n = 0;
-                if ((re.y & 0x18u) && (re.y & (1u << 16))) {
-                    const u32 hgt = (ctrl & 0x20u) ? 16u : 8u;
-                    const bool in0 = static_cast<u32>(e - static_cast<int>(spA & 0xFFu)) < hgt;
-                    const bool in1 = static_cast<u32>(e - static_cast<int>(spB & 0xFFu)) < hgt;
-                    const u32 b0 = __ballot_sync(0xFFFFFFFFu, in0), b1 = __ballot_sync(0xFFFFFFFFu, in1);
-                    if (b0 | b1) {
-                        const u32* pages = F.chr[(re.y >> 12) & 3u];
-                        const u32 vofs = ((ctrl & 0x08u) && !(ctrl & 0x20u)) ? 0x1000u : 0u;
-                        const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
-                        n = min(__popc(b0) + __popc(b1), 8);
-#pragma unroll
-                        for (int half = 0; half < 2; ++half) {
-                            const bool in = half ? in1 : in0;
-                            const u32 rk = half ? r1 : r0;
-                            if (in && rk < 8) {
-                                const u32 spw = half ? spB : spA;
-                                const u32 tile = (spw >> 8) & 0xFFu, attr = (spw >> 16) & 0xFFu, xx = spw >> 24;
-                                const u32 t = static_cast<u32>(e - static_cast<int>(spw & 0xFFu));
-                                u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
-                                if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (ctrl & 0x20u) >> 1; vadr -= t & 8u; }
-                                else { vadr += t; vadr += t & 8u; }
-                                u32 cw = chr_sel(pages, vadr & 0x1FFFu);
-                                if (attr & 0x40u) cw = nib_reverse(cw);
-                                sbuf[k * 8 + rk] = make_uint2(cw, (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8));
-                            }
-                        }
+                const bool on = (re.y & 0x18u) && (re.y & (1u << 16));
+                const u32 hgt = (ctrl & 0x20u) ? 16u : 8u;
+                const u32* pages = F.chr[(re.y >> 12) & 3u];
+                const u32 vofs = ((ctrl & 0x08u) && !(ctrl & 0x20u)) ? 0x1000u : 0u;
+                for (u32 c0 = 0; c0 < nv; c0 += 8) {   // warp-uniform trip count
+                    const u32 c = c0 + j;
+                    const u32 si = c < nv ? vis[c] : 0u;
+                    const u32 wa = __shfl_sync(0xFFFFFFFFu, spA, si & 31u), wb = __shfl_sync(0xFFFFFFFFu, spB, si & 31u);
+                    const u32 spw = si >= 32u ? wb : wa;
+                    const u32 t = static_cast<u32>(e - static_cast<int>(spw & 0xFFu));
+                    const bool in = on && c < nv && t < hgt;
+                    const u32 gb = (__ballot_sync(0xFFFFFFFFu, in) >> (8u * g)) & 0xFFu;
+                    const u32 rk = nsp + __popc(gb & ((1u << j) - 1u));
+                    if (in && rk < 8) {
+                        const u32 tile = (spw >> 8) & 0xFFu, attr = (spw >> 16) & 0xFFu, xx = spw >> 24;
+                        u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+                        if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (ctrl & 0x20u) >> 1; vadr -= t & 8u; }
+                        else { vadr += t; vadr += t & 8u; }
+                        u32 cw = chr_sel(pages, vadr & 0x1FFFu);
+                        if (attr & 0x40u) cw = nib_reverse(cw);
+                        sbuf[g * 8 + rk] = make_uint2(cw, (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8));
                     }
+                    nsp += __popc(gb);
                 }
-                if (g == static_cast<u32>(k)) nsp = n;
+                nsp = min(nsp, 8u);
             }
             __syncwarp();
             // ---- background of line l (this lane group's), 32 pixels per lane
