@@ -706,7 +706,7 @@ __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_co
         const u32 ge = R.list ? R.list[k] : R.e0 + k;
         if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
         if (R.skip && R.skip[ge]) continue;   // restarting: the restart pass draws its new episode's first frames
-        if (lane < R.frames) rd.walk(ge, lane, RW.fw[lane]);
+        rd.walk_group(ge, RW.fw, R.frames);
         __syncwarp();
         for (u32 f = 0; f < R.frames; ++f) {
             u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)

@@ -438,10 +438,9 @@ struct Renderer {
     }
 
     // ================================================================ two-phase path
-    // ---- phase 1 (one lane per frame): replay the frame log's register state line by line (the same order of event
-    // application, v increments and line ends as draw / end_of_line) and record it; pixels, sprites and sprite-0
-    // bookkeeping are left to phase 2 (sprite-0 state only changes what a mid-line write sees, and such frames take
-    // the sequential path).
+    // ---- phase 1: replay the frame log's register state line by line (the same order of event application, v
+    // increments and line ends as draw / end_of_line) and record it; pixels, sprites and sprite-0 bookkeeping are left
+    // to phase 2 (sprite-0 state only changes what a mid-line write sees, and such frames take the sequential path).
     struct Walk {
         u32 ctrl, mask, x, v, t, mir, pv, cv, cursor, count, seq;
         bool pused, cused;
@@ -503,10 +502,10 @@ struct Renderer {
         ++w.cursor;
         w.next_t = walk_time(w, w.cursor);
     }
-    __device__ void walk(u32 ge, u32 f, FrameWalk& F) const {
+    // The header state, the frame's first tables and the events before the first line (group leader).
+    __device__ void walk_begin(u32 ge, u32 f, FrameWalk& F, Walk& w) const {
         const u64 sl = static_cast<u64>(ge) * 4 + f;
         const u32* hh = A.st.log + (static_cast<u64>(ge) * kLogBanks + A.st.slot_bank[sl]) * kLogBankWords;
-        Walk w;
         w.ev = hh + kLogHdr;
         w.count = min(hh[0] & ~kLogOverflow, kLogEv);
         w.kook = (hh[15] & kLogKook) ? 1 : 0;
@@ -522,25 +521,90 @@ struct Renderer {
         w.next_t = walk_time(w, 0);
         while (w.next_t < -16 && !w.seq) walk_apply(w, F, false);
         if (w.mask & 0x18u) w.v = w.t;
-        for (int l = 0; l < kObsY0 + kObsH && !w.seq; ++l) {
-            const int start = l * 341 - 16;
-            if (w.next_t < start + 272) { w.seq = 1; break; }   // a write inside the drawn part of the line
-            if (!w.pused) { derive(F, w.pv); w.pused = true; }
-            w.cused = true;
-            const u32 rx = w.v | (w.x << 15) | (((w.ctrl >> 3) & 7u) << 18) | ((w.mir & 0xFu) << 21);
-            const u32 ry = w.mask | (w.pv << 8) | (w.cv << 12);
-            const u32 fetch_mask = w.mask;
-            if (w.mask & 0x18u) w.v = v_inc_y(v_inc_x_n(w.v, 34));
-            while (w.next_t < start + 278 && !w.seq) walk_apply(w, F, true);
-            if (w.mask & 0x18u) w.v = (w.v & 0xFBE0u) | (w.t & 0x041Fu);
-            while (w.next_t < start + 341 && !w.seq) walk_apply(w, F, true);
-            if (!w.pused) { derive(F, w.pv); w.pused = true; }
-            // sprites switched on during the hblank of a line drawn with rendering off would show an older line's
-            // sprite fetch (the buffer's count is stale): the sequential path keeps that
-            if (!(fetch_mask & 0x18u) && (w.mask & 0x10u)) w.seq = 1;
-            F.rec[l] = make_uint2(rx, ry | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20));
+    }
+    // Line l with its events (group leader): the line-by-line replay order of draw / end_of_line.
+    __device__ void walk_line(Walk& w, FrameWalk& F, int l) const {
+        const int start = l * 341 - 16;
+        if (w.next_t < start + 272) { w.seq = 1; return; }   // a write inside the drawn part of the line
+        if (!w.pused) { derive(F, w.pv); w.pused = true; }
+        w.cused = true;
+        const u32 rx = w.v | (w.x << 15) | (((w.ctrl >> 3) & 7u) << 18) | ((w.mir & 0xFu) << 21);
+        const u32 ry = w.mask | (w.pv << 8) | (w.cv << 12);
+        const u32 fetch_mask = w.mask;
+        if (w.mask & 0x18u) w.v = v_inc_y(v_inc_x_n(w.v, 34));
+        while (w.next_t < start + 278 && !w.seq) walk_apply(w, F, true);
+        if (w.mask & 0x18u) w.v = (w.v & 0xFBE0u) | (w.t & 0x041Fu);
+        while (w.next_t < start + 341 && !w.seq) walk_apply(w, F, true);
+        if (!w.pused) { derive(F, w.pv); w.pused = true; }
+        // sprites switched on during the hblank of a line drawn with rendering off would show an older line's
+        // sprite fetch (the buffer's count is stale): the sequential path keeps that
+        if (!(fetch_mask & 0x18u) && (w.mask & 0x10u)) w.seq = 1;
+        F.rec[l] = make_uint2(rx, ry | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20));
+    }
+    // v after k line ends without events (k <= 240): the vertical increment k times (coarse Y 29 -> 0 toggles the
+    // vertical nametable, 31 -> 0 does not), the horizontal bits from t (th) once k >= 1; rendering off: v stays.
+    __device__ __forceinline__ static u32 v_after_lines(u32 v, u32 k, u32 th, bool ren) {
+        if (k == 0 || !ren) return v;
+        u32 y = ((v >> 5) & 31u) * 8u + ((v >> 12) & 7u);
+        u32 nty = v & 0x800u;
+        y += k;
+        if (y - k < 240u) {
+            if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
+        } else if (y >= 256u) {
+            y -= 256u;
+            if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
         }
-        F.seq = w.seq;
+        return th | nty | ((y & 7u) << 12) | ((y >> 3) << 5);
+    }
+    // ---- phase 1 (8 lanes per frame, lane group f = lane / 8 walks frame f): the group leader replays the frame
+    // log's events; every stretch of lines without events is recorded by the 8 lanes of the group at once, v from
+    // the closed form above (the record of such a line is its start state, unchanged through the line).
+    __device__ void walk_group(u32 ge, FrameWalk* FW, u32 frames) const {
+        constexpr int kLines = kObsY0 + kObsH;
+        const u32 f = lane >> 3, sub = lane & 7u, lead = lane & ~7u;
+        const bool active = f < frames;
+        FrameWalk& F = FW[active ? f : 0u];
+        Walk w;
+        int l = 0;
+        bool done = !active;
+        if (sub == 0 && active) walk_begin(ge, f, F, w);
+        for (;;) {
+            int run = 0;
+            u32 v = 0, xc = 0, ry = 0, th = 0, ren = 0;
+            if (sub == 0 && !done) {
+                if (w.seq) {
+                    done = true;
+                } else {
+                    if (!w.pused) { derive(F, w.pv); w.pused = true; }
+                    w.cused = true;
+                    // the next event is applied in line (next_t + 16) / 341: the lines before it have none
+                    const int lev = w.next_t >= kLines * 341 ? kLines : (w.next_t + 16) / 341;
+                    run = max(0, min(lev, kLines) - l);
+                    v = w.v;
+                    xc = (w.x << 15) | (((w.ctrl >> 3) & 7u) << 18) | ((w.mir & 0xFu) << 21);
+                    ry = w.mask | (w.pv << 8) | (w.cv << 12) | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20);
+                    th = w.t & 0x041Fu;
+                    ren = (w.mask & 0x18u) ? 1u : 0u;
+                }
+            }
+            run = __shfl_sync(0xFFFFFFFFu, run, lead);
+            const int l0 = __shfl_sync(0xFFFFFFFFu, l, lead);
+            v = __shfl_sync(0xFFFFFFFFu, v, lead);
+            xc = __shfl_sync(0xFFFFFFFFu, xc, lead);
+            ry = __shfl_sync(0xFFFFFFFFu, ry, lead);
+            th = __shfl_sync(0xFFFFFFFFu, th, lead);
+            ren = __shfl_sync(0xFFFFFFFFu, ren, lead);
+            for (int k = static_cast<int>(sub); k < run; k += 8)
+                F.rec[l0 + k] = make_uint2(v_after_lines(v, static_cast<u32>(k), th, ren != 0) | xc, ry);
+            if (sub == 0 && !done) {
+                w.v = v_after_lines(w.v, static_cast<u32>(run), th, ren != 0);
+                l += run;
+                if (l < kLines) walk_line(w, F, l++);
+                if (l >= kLines || w.seq) done = true;
+            }
+            if (__all_sync(0xFFFFFFFFu, __shfl_sync(0xFFFFFFFFu, done ? 1u : 0u, lead) != 0u)) break;
+        }
+        if (sub == 0 && active) F.seq = w.seq;
     }
 
     // One line's background fetch from a record (v, control, page map given).
