@@ -275,6 +275,7 @@ struct EnvArgs {
     i32* ep_idle;
     u32* fault;
     u8* resetting;
+    u8* render_seq;     // [N, 4] frames left to the sequential renderer by the last render pass
     // restart list
     u32* list;
     u32* list_count;
@@ -677,45 +678,83 @@ static __global__ void __launch_bounds__(128) k_place_save(const __grid_constant
     }
 }
 
-// Warp per env: lanes 0-3 walk the env's 4 frame logs (phase 1), then the warp draws the frames from the walks, or
-// sequentially (Renderer::draw) a frame with a write inside a line's drawn part. Grid-stride over the envs of this
-// game slice (or the restart list).
+// Warp per (env, frame) of this game slice (or of the restart list), grid-stride: the warp walks the frame's log
+// (phase 1) and draws it from the walk (phase 2); a frame with a write inside a line's drawn part is flagged for
+// k_render_seq instead. The sequential renderer lives in its own kernel, so this one needs 96 registers instead
+// of 124; a frame per warp lets a short restart list spread over 4x as many warps.
 struct RenderWarp {
     RWarp w;
-    FrameWalk fw[kFramesPerDecision];
+    FrameWalk fw;
 };
 constexpr u32 kRenderWarps = 8;
 inline std::size_t render_smem(bool chrx_smem) {
     return 1024 + (chrx_smem ? 16384 : 0) + kRenderWarps * sizeof(RenderWarp);
 }
+inline std::size_t render_seq_smem(bool chrx_smem) {
+    return 1024 + (chrx_smem ? 16384 : 0) + kRenderWarps * sizeof(RWarp);
+}
+
+// Item k of a render launch: env item k / frames, frame k % frames; false when the env is not drawn by this pass.
+__device__ __forceinline__ bool render_item(const RenderArgs& R, u32 k, u32& ge, u32& f) {
+    const u32 ei = k / R.frames;
+    f = k - ei * R.frames;
+    ge = R.list ? R.list[ei] : R.e0 + ei;
+    if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) return false;
+    if (R.skip && R.skip[ge]) return false;   // restarting: the restart pass draws its new episode's first frames
+    return true;
+}
+
+template <u32 BOARD>
+__device__ __forceinline__ void render_setup(const RenderArgs& R, u8* smem, u32*& spread, u32*& chrx) {
+    spread = reinterpret_cast<u32*>(smem);                 // 1 KB
+    chrx = spread + 256;                                   // 16 KB when staged
+    for (u32 i = threadIdx.x; i < 256; i += blockDim.x) spread[i] = spread8(i);
+    if (R.chrx_smem) for (u32 i = threadIdx.x; i < 4096; i += blockDim.x) chrx[i] = R.cart.chrx[i];
+    __syncthreads();
+}
 
 template <u32 BOARD>
 __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_constant__ RenderArgs R) {
     extern __shared__ __align__(16) u8 smem[];
-    u32* spread = reinterpret_cast<u32*>(smem);                 // 1 KB
-    u32* chrx = spread + 256;                                   // 16 KB when staged
+    u32 *spread, *chrx;
+    render_setup<BOARD>(R, smem, spread, chrx);
     RenderWarp* warps = reinterpret_cast<RenderWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
-    for (u32 i = threadIdx.x; i < 256; i += blockDim.x) spread[i] = spread8(i);
-    if (R.chrx_smem) for (u32 i = threadIdx.x; i < 4096; i += blockDim.x) chrx[i] = R.cart.chrx[i];
-    __syncthreads();
     const u32 lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
     RenderWarp& RW = warps[wid];
     Renderer<BOARD> rd(R, lane, R.chrx_smem ? chrx : R.cart.chrx, spread, RW.w);
-    const u32 items = R.list ? *R.list_count : R.count;
+    const u32 items = (R.list ? *R.list_count : R.count) * R.frames;
     for (u32 k = blockIdx.x * kRenderWarps + wid; k < items; k += gridDim.x * kRenderWarps) {
-        const u32 ge = R.list ? R.list[k] : R.e0 + k;
-        if (R.list && (ge < R.e0 || ge >= R.e0 + R.count)) continue;
-        if (R.skip && R.skip[ge]) continue;   // restarting: the restart pass draws its new episode's first frames
-        rd.walk_group(ge, RW.fw, R.frames);
-        __syncwarp();
-        for (u32 f = 0; f < R.frames; ++f) {
-            u8* out = R.packed ? R.packed + (static_cast<u64>(ge) * 4 + f) * (kObsPixels / 4 * 3)
-                               : R.obs + (static_cast<u64>(ge) * 4 + f) * kObsPixels;
-            u8* eo = R.emph + (static_cast<u64>(ge) * 4 + f) * kObsH;
-            if (RW.fw[f].seq) rd.draw(ge, f, out, eo, R.packed != nullptr);
-            else rd.draw_fast(ge, f, RW.fw[f], out, eo, R.packed != nullptr);
-            __syncwarp();
+        u32 ge, f;
+        if (!render_item(R, k, ge, f)) continue;
+        rd.walk_frame(ge, f, RW.fw);
+        const u64 sl = static_cast<u64>(ge) * 4 + f;
+        if (lane == 0) R.seqf[sl] = RW.fw.seq ? 1u : 0u;
+        if (!RW.fw.seq) {
+            u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
+            rd.draw_fast(ge, f, RW.fw, out, R.emph + sl * kObsH, R.packed != nullptr);
         }
+        __syncwarp();
+    }
+}
+
+// The frames k_render flagged (same launch arguments, after it on the same stream): the sequential renderer.
+template <u32 BOARD>
+__global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render_seq(const __grid_constant__ RenderArgs R) {
+    extern __shared__ __align__(16) u8 smem[];
+    u32 *spread, *chrx;
+    render_setup<BOARD>(R, smem, spread, chrx);
+    RWarp* warps = reinterpret_cast<RWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
+    const u32 lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    Renderer<BOARD> rd(R, lane, R.chrx_smem ? chrx : R.cart.chrx, spread, warps[wid]);
+    const u32 items = (R.list ? *R.list_count : R.count) * R.frames;
+    for (u32 k = blockIdx.x * kRenderWarps + wid; k < items; k += gridDim.x * kRenderWarps) {
+        u32 ge, f;
+        if (!render_item(R, k, ge, f)) continue;
+        const u64 sl = static_cast<u64>(ge) * 4 + f;
+        if (!R.seqf[sl]) continue;
+        u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
+        rd.draw(ge, f, out, R.emph + sl * kObsH, R.packed != nullptr);
+        __syncwarp();
     }
 }
 

@@ -222,8 +222,8 @@ inline void check_launch(const char* what) {
 
 // One game slice's decision (or start) on the caller's stream `s`, with the restart work forked onto the env's
 // high-priority side stream so it overlaps the main render:
-//   s:    [list reset] k_frames -> k_finish --fork--> k_render (envs not restarting) ...... join (join_side)
-//   side:                                     k_restore -> [k_archive] -> k_frames(restart) -> k_render(restart)
+//   s:    [list reset] k_frames -> k_finish --fork--> k_render, k_render_seq (envs not restarting) .. join (join_side)
+//   side:                          k_restore -> [k_archive] -> k_frames(restart) -> k_render, k_render_seq (restart)
 // Games run on their own stream pairs, concurrently (launch_all).
 // k_finish decides the episode ends and lists the restarting envs; the main render leaves them out (their outputs
 // are the new episode's first frames, drawn by the restart pass), so the two branches touch disjoint envs. The level
@@ -256,11 +256,12 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     R.obs = A.obs;
     R.emph = A.emph;
     R.packed = A.packed;
+    R.seqf = A.render_seq;
     R.e0 = g.e0;
     R.count = n;
     R.frames = kFramesPerDecision;
     R.chrx_smem = gm.chrx_smem ? 1u : 0u;
-    const std::size_t smem = render_smem(gm.chrx_smem);
+    const std::size_t smem = render_smem(gm.chrx_smem), seq_smem = render_seq_smem(gm.chrx_smem);
     KTimer& T = *env.timer;
     if (phases & kPhFrames) {
         ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
@@ -281,11 +282,16 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     if ((phases & kPhRender) && !start && !A.no_render) {
         R.list = nullptr;
         R.skip = A.done;
-        const u32 blocks = std::min<u32>((n + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u);
+        const u32 items = n * R.frames;
+        const u32 blocks = std::min<u32>((items + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u);
         T.begin(kKRender, s);
         k_render<B><<<blocks, 32 * kRenderWarps, smem, s>>>(R);
         T.end(kKRender, s);
         check_launch("k_render");
+        T.begin(kKRender, s);
+        k_render_seq<B><<<std::min<u32>(blocks, 148u * 2u), 32 * kRenderWarps, seq_smem, s>>>(R);
+        T.end(kKRender, s);
+        check_launch("k_render_seq");
     }
     if (!(phases & kPhRestart)) return;
     ck(cudaStreamWaitEvent(side, sd.fork, 0), "fork");
@@ -315,11 +321,15 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
         R.list = A.list;
         R.list_count = A.list_count;
         R.skip = nullptr;
-        const u32 blocks = start ? std::min<u32>((n + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u) : 148u;
+        const u32 blocks = start ? std::min<u32>((n * R.frames + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u) : 148u;
         T.begin(kKRestartRender, side);
         k_render<B><<<blocks, 32 * kRenderWarps, smem, side>>>(R);
         T.end(kKRestartRender, side);
         check_launch("k_render restart");
+        T.begin(kKRestartRender, side);
+        k_render_seq<B><<<std::min<u32>(blocks, 148u * 2u), 32 * kRenderWarps, seq_smem, side>>>(R);
+        T.end(kKRestartRender, side);
+        check_launch("k_render_seq restart");
     }
 }
 
@@ -345,6 +355,8 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
        "smem attr");
     ck(cudaFuncSetAttribute(k_chain<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kFramesSmem + kPrgStageMax)),
        "smem attr");
+    ck(cudaFuncSetAttribute(k_render_seq<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(render_seq_smem(gm.chrx_smem))), "smem attr");
     ck(cudaFuncSetAttribute(k_render<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(render_smem(gm.chrx_smem))),
        "smem attr");
     k_boot<B><<<1, 32, frames_smem(gm.g.cart)>>>(gm.g, env.A.st, slot, dpads, static_cast<u32>(npads), idle, recs, fault);

@@ -66,6 +66,7 @@ struct RenderArgs {
     const u32* list;     // env list (restart pass), nullptr = all envs [e0, e0 + count)
     const u32* list_count;
     const u8* skip;      // envs to leave out (non-zero), nullptr = none
+    u8* seqf;            // [N, 4]: 1 = the frame is left to the sequential renderer (k_render_seq)
     u32 e0, count;       // global env range of this launch (game slice)
     u32 frames;          // frames per env to draw (4)
     u32 chrx_smem;       // 1: the cart's pattern table is staged in shared memory (8 KB CHR ROM boards)
@@ -556,22 +557,19 @@ struct Renderer {
         }
         return th | nty | ((y & 7u) << 12) | ((y >> 3) << 5);
     }
-    // ---- phase 1 (8 lanes per frame, lane group f = lane / 8 walks frame f): the group leader replays the frame
-    // log's events; every stretch of lines without events is recorded by the 8 lanes of the group at once, v from
-    // the closed form above (the record of such a line is its start state, unchanged through the line).
-    __device__ void walk_group(u32 ge, FrameWalk* FW, u32 frames) const {
+    // ---- phase 1 for frame f of env ge (the whole warp): lane 0 replays the frame log's events; every stretch of
+    // lines without events is recorded by the 32 lanes at once, v from the closed form above (the record of such a
+    // line is its start state, unchanged through the line).
+    __device__ void walk_frame(u32 ge, u32 f, FrameWalk& F) const {
         constexpr int kLines = kObsY0 + kObsH;
-        const u32 f = lane >> 3, sub = lane & 7u, lead = lane & ~7u;
-        const bool active = f < frames;
-        FrameWalk& F = FW[active ? f : 0u];
         Walk w;
         int l = 0;
-        bool done = !active;
-        if (sub == 0 && active) walk_begin(ge, f, F, w);
+        bool done = false;
+        if (lane == 0) walk_begin(ge, f, F, w);
         for (;;) {
             int run = 0;
             u32 v = 0, xc = 0, ry = 0, th = 0, ren = 0;
-            if (sub == 0 && !done) {
+            if (lane == 0 && !done) {
                 if (w.seq) {
                     done = true;
                 } else {
@@ -587,24 +585,25 @@ struct Renderer {
                     ren = (w.mask & 0x18u) ? 1u : 0u;
                 }
             }
-            run = __shfl_sync(0xFFFFFFFFu, run, lead);
-            const int l0 = __shfl_sync(0xFFFFFFFFu, l, lead);
-            v = __shfl_sync(0xFFFFFFFFu, v, lead);
-            xc = __shfl_sync(0xFFFFFFFFu, xc, lead);
-            ry = __shfl_sync(0xFFFFFFFFu, ry, lead);
-            th = __shfl_sync(0xFFFFFFFFu, th, lead);
-            ren = __shfl_sync(0xFFFFFFFFu, ren, lead);
-            for (int k = static_cast<int>(sub); k < run; k += 8)
+            run = __shfl_sync(0xFFFFFFFFu, run, 0);
+            const int l0 = __shfl_sync(0xFFFFFFFFu, l, 0);
+            v = __shfl_sync(0xFFFFFFFFu, v, 0);
+            xc = __shfl_sync(0xFFFFFFFFu, xc, 0);
+            ry = __shfl_sync(0xFFFFFFFFu, ry, 0);
+            th = __shfl_sync(0xFFFFFFFFu, th, 0);
+            ren = __shfl_sync(0xFFFFFFFFu, ren, 0);
+            for (int k = static_cast<int>(lane); k < run; k += 32)
                 F.rec[l0 + k] = make_uint2(v_after_lines(v, static_cast<u32>(k), th, ren != 0) | xc, ry);
-            if (sub == 0 && !done) {
+            if (lane == 0 && !done) {
                 w.v = v_after_lines(w.v, static_cast<u32>(run), th, ren != 0);
                 l += run;
                 if (l < kLines) walk_line(w, F, l++);
                 if (l >= kLines || w.seq) done = true;
             }
-            if (__all_sync(0xFFFFFFFFu, __shfl_sync(0xFFFFFFFFu, done ? 1u : 0u, lead) != 0u)) break;
+            if (__shfl_sync(0xFFFFFFFFu, done ? 1u : 0u, 0) != 0u) break;
         }
-        if (sub == 0 && active) F.seq = w.seq;
+        if (lane == 0) F.seq = w.seq;
+        __syncwarp();
     }
 
     // One line's background fetch from a record (v, control, page map given).

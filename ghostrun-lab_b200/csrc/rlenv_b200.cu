@@ -174,6 +174,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         A.ep_idle = M.allocn<i32>(N, true);
         A.fault = M.allocn<u32>(N, true);
         A.resetting = M.allocn<u8>(N);
+        A.render_seq = M.allocn<u8>(static_cast<std::size_t>(N) * kFramesPerDecision);   // transient: not saved
         A.list = M.allocn<u32>(N);                                    // per game: its slice [game_e0, game_e0 + n)
         A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1 + N);   // per game, then per range start
         {
