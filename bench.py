@@ -48,7 +48,7 @@ EMPH_ROW = 4 * 224
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=100)
+    ap.add_argument('--steps', type=int, default=300)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--envs', type=int, default=None, help='envs per GPU (default 8192; 32768 for --workload config3)')
@@ -136,15 +136,48 @@ def cpu_model():
 # ------------------------------------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed region runs: NVML read-only queries every
+    10 ms from a thread (a timed region of a few tens of milliseconds still gets samples), else nvidia-smi every
+    200 ms. `index` is the CUDA device; NVML finds the same GPU by its PCI bus id."""
     Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
          'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
          'clocks_event_reasons.sw_power_cap')
+    # NVML clock-event reason bits
+    BITS = {'sw_power_cap': 0x4, 'hw_slowdown': 0x8, 'sw_thermal_slowdown': 0x20, 'hw_thermal_slowdown': 0x40,
+            'hw_power_brake_slowdown': 0x80}
 
     def __init__(self, index):
         self.index, self.proc, self.lines = index, None, []
+        self.samples, self.stop, self.nvml = [], threading.Event(), None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.index)
+        bus = f'{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0'
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+
+    def _poll(self):
+        nv, h = self.nvml
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((sm, mx, rs))
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.Q}', '--format=csv,noheader,nounits',
                                           '-i', str(self.index), '-lms', '200'], stdout=subprocess.PIPE,
@@ -160,6 +193,10 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self.stop.set()
+            self.t.join(timeout=2)
+            return
         if self.proc:
             self.proc.terminate()
             try:
@@ -170,21 +207,29 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for line in self.lines:
-            f = [x.strip() for x in line.split(',')]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1])); mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith('active'):
-                    reasons.add(n)
+        if self.nvml is not None:
+            for a, b, rs in self.samples:
+                sm.append(float(a)); mx.append(float(b))
+                reasons.update(n for n, bit in self.BITS.items() if rs & bit)
+            src = 'nvml 10 ms'
+        else:
+            names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+            for line in self.lines:
+                f = [x.strip() for x in line.split(',')]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1])); mx.append(float(f[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower().startswith('active'):
+                        reasons.add(n)
+            src = 'nvidia-smi 200 ms'
         if not sm:
-            return dict(sm_mhz=None, sm_max_mhz=None, reasons=[], samples=0)
-        return dict(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), reasons=sorted(reasons), samples=len(sm))
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=[], samples=0, source=src)
+        return dict(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), reasons=sorted(reasons), samples=len(sm),
+                    source=src)
 
 
 # ------------------------------------------------------------------------------------------------ GPU arm
