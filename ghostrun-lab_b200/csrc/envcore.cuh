@@ -229,6 +229,16 @@ static __device__ Upd reward_update(const Spec& G, const Sig& s, int frames, Tra
 
 // ------------------------------------------------------------------------------------------------ env arrays
 
+// A boot restart's outcome besides the machine record: the env's clock, fault code and tracker after the idle frames,
+// the 4 neutral frames and the first tracker update.
+struct RestartMeta {
+    Tracker trk;
+    u64 target;
+    u32 ep_frame, fault;
+    i32 ep_maxlvl;
+    u32 ok;          // 1: template k was taken
+};
+
 struct GameArgs {   // one game slice
     CartView cart;
     Spec spec;
@@ -256,6 +266,18 @@ struct GameArgs {   // one game slice
     u32* lv_idle_fault;        // [lv_cap][lv_idle_n] fault code after those frames
     u32* lv_chain_ok;          // [lv_cap] 1: the chain matches the slot
     StateView lv_scratch;      // emulation space of k_chain, env index = slot
+    // Restart templates: a boot restart with k <= idle_tmpl idle frames (the boot snapshot's record k, then the 4
+    // neutral frames with pad 0 and the first tracker update) is a pure function of k, so the whole outcome - machine
+    // record, the 4 presentation slots, clock, fault, tracker and the first observation - is taken once from an env
+    // that made it (k_tmpl_capture, after rlenv_start) and copied by k_restore instead of emulating and drawing it.
+    u8* tm_rec;                // [idle_tmpl + 1][kRecBytes]
+    u8* tm_nt;                 // [idle_tmpl + 1][4][2048] presentation slots
+    u8* tm_oam;                // [idle_tmpl + 1][4][256]
+    u8* tm_chr;                // [idle_tmpl + 1][4][8192] (CHR-RAM carts)
+    u8* tm_bank;               // [idle_tmpl + 1][4]
+    u8* tm_pix;                // [idle_tmpl + 1][4][224][240] colour numbers of the first observation
+    u8* tm_emph;               // [idle_tmpl + 1][4][224]
+    RestartMeta* tm_meta;      // [idle_tmpl + 1]
 };
 
 struct EnvArgs {
@@ -276,6 +298,7 @@ struct EnvArgs {
     u32* fault;
     u8* resetting;
     u8* render_seq;     // [N, 4] frames left to the sequential renderer by the last render pass
+    u8* tm_used;        // [N] 1: the env's restart was copied from a restart template (no restart frames to run)
     // restart list
     u32* list;
     u32* list_count;
@@ -471,7 +494,7 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
         bool valid = lane < kEnvsPerWarp && k < total;
         if (valid) {
             ge = restart ? A.list[k] : g.e0 + k;
-            valid = ge >= g.e0 && ge < g.e0 + g.n;
+            valid = ge >= g.e0 && ge < g.e0 + g.n && !(restart && A.tm_used[ge]);
         }
         Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab, prg_s);
         m.froze = 0;
@@ -615,23 +638,153 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
     }
 }
 
-// Restarting envs <- their snapshot records (after k_finish listed them): one block per listed env.
+// A boot restart with k idle frames that has a template (0 <= k <= idle_tmpl, template taken).
+__device__ __forceinline__ bool tmpl_restart(const GameArgs& g, const EnvArgs& A, u32 ge, int& k) {
+    k = A.ep_idle[ge];
+    if (!g.tm_meta || (A.ep_start && A.ep_start[ge] >= 0)) return false;
+    return k >= 0 && k <= static_cast<int>(g.idle_tmpl) && g.tm_meta[k].ok != 0u;
+}
+
+// Restarting envs <- their snapshot records (after k_finish listed them): one block per listed env. A boot restart
+// with a template takes the template's whole outcome instead (record, presentation slots, first observation, clock,
+// fault, tracker; controls from its own dropout state) and is left out of the restart frames and drawing.
 static __global__ void __launch_bounds__(128) k_restore(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A) {
     const u32 total = *A.list_count;
+    const bool chr_ram = g.cart.chr == nullptr;
     for (u32 k = blockIdx.x; k < total; k += gridDim.x) {
         const u32 ge = A.list[k];
+        int tk;
+        if (tmpl_restart(g, A, ge, tk)) {
+            const u64 t4 = static_cast<u64>(tk) * 4;
+            scatter_record(A.st, ge, g.tm_rec + static_cast<u64>(tk) * kRecBytes, chr_ram, threadIdx.x, blockDim.x);
+            const u64 s4 = static_cast<u64>(ge) * 4;
+            {   // presentation slots
+                const uint4* src = reinterpret_cast<const uint4*>(g.tm_nt + t4 * kNtBytes);
+                uint4* dst = reinterpret_cast<uint4*>(A.st.snap_nt + s4 * kNtBytes);
+                for (u32 i = threadIdx.x; i < 4 * kNtBytes / 16; i += blockDim.x) dst[i] = src[i];
+                const uint4* so = reinterpret_cast<const uint4*>(g.tm_oam + t4 * kOamBytes);
+                uint4* doam = reinterpret_cast<uint4*>(A.st.snap_oam + s4 * kOamBytes);
+                for (u32 i = threadIdx.x; i < 4 * kOamBytes / 16; i += blockDim.x) doam[i] = so[i];
+                if (chr_ram && A.st.snap_chr) {
+                    const uint4* sc = reinterpret_cast<const uint4*>(g.tm_chr + t4 * kChrRamBytes);
+                    uint4* dc = reinterpret_cast<uint4*>(A.st.snap_chr + s4 * kChrRamBytes);
+                    for (u32 i = threadIdx.x; i < 4 * kChrRamBytes / 16; i += blockDim.x) dc[i] = sc[i];
+                }
+                if (threadIdx.x < 4) A.st.slot_bank[s4 + threadIdx.x] = g.tm_bank[t4 + threadIdx.x];
+            }
+            if (!A.no_render) {   // the first observation: colour numbers, or 6-bit packed (4 pixels -> 3 bytes)
+                const u32* px = reinterpret_cast<const u32*>(g.tm_pix + t4 * kObsPixels);
+                if (A.packed) {
+                    u8* dst = A.packed + s4 * (kObsPixels / 4 * 3);
+                    for (u32 i = threadIdx.x; i < 4 * kObsPixels / 4; i += blockDim.x) {
+                        const u32 w = px[i];
+                        const u32 v = (w & 0x3Fu) | (((w >> 8) & 0x3Fu) << 6) | (((w >> 16) & 0x3Fu) << 12) | (((w >> 24) & 0x3Fu) << 18);
+                        dst[3 * i] = static_cast<u8>(v); dst[3 * i + 1] = static_cast<u8>(v >> 8); dst[3 * i + 2] = static_cast<u8>(v >> 16);
+                    }
+                } else {
+                    const uint4* src = reinterpret_cast<const uint4*>(px);
+                    uint4* dst = reinterpret_cast<uint4*>(A.obs + s4 * kObsPixels);
+                    for (u32 i = threadIdx.x; i < 4 * kObsPixels / 16; i += blockDim.x) dst[i] = src[i];
+                }
+                const u8* se = g.tm_emph + t4 * kObsH;
+                u8* de = A.emph + s4 * kObsH;
+                for (u32 i = threadIdx.x; i < 4 * kObsH; i += blockDim.x) de[i] = se[i];
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {   // ph_reset_finish_controls as the template made it, then this env's controls
+                const RestartMeta& M = g.tm_meta[tk];
+                A.trk[ge] = M.trk;
+                A.target[ge] = M.target;
+                A.ep_frame[ge] = M.ep_frame;
+                A.fault[ge] = M.fault;
+                A.ep_ret[ge] = 0.0f;
+                A.ep_len[ge] = 0;
+                A.ep_maxlvl[ge] = M.ep_maxlvl;
+                A.resetting[ge] = 0;
+                A.tm_used[ge] = 1;
+                if (A.lv_chained) A.lv_chained[ge] = 0;
+                write_controls(g, A, ge);
+            }
+            __syncthreads();
+            continue;
+        }
         bool chained;
         const u8* rec = restart_record(g, A, ge, chained);
-        scatter_record(A.st, ge, rec, g.cart.chr == nullptr, threadIdx.x, blockDim.x);
-        if (threadIdx.x == 0 && A.lv_chained) {
-            A.lv_chained[ge] = chained ? 1 : 0;
-            if (chained) {   // the idle frames are in the record: the episode's clock and fault move on with them
-                const int lv = A.ep_start[ge], idle = A.ep_idle[ge];
-                A.target[ge] += static_cast<u64>(idle) * kFrameDots;
-                A.ep_frame[ge] += static_cast<u32>(idle);
-                A.fault[ge] = g.lv_idle_fault[static_cast<u64>(lv) * g.lv_idle_n + static_cast<u64>(idle - 1)];
+        scatter_record(A.st, ge, rec, chr_ram, threadIdx.x, blockDim.x);
+        if (threadIdx.x == 0) {
+            A.tm_used[ge] = 0;
+            if (A.lv_chained) {
+                A.lv_chained[ge] = chained ? 1 : 0;
+                if (chained) {   // the idle frames are in the record: the episode's clock and fault move on with them
+                    const int lv = A.ep_start[ge], idle = A.ep_idle[ge];
+                    A.target[ge] += static_cast<u64>(idle) * kFrameDots;
+                    A.ep_frame[ge] += static_cast<u32>(idle);
+                    A.fault[ge] = g.lv_idle_fault[static_cast<u64>(lv) * g.lv_idle_n + static_cast<u64>(idle - 1)];
+                }
             }
         }
+        __syncthreads();
+    }
+}
+
+// Restart templates from the envs that just started (after rlenv_start, pictures drawn): block k takes the lowest env
+// of the game slice whose first episode began from the boot snapshot with k idle frames; none: template k stays off.
+static __global__ void __launch_bounds__(128) k_tmpl_capture(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A) {
+    const u32 tk = blockIdx.x;
+    __shared__ u32 best;
+    if (threadIdx.x == 0) best = 0xFFFFFFFFu;
+    __syncthreads();
+    for (u32 i = threadIdx.x; i < g.n; i += blockDim.x) {
+        const u32 ge = g.e0 + i;
+        if (A.ep_idle[ge] == static_cast<int>(tk) && !(A.ep_start && A.ep_start[ge] >= 0) && A.resetting[ge] == 0) {
+            atomicMin(&best, ge);
+            break;
+        }
+    }
+    __syncthreads();
+    const u32 ge = best;
+    RestartMeta& M = g.tm_meta[tk];
+    if (ge == 0xFFFFFFFFu) {
+        if (threadIdx.x == 0) M.ok = 0;
+        return;
+    }
+    const bool chr_ram = g.cart.chr == nullptr;
+    const u64 t4 = static_cast<u64>(tk) * 4, s4 = static_cast<u64>(ge) * 4;
+    gather_record(A.st, ge, g.tm_rec + static_cast<u64>(tk) * kRecBytes, chr_ram, threadIdx.x, blockDim.x);
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(A.st.snap_nt + s4 * kNtBytes);
+        uint4* dst = reinterpret_cast<uint4*>(g.tm_nt + t4 * kNtBytes);
+        for (u32 i = threadIdx.x; i < 4 * kNtBytes / 16; i += blockDim.x) dst[i] = src[i];
+        const uint4* so = reinterpret_cast<const uint4*>(A.st.snap_oam + s4 * kOamBytes);
+        uint4* doam = reinterpret_cast<uint4*>(g.tm_oam + t4 * kOamBytes);
+        for (u32 i = threadIdx.x; i < 4 * kOamBytes / 16; i += blockDim.x) doam[i] = so[i];
+        if (chr_ram && A.st.snap_chr) {
+            const uint4* sc = reinterpret_cast<const uint4*>(A.st.snap_chr + s4 * kChrRamBytes);
+            uint4* dc = reinterpret_cast<uint4*>(g.tm_chr + t4 * kChrRamBytes);
+            for (u32 i = threadIdx.x; i < 4 * kChrRamBytes / 16; i += blockDim.x) dc[i] = sc[i];
+        }
+        if (threadIdx.x < 4) g.tm_bank[t4 + threadIdx.x] = A.st.slot_bank[s4 + threadIdx.x];
+    }
+    u32* px = reinterpret_cast<u32*>(g.tm_pix + t4 * kObsPixels);
+    if (A.packed) {   // 3 bytes -> 4 colour numbers
+        const u8* src = A.packed + s4 * (kObsPixels / 4 * 3);
+        for (u32 i = threadIdx.x; i < 4 * kObsPixels / 4; i += blockDim.x) {
+            const u32 v = src[3 * i] | (static_cast<u32>(src[3 * i + 1]) << 8) | (static_cast<u32>(src[3 * i + 2]) << 16);
+            px[i] = (v & 0x3Fu) | (((v >> 6) & 0x3Fu) << 8) | (((v >> 12) & 0x3Fu) << 16) | (((v >> 18) & 0x3Fu) << 24);
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(A.obs + s4 * kObsPixels);
+        for (u32 i = threadIdx.x; i < 4 * kObsPixels / 16; i += blockDim.x) reinterpret_cast<uint4*>(px)[i] = src[i];
+    }
+    for (u32 i = threadIdx.x; i < 4 * kObsH; i += blockDim.x) g.tm_emph[t4 * kObsH + i] = A.emph[s4 * kObsH + i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        M.trk = A.trk[ge];
+        M.target = A.target[ge];
+        M.ep_frame = A.ep_frame[ge];
+        M.fault = A.fault[ge];
+        M.ep_maxlvl = A.ep_maxlvl[ge];
+        M.ok = 1;
     }
 }
 

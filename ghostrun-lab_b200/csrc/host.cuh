@@ -224,6 +224,8 @@ inline void check_launch(const char* what) {
 // high-priority side stream so it overlaps the main render:
 //   s:    [list reset] k_frames -> k_finish --fork--> k_render, k_render_seq (envs not restarting) .. join (join_side)
 //   side:                          k_restore -> [k_archive] -> k_frames(restart) -> k_render, k_render_seq (restart)
+// (k_restore copies a boot restart's whole outcome from its restart template when there is one; the restart frames
+// and drawing then leave that env out)
 // Games run on their own stream pairs, concurrently (launch_all).
 // k_finish decides the episode ends and lists the restarting envs; the main render leaves them out (their outputs
 // are the new episode's first frames, drawn by the restart pass), so the two branches touch disjoint envs. The level
@@ -320,7 +322,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     if (!A.no_render) {
         R.list = A.list;
         R.list_count = A.list_count;
-        R.skip = nullptr;
+        R.skip = A.tm_used;   // restarts copied from a template have their first observation already
         const u32 blocks = start ? std::min<u32>((n * R.frames + kRenderWarps - 1) / kRenderWarps, 148u * 2u * 4u) : 148u;
         T.begin(kKRestartRender, side);
         k_render<B><<<blocks, 32 * kRenderWarps, smem, side>>>(R);
@@ -370,6 +372,17 @@ void boot_game(Env& env, Game& gm, const u8* pads, std::size_t npads, int idle_m
     }
     gm.g.recs = recs;
     gm.g.idle_tmpl = idle;
+    {   // restart templates, taken after rlenv_start (k_tmpl_capture)
+        const std::size_t nk = static_cast<std::size_t>(idle) + 1;
+        gm.g.tm_rec = env.mem.allocn<u8>(nk * kRecBytes);
+        gm.g.tm_nt = env.mem.allocn<u8>(nk * 4 * kNtBytes);
+        gm.g.tm_oam = env.mem.allocn<u8>(nk * 4 * kOamBytes);
+        gm.g.tm_chr = gm.g.cart.chr == nullptr ? env.mem.allocn<u8>(nk * 4 * kChrRamBytes) : nullptr;
+        gm.g.tm_bank = env.mem.allocn<u8>(nk * 4);
+        gm.g.tm_pix = env.mem.allocn<u8>(nk * 4 * kObsPixels);
+        gm.g.tm_emph = env.mem.allocn<u8>(nk * 4 * kObsH);
+        gm.g.tm_meta = env.mem.allocn<RestartMeta>(nk);   // zeroed: no template taken
+    }
     gm.g.tmpl_target = static_cast<u64>(kVblankDot) + static_cast<u64>(npads) * kFrameDots;
 }
 

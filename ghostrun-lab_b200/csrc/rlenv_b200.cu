@@ -175,6 +175,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         A.fault = M.allocn<u32>(N, true);
         A.resetting = M.allocn<u8>(N);
         A.render_seq = M.allocn<u8>(static_cast<std::size_t>(N) * kFramesPerDecision);   // transient: not saved
+        A.tm_used = M.allocn<u8>(N);
         A.list = M.allocn<u32>(N);                                    // per game: its slice [game_e0, game_e0 + n)
         A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1 + N);   // per game, then per range start
         {
@@ -302,7 +303,15 @@ void rlenv_bind_obs(void* h, std::uint8_t* obs, std::uint8_t* emph) {
 
 int rlenv_start(void* h, void* stream) {
     try {
-        launch_all(*static_cast<Env*>(h), true, static_cast<cudaStream_t>(stream));
+        Env& env = *static_cast<Env*>(h);
+        auto s = static_cast<cudaStream_t>(stream);
+        launch_all(env, true, s);
+        if (!env.A.no_render) {   // every env just made a boot (or level) restart: take the restart templates
+            for (const Game& gm : env.games) {
+                k_tmpl_capture<<<gm.g.idle_tmpl + 1, 128, 0, s>>>(gm.g, env.A);
+                check_launch("k_tmpl_capture");
+            }
+        }
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }
