@@ -281,6 +281,21 @@ def stem_arm(args):
     out_bytes = out.numel() * 2
     peak, kind = measured_peaks()
     achieved = (in_bytes + out_bytes) / (ms / 1e3) / 1e9
+    # backward (rl_stem_bwd): reads the output gradient and the packed pictures again, writes dW / dbias
+    from stem import palette4, stem_backward
+    gout = (torch.randn(B, 112, 120, 16, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    pal4 = palette4(pal)
+    for _ in range(W):
+        stem_backward(gout, obs6, emph, pal4, packed=True, check=False)
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for _ in range(K):
+        stem_backward(gout, obs6, emph, pal4, packed=True, check=False)
+    b1.record()
+    torch.cuda.synchronize()
+    bwd_ms = b0.elapsed_time(b1) / K
+    bwd_bytes = in_bytes + gout.numel() * 2
     # e2e: the learner's view - the packed rollout slice from pinned host memory, the stem, a per-channel mean back
     host6 = obs6.cpu().pin_memory()
     hoste = emph.cpu().pin_memory()
@@ -306,6 +321,10 @@ def stem_arm(args):
                 roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
                               traffic=None, kernel='k_stem_fwd<packed>', bytes_per_call=in_bytes + out_bytes,
                               peak_source=f'{kind} (MEASURED_PEAKS.json hbm_gbs)' if kind == 'measured' else 'fallback'),
+                backward=dict(ms=round(bwd_ms, 4), samples_per_s=round(B / (bwd_ms / 1e3), 1),
+                              achieved_gbs=round(bwd_bytes / (bwd_ms / 1e3) / 1e9, 1),
+                              frac=round(bwd_bytes / (bwd_ms / 1e3) / 1e9 / peak, 4), bytes_per_call=bwd_bytes,
+                              kernel='k_stem_bwd<packed> + k_stem_bwd_reduce'),
                 gpu_launches=K, clocks=clk.summary(), cpu_baseline=None,
                 checksum=[round(float(x), 5) for x in m[:4]])
 

@@ -287,6 +287,199 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stem_fwd(const __grid_
     }
 }
 
+// ------------------------------------------------------------------------------------------------ backward
+// dW = sum_p g[p] x[p]^T and dbias = sum_p g[p] over the output pixels p (the reference's _stem_bwd_kernel,
+// rl/fused.py:89-107; the input pictures are not trained). On the tensor cores with K = pixels: A = x^T (M = the 64
+// permuted inputs k', padded to M = 128 with zero rows), B = g (N = 16 channels), D = dW^T in tensor memory,
+// accumulated over all of a CTA's tiles. Both operands are MN-major no-swizzle core matrices: pixel p's 64 inputs
+// are 8 chunks of 16 bytes, chunk c of A at c * 2048 + (p / 8) * 128 + (p % 8) * 16; g's 16 channels are 2 chunks
+// of B at the same places. A's padding rows 64..127 (chunks 8..15) are whatever shared memory follows the buffer:
+// they only reach D rows 64..127, which are never read. The constant-1 input of position 0 (k' = 3) makes
+// D row 3 the bias gradient. Tiles are output rows (120 pixels, 8 zero rows of g); each CTA writes its 64 x 16
+// partial sums, and k_stem_bwd_reduce adds the CTAs' partials in a fixed order into dW [16][48] and dbias [16].
+constexpr uint32_t kBwdChunk = 2048;                    // bytes between core-matrix columns along M / N
+constexpr int kBwdCtasPerSm = 4;
+constexpr uint32_t kBwdA = 8 * kBwdChunk;               // 16 KB per A buffer (its 8 chunks of inputs)
+constexpr uint32_t kBwdB = 2 * kBwdChunk;               // 4 KB per B buffer
+constexpr uint32_t kBwdSmem = 2 * kBwdA + 2 * kBwdB + 4096 + 2 * 2048 + 64 + 64;
+// the M = 128 operand of buffer 1 reaches 16 KB past its 8 chunks: into the buffers and tables after it
+static_assert(kBwdSmem >= 3 * kBwdA, "A's padding rows must stay inside the block's shared memory");
+// kind::f16, fp32 D, bf16 A and B, both MN-major (bits 15, 16), N = 16, M = 128
+constexpr uint32_t kIdescBwd = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+                               (static_cast<uint32_t>(kN >> 3) << 17) | (static_cast<uint32_t>(kTileM >> 4) << 24);
+
+struct StemBwdArgs {
+    const uint8_t* obs;
+    const uint8_t* emph;
+    const uint16_t* pal;
+    const uint16_t* g;          // [B, 112, 120, 16] bf16 bits: the output gradient
+    float* part;                // [grid][64][16] per-CTA dW^T partial sums
+    int* err;
+    long long n_out;
+};
+
+template <bool PACKED>
+__global__ void __launch_bounds__(kThreads) k_stem_bwd(const __grid_constant__ StemBwdArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* sA = smem;                                                    // [2][kBwdA]
+    uint8_t* sB = smem + 2 * kBwdA;                                        // [2][kBwdB]
+    uint2* sPal = reinterpret_cast<uint2*>(sB + 2 * kBwdB);                // [512]
+    uint32_t* sRow = reinterpret_cast<uint32_t*>(sB + 2 * kBwdB + 4096);   // [2][8 * 64]
+    uint32_t* sEmph = sRow + 2 * 8 * 64;                                   // [2][8]
+    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ uint32_t tmem_base;
+    const int tid = threadIdx.x, warp = tid >> 5;
+
+    for (int i = tid; i < 512; i += kThreads) {
+        const uint2 v = reinterpret_cast<const uint2*>(a.pal)[i];
+        sPal[i] = make_uint2(v.x, (v.y & 0xFFFFu) | (kOneBf16 << 16));
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar[0])));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar[1])));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" :: "r"(smem_u32(&tmem_base)));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    const long long rows = a.n_out / kOW;
+    const long long step = gridDim.x;
+    StemArgs fa;   // the input side shares the forward's row loads
+    fa.obs = a.obs; fa.emph = a.emph;
+    RowLoad<PACKED> L;
+    rows_load<PACKED>(fa, blockIdx.x, rows, tid, L);
+    rows_store<PACKED>(L, sRow, sEmph, tid);
+    rows_load<PACKED>(fa, blockIdx.x + step, rows, tid, L);
+    // the output gradient of the next tile, one tile ahead (pixels 120..127 weigh nothing)
+    auto g_load = [&](long long r, uint4& q0, uint4& q1) {
+        q0 = make_uint4(0u, 0u, 0u, 0u);
+        q1 = q0;
+        if (tid < kOW && r < rows) {
+            const uint4* gp = reinterpret_cast<const uint4*>(a.g + (r * kOW + tid) * kN);
+            q0 = __ldg(gp);
+            q1 = __ldg(gp + 1);
+        }
+    };
+    uint4 g0, g1;
+    g_load(blockIdx.x, g0, g1);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+    const int ox = tid < kOW ? tid : kOW - 1;
+    const uint32_t bit = PACKED ? 12u * static_cast<uint32_t>(ox) : 16u * static_cast<uint32_t>(ox);
+    const uint32_t wi = bit >> 5, sh = bit & 31u;
+    const uint32_t cm = (static_cast<uint32_t>(tid) / 8) * 128 + (static_cast<uint32_t>(tid) % 8) * 16;   // this pixel's row
+    uint32_t phase[2] = {0u, 0u};
+    int fail = 0;
+    int it = 0;
+    for (long long r = blockIdx.x; r < rows; r += step, ++it) {
+        const int buf = it & 1;
+        uint32_t ok = 1;
+        if (it >= 2) {   // tile it-2 read this buffer
+            ok = mbar_wait(smem_u32(&mbar[buf]), phase[buf]);
+            if (ok) phase[buf] ^= 1u;
+        }
+        if (ok) {
+            uint8_t* A = sA + buf * kBwdA;
+            uint32_t x[16];
+            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPal, 0, wi, sh, x);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(A + c * kBwdChunk + cm) = make_uint4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPal, 4, wi, sh, x);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                *reinterpret_cast<uint4*>(A + (4 + c) * kBwdChunk + cm) = make_uint4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
+            uint8_t* Bb = sB + buf * kBwdB;
+            *reinterpret_cast<uint4*>(Bb + cm) = g0;
+            *reinterpret_cast<uint4*>(Bb + kBwdChunk + cm) = g1;
+            if (r + step < rows) rows_store<PACKED>(L, sRow + (buf ^ 1) * 8 * 64, sEmph + (buf ^ 1) * 8, tid);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        fail = __syncthreads_or(ok == 0u);
+        if (fail) break;
+        if (tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_base = smem_u32(sA + buf * kBwdA), b_base = smem_u32(sB + buf * kBwdB);
+#pragma unroll
+            for (int ks = 0; ks < kTileM / 16; ++ks) {   // 8 steps of 16 pixels
+                const uint64_t da = smem_desc(a_base + ks * 256, 128, kBwdChunk);
+                const uint64_t db = smem_desc(b_base + ks * 256, 128, kBwdChunk);
+                const uint32_t acc = (it > 0 || ks > 0) ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\t"
+                    "setp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+                    :: "r"(tmem), "l"(da), "l"(db), "r"(kIdescBwd), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         :: "r"(smem_u32(&mbar[buf])) : "memory");
+        }
+        rows_load<PACKED>(fa, r + 2 * step, rows, tid, L);
+        g_load(r + step, g0, g1);
+    }
+    // drain (also after a failure): the MMAs of the last two tiles issued, bounded; then rows 0..63 of D (warps 0
+    // and 1) to this CTA's partial
+    uint32_t ok = 1;
+    for (int k = 1; k <= 2; ++k) {
+        const int j = it - k;
+        if (j >= 0) ok &= mbar_wait(smem_u32(&mbar[j & 1]), phase[j & 1]);
+    }
+    if (__syncthreads_or(fail != 0 || ok == 0u)) {
+        if (tid == 0) atomicExch(a.err, 1);
+    } else if (it > 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (warp < 2) {
+            uint32_t d[16];
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]),
+                           "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
+                         : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            float4* dst = reinterpret_cast<float4*>(a.part + (static_cast<size_t>(blockIdx.x) * 64 + tid) * kN);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                dst[q] = make_float4(__uint_as_float(d[4 * q]), __uint_as_float(d[4 * q + 1]),
+                                     __uint_as_float(d[4 * q + 2]), __uint_as_float(d[4 * q + 3]));
+        }
+    } else if (tid < 64) {   // no tile: a zero partial
+        float4* dst = reinterpret_cast<float4*>(a.part + (static_cast<size_t>(blockIdx.x) * 64 + tid) * kN);
+        for (int q = 0; q < 4; ++q) dst[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" :: "r"(tmem));
+    }
+}
+
+// dW[o][k] and dbias[o] from the CTAs' partials (fixed order): k = (frame * 3 + c) * 4 + dy * 2 + dx is row
+// k' = (frame * 4 + dy * 2 + dx) * 4 + c of D; dbias is row 3.
+__global__ void k_stem_bwd_reduce(const float* part, int parts, float* dw, float* db) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;   // 16 * 48 weights, then 16 biases
+    if (i >= kN * kK + kN) return;
+    int row, o;
+    if (i < kN * kK) {
+        o = i / kK;
+        const int k = i % kK, c = (k / 4) % 3, f = k / 12, pos = f * 4 + (k % 4);
+        row = pos * 4 + c;
+    } else {
+        o = i - kN * kK;
+        row = 3;
+    }
+    float s = 0.f;
+    for (int p = 0; p < parts; ++p) s += part[(static_cast<size_t>(p) * 64 + row) * kN + o];
+    if (i < kN * kK) dw[i] = s;
+    else db[o] = s;
+}
+
 thread_local std::string g_stem_error;
 
 }  // namespace
@@ -333,5 +526,65 @@ int rl_stem_fwd(const void* obs, const void* emph, const void* pal4, const void*
 }
 
 const char* rl_stem_error(void) { return g_stem_error.c_str(); }
+
+// Work space of rl_stem_bwd on the current device: the CTAs' partial sums (64 x 16 fp32 each, 4 CTAs per SM).
+size_t rl_stem_bwd_work_bytes(void) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return static_cast<size_t>(sms) * kBwdCtasPerSm * 64 * kN * sizeof(float);
+}
+
+// Stem backward (rl/fused.py:130-160 stem_bwd semantics): grad [B,112,120,16] bf16 (channels-last), the forward's
+// obs / emph / pal4 -> dw [16][48] fp32 (the conv weight's gradient, flattened as the forward's weight) and db [16]
+// fp32. work: device memory of rl_stem_bwd_work_bytes() bytes. err as in rl_stem_fwd. Asynchronous on `stream`.
+int rl_stem_bwd(const void* grad, const void* obs, const void* emph, const void* pal4, void* dw, void* db,
+                long long batch, int packed, void* work, size_t work_bytes, int* err, void* stream) {
+    StemBwdArgs a;
+    a.obs = static_cast<const uint8_t*>(obs);
+    a.emph = static_cast<const uint8_t*>(emph);
+    a.pal = static_cast<const uint16_t*>(pal4);
+    a.g = static_cast<const uint16_t*>(grad);
+    a.part = static_cast<float*>(work);
+    a.err = err;
+    a.n_out = batch * kOH * kOW;
+    if (batch <= 0) {
+        g_stem_error = "rl_stem_bwd: batch must be positive";
+        return 1;
+    }
+    if (a.n_out >= (1ll << 31)) { g_stem_error = "rl_stem_bwd: batch too large (B * 112 * 120 must be below 2^31)"; return 1; }
+    if ((reinterpret_cast<uintptr_t>(obs) & 3) || (reinterpret_cast<uintptr_t>(grad) & 15) ||
+        (reinterpret_cast<uintptr_t>(work) & 15)) {
+        g_stem_error = "rl_stem_bwd: obs must be 4-byte, grad and work 16-byte aligned";
+        return 1;
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long tiles = batch * kOH;
+    const long long want = static_cast<long long>(sms) * kBwdCtasPerSm;
+    const unsigned grid = static_cast<unsigned>(tiles < want ? tiles : want);
+    if (work_bytes < static_cast<size_t>(grid) * 64 * kN * sizeof(float)) {
+        g_stem_error = "rl_stem_bwd: work space smaller than rl_stem_bwd_work_bytes()";
+        return 1;
+    }
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (packed) {
+        e = cudaFuncSetAttribute(k_stem_bwd<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBwdSmem));
+        if (e == cudaSuccess) k_stem_bwd<true><<<grid, kThreads, kBwdSmem, s>>>(a);
+    } else {
+        e = cudaFuncSetAttribute(k_stem_bwd<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBwdSmem));
+        if (e == cudaSuccess) k_stem_bwd<false><<<grid, kThreads, kBwdSmem, s>>>(a);
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        k_stem_bwd_reduce<<<(kN * kK + kN + 255) / 256, 256, 0, s>>>(a.part, static_cast<int>(grid), static_cast<float*>(dw),
+                                                                      static_cast<float*>(db));
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) { g_stem_error = cudaGetErrorString(e); return 1; }
+    return 0;
+}
 
 }  // extern "C"

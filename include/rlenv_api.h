@@ -129,6 +129,14 @@ int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, uint8_t* host_out, 
 int rl_stem_fwd(const void* obs, const void* emph, const void* pal4, const void* weight, const void* bias, void* out,
                 long long batch, int packed, int* err, void* stream);
 const char* rl_stem_error(void);
+// rl/fused.py:89-107, 130-160 (the reference's _stem_bwd_kernel / stem_bwd custom op): grad [B,112,120,16] bf16
+// (the stem output's gradient, channels-last), obs / emph / pal4 / packed as for rl_stem_fwd -> dw [16][48] fp32
+// (dW = sum over output pixels of grad x input^T, flattened as the forward's weight) and db [16] fp32 (sum of grad).
+// work: device scratch of at least rl_stem_bwd_work_bytes() bytes (per-CTA partial sums, added in a fixed order:
+// the result is deterministic). err as for rl_stem_fwd. Asynchronous on `stream`; non-zero on a bad argument.
+size_t rl_stem_bwd_work_bytes(void);
+int rl_stem_bwd(const void* grad, const void* obs, const void* emph, const void* pal4, void* dw, void* db,
+                long long batch, int packed, void* work, size_t work_bytes, int* err, void* stream);
 
 // Per-kernel device time (CUDA events on the launching stream) and launch counts, for benchmarks.
 void rlenv_set_timing(void* h, int on);
