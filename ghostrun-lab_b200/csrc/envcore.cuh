@@ -299,6 +299,7 @@ struct EnvArgs {
     u8* resetting;
     u8* render_seq;     // [N, 4] frames left to the sequential renderer by the last render pass
     u8* tm_used;        // [N] 1: the env's restart was copied from a restart template (no restart frames to run)
+    double* ep_acc;     // optional [4]: finished episodes, their deaths, their returns, level events (added here)
     // restart list
     u32* list;
     u32* list_count;
@@ -627,6 +628,14 @@ static __global__ void __launch_bounds__(128) k_finish(const __grid_constant__ G
             inf[5] = t.overflow ? 1.0f : 0.0f;
             inf[6] = static_cast<float>(A.ep_idle[ge]);
             inf[7] = static_cast<float>(A.episode[ge]);
+        }
+        if (A.ep_acc) {   // the rollout's episode counters: one fp64 atomic per finished episode or level event
+            if (done) {
+                atomicAdd(&A.ep_acc[0], 1.0);
+                atomicAdd(&A.ep_acc[1], static_cast<double>(t.deaths));
+                atomicAdd(&A.ep_acc[2], static_cast<double>(ret));
+            }
+            if (u.events & kEvLevel) atomicAdd(&A.ep_acc[3], 1.0);
         }
     }
     if (done) {

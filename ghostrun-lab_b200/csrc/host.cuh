@@ -119,6 +119,7 @@ enum KernelKind : int { kKFrames = 0, kKRender, kKFinish, kKRestart, kKRestartRe
 
 struct KTimer {
     bool on = false;
+    unsigned mask = ~0u;   // kinds timed while on (bit k = kind k)
     double ms[kKinds] = {};
     unsigned long long launches[kKinds] = {};
     unsigned long long total_launches = 0;
@@ -132,12 +133,12 @@ struct KTimer {
     void begin(int kind, cudaStream_t s) {
         ++total_launches;
         ++launches[kind];
-        if (!on) return;
+        if (!on || !((mask >> kind) & 1u)) { cur_a = nullptr; return; }
         cur_a = take();
         ck(cudaEventRecord(cur_a, s), "event");
     }
     void end(int kind, cudaStream_t s) {
-        if (!on) return;
+        if (!on || !cur_a) return;
         cudaEvent_t b = take();
         ck(cudaEventRecord(b, s), "event");
         pending.push_back({kind, {cur_a, b}});

@@ -594,6 +594,12 @@ void rlenv_set_timing(void* h, int on) {
     T.collect();
     T.on = on != 0;
 }
+void rlenv_bind_episode_counters(void* h, double* acc) { static_cast<Env*>(h)->A.ep_acc = acc; }
+void rlenv_set_timing_kinds(void* h, unsigned mask) {
+    KTimer& T = *static_cast<Env*>(h)->timer;
+    T.collect();
+    T.mask = mask;
+}
 // out[0..5] = ms of frames / render / finish / restart frames / restart render / pack6 kernels since the last reset,
 // out[6..11] their launch counts, out[12] all launches; reset != 0 clears the counters afterwards.
 int rlenv_timing(void* h, double* out, int reset) {

@@ -83,6 +83,8 @@ def _load(path: Path):
         lib.rlenv_bind_obs_pack6.argtypes = [P, P]
         lib.rlenv_set_timing.argtypes = [P, I]
         lib.rlenv_timing.argtypes = [P, P, I]
+    if hasattr(lib, 'rlenv_set_timing_kinds'):
+        lib.rlenv_set_timing_kinds.argtypes = [P, ctypes.c_uint]
     if hasattr(lib, 'rlenv_dump_env'):
         lib.rlenv_dump_env.argtypes = [P, I, P, P]
         lib.rlenv_env_scalars.argtypes = [P, I, P, P]
@@ -322,8 +324,12 @@ class RlEnv:
         self._packed_keep = packed
         self.lib.rlenv_bind_obs_pack6(self.h, ctypes.c_void_p(packed.data_ptr()))
 
-    def set_timing(self, on: bool):
-        """Record CUDA events around every kernel launch (per-kernel device time, see timing())."""
+    def set_timing(self, on: bool, kinds=None):
+        """Record CUDA events around kernel launches (per-kernel device time, see timing()); kinds: names of the
+        kinds to time (timing() order), None = all."""
+        names = ('frames', 'render', 'finish', 'restart_frames', 'restart_render', 'pack6')
+        mask = 0xFFFFFFFF if kinds is None else sum(1 << names.index(k) for k in kinds)
+        self.lib.rlenv_set_timing_kinds(self.h, mask)
         self.lib.rlenv_set_timing(self.h, int(bool(on)))
 
     def timing(self, reset=False) -> dict:

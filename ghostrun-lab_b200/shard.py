@@ -9,6 +9,8 @@ is one all-reduce of scalar episode counters per rollout (rl/train.py:331-450: p
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -28,8 +30,23 @@ class EpisodeCounters:
     def __init__(self, device):
         self.v = torch.zeros(len(FIELDS), dtype=torch.float64, device=device)       # this rollout, this rank
         self.total = torch.zeros(len(FIELDS), dtype=torch.float64, device=device)   # all finished rollouts, all ranks
+        self._attached = None
+
+    def attach(self, env) -> bool:
+        """Let the GPU library add each decision's counters in its finishing kernel (rlenv_bind_episode_counters):
+        account() then has nothing to do for this env. False (torch reductions per decision) on a library without it."""
+        fn = getattr(env.lib, 'rlenv_bind_episode_counters', None)
+        if fn is None or self.v.device.type != 'cuda':
+            return False
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        fn(env.h, ctypes.c_void_p(self.v.data_ptr()))
+        env._counters_keep = self.v
+        self._attached = env
+        return True
 
     def account(self, env):
+        if env is self._attached:
+            return
         d = env.done.bool()
         self.v[0] += d.sum()
         self.v[1] += torch.where(d, env.info[:, 3], 0).sum()

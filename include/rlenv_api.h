@@ -138,8 +138,18 @@ size_t rl_stem_bwd_work_bytes(void);
 int rl_stem_bwd(const void* grad, const void* obs, const void* emph, const void* pal4, void* dw, void* db,
                 long long batch, int packed, void* work, size_t work_bytes, int* err, void* stream);
 
+// No reference counterpart (the reference sums its rollout statistics in Python from the rollout buffers,
+// rl/train.py:450): acc = device float64[4] to which every later decision adds the finished episodes' count, their
+// deaths, their returns and the level events (added by the finishing kernel, no extra launch; the order of the fp64
+// additions varies, so the return sum may differ in its last bits between runs). NULL stops it. Takes effect at the
+// next call.
+void rlenv_bind_episode_counters(void* h, double* acc);
+
 // Per-kernel device time (CUDA events on the launching stream) and launch counts, for benchmarks.
 void rlenv_set_timing(void* h, int on);
+// Which kernel kinds rlenv_set_timing times (bit k = out13[k]'s kind: 0 frames, 1 render, 2 finish, 3 restart frames,
+// 4 restart render, 5 pack6; default all): each timed launch adds two CUDA events to its stream.
+void rlenv_set_timing_kinds(void* h, unsigned mask);
 int rlenv_timing(void* h, double* out13, int reset);
 
 #ifdef __cplusplus

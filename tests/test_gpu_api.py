@@ -167,3 +167,25 @@ def test_gathers(gpu_lib_path):
     torch.cuda.synchronize()
     assert torch.equal(dst, src.reshape(T * N, row)[rows])
     assert torch.equal(dst2, src[:, torch.from_numpy(envs).cuda()])
+
+
+@pytest.mark.gpu
+def test_episode_counters_in_finishing_kernel(gpu_lib_path):
+    """rlenv_bind_episode_counters: the finishing kernel's per-decision sums equal the torch reductions over the
+    outputs (counts exactly; returns to float32 rounding of the torch sum)."""
+    from shard import EpisodeCounters
+    a, b = _env(gpu_lib_path), _env(gpu_lib_path)
+    ca, cb = EpisodeCounters(torch.device('cuda')), EpisodeCounters(torch.device('cuda'))
+    assert cb.attach(b)
+    gen = torch.Generator().manual_seed(3)
+    for t in range(400):
+        act = random_legal(a.masks.cpu(), gen).cuda()
+        a.actions.copy_(act); b.actions.copy_(act)
+        a.step(); b.step()
+        ca.account(a); cb.account(b)
+    torch.cuda.synchronize()
+    va, vb = ca.rollout_end().as_dict(), cb.rollout_end().as_dict()
+    assert va['finished'] > 0 and va['level_events'] >= 0
+    for k in ('finished', 'deaths', 'level_events'):
+        assert va[k] == vb[k], (k, va[k], vb[k])
+    assert abs(va['return_sum'] - vb['return_sum']) <= 1e-4 * max(1.0, abs(vb['return_sum']))
