@@ -684,6 +684,7 @@ struct Renderer {
         // and drawn on lines y+1..y+16. A superset; iterations whose 4 lines have none skip the sprite work.
         u32* may = reinterpret_cast<u32*>(W.emph);   // 8 words: bit l of the 256-line mask
         u8* vis = W.emph + 32;                       // OAM indices of the sprites that can show, in OAM order
+        u32* ov = reinterpret_cast<u32*>(W.emph + 96);   // per lane: bit r = sprite rank r of its line reaches its pixels
         u32 nv;
         {
             auto span = [](u32 sp, u32 base) -> u32 {
@@ -712,6 +713,8 @@ struct Renderer {
             u32 nsp = 0;   // this lane group's sprite count
             const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;
             if (any) {
+                ov[lane] = 0u;
+                __syncwarp();
                 const int e = l0 + static_cast<int>(g) - 1;
                 const uint2 re = F.rec[e];
                 const u32 ctrl = ((re.x >> 18) & 7u) << 3;
@@ -736,6 +739,10 @@ struct Renderer {
                         u32 cw = chr_sel(pages, vadr & 0x1FFFu);
                         if (attr & 0x40u) cw = nib_reverse(cw);
                         sbuf[g * 8 + rk] = make_uint2(cw, (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8));
+                        // the lanes whose 32 pixels (screen x 8 + 32j ..) the sprite's x .. x + 7 reach
+                        const int wlo = (static_cast<int>(xx) - 8) >> 5, whi = (static_cast<int>(xx) - 1) >> 5;
+                        if (wlo >= 0) atomicOr(&ov[g * 8 + static_cast<u32>(wlo)], 1u << rk);
+                        if (whi != wlo && whi >= 0 && whi < 8) atomicOr(&ov[g * 8 + static_cast<u32>(whi)], 1u << rk);
                     }
                     nsp += __popc(gb);
                 }
@@ -777,11 +784,12 @@ struct Renderer {
             if (nmax) {
                 u32 n0 = 0, n1 = 0, n2 = 0, n3 = 0, a0 = 0, a1 = 0, a2 = 0, a3 = 0, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
                 const int x0 = 8 + 32 * static_cast<int>(j);
-                for (int i = static_cast<int>(nmax) - 1; i >= 0; --i) {
-                    if (i >= static_cast<int>(nsp)) continue;
-                    const uint2 sd = sbuf[g * 8 + static_cast<u32>(i)];
+                // the sprites that reach this lane's pixels, last in OAM order first (the first one wins)
+                for (u32 m = ov[lane]; m != 0u;) {
+                    const u32 i = 31u - static_cast<u32>(__clz(m));
+                    m &= ~(1u << i);
+                    const uint2 sd = sbuf[g * 8 + i];
                     const int rel = static_cast<int>(sd.y >> 8) - x0;
-                    if (rel <= -8 || rel >= 32) continue;
                     const int w = rel >> 3;                  // -1..3: word of the sprite's first pixel
                     const u32 o = static_cast<u32>(rel) & 7u;
                     const u32 lo = sd.x << (4 * o), hi = o ? (sd.x >> (32 - 4 * o)) : 0u;
