@@ -103,6 +103,13 @@ __device__ __forceinline__ u32 pal_lookup4(u32 sel16, u32 p0, u32 p1, u32 p2, u3
 // nibble mask (4 nibbles, each 0 or 0xF, low 16 bits) -> byte mask
 __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0xFFFFFFFFu, nm16 & 0x4444u); }
 
+// 4 colour numbers (bytes <= 0x3F) -> their 24-bit 6-bit group in bits 0-23 (rl/csrc/rlenv.cu:126-134 layout) with
+// leftovers in bits 24-25, which the joins of groups into words mask off: two shift + merge steps.
+__device__ __forceinline__ u32 pack_group6_loose(u32 w) {
+    const u32 u = w ^ ((w ^ (w >> 2)) & 0x0FC00FC0u);   // c0 | c1 << 6 in bits 0-11, c2 | c3 << 6 in bits 16-27
+    return u ^ ((u ^ (u >> 4)) & 0xFFFFF000u);           // bits 16-27 down to 12-23
+}
+
 // 4 colour numbers (bytes) -> one 24-bit 6-bit group (rl/csrc/rlenv.cu:126-134 layout)
 __device__ __forceinline__ u32 pack_group6(u32 w) {
     return (w & 0x3Fu) | ((w >> 2) & 0xFC0u) | ((w >> 4) & 0x3F000u) | ((w >> 6) & 0xFC0000u);
@@ -680,16 +687,20 @@ struct Renderer {
         const u32 g = lane >> 3, j = lane & 7u;
         const u32 lt = (1u << lane) - 1u;
         uint2* sbuf = reinterpret_cast<uint2*>(W.px);   // [4 lines][8 sprites] (colour nibbles, meta)
-        // Lines that can show a sprite: one at y is found by the evaluation at the end of lines y..y+15 (height <= 16)
-        // and drawn on lines y+1..y+16. A superset; iterations whose 4 lines have none skip the sprite work.
+        // Lines that can show a sprite: one at y is found by the evaluation at the end of lines y..y+h-1 (height h) and
+        // drawn on lines y+1..y+h. A superset; iterations whose 4 lines have none skip the sprite work.
         u32* may = reinterpret_cast<u32*>(W.emph);   // 8 words: bit l of the 256-line mask
         u8* vis = W.emph + 32;                       // OAM indices of the sprites that can show, in OAM order
         u32* ov = reinterpret_cast<u32*>(W.emph + 96);   // per lane: bit r = sprite rank r of its line reaches its pixels
         u32 nv;
         {
-            auto span = [](u32 sp, u32 base) -> u32 {
+            // 8x16 sprites on any line of the frame (control bit 5 in the records): 16 lines per sprite, else 8
+            u32 tall = 0;
+            for (u32 l = lane; l < static_cast<u32>(kObsY0 + kObsH); l += 32) tall |= F.rec[l].x;
+            const int extra = __any_sync(0xFFFFFFFFu, (tall >> 20) & 1u) ? 15 : 7;
+            auto span = [extra](u32 sp, u32 base) -> u32 {
                 const int lo = static_cast<int>(sp & 0xFFu) + 1 - static_cast<int>(base);
-                const int hi = lo + 15;
+                const int hi = lo + extra;
                 if (hi < 0 || lo > 31) return 0u;
                 const u32 a = lo < 0 ? 0u : static_cast<u32>(lo), b = hi > 31 ? 31u : static_cast<u32>(hi);
                 return (0xFFFFFFFFu >> (31u - b)) & (0xFFFFFFFFu << a);
@@ -825,15 +836,15 @@ struct Renderer {
             } else {
                 u32 gq[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) gq[q] = pack_group6(px[q]);
+                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);   // px bytes are <= 0x3F (keep mask)
                 u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3) + 24u * j);
-                row[0] = gq[0] | (gq[1] << 24);
-                row[1] = (gq[1] >> 8) | (gq[2] << 16);
-                row[2] = (gq[2] >> 16) | (gq[3] << 8);
+                row[0] = (gq[0] & 0xFFFFFFu) | (gq[1] << 24);
+                row[1] = ((gq[1] >> 8) & 0xFFFFu) | (gq[2] << 16);
+                row[2] = ((gq[2] >> 16) & 0xFFu) | (gq[3] << 8);
                 if (j < 7) {
-                    row[3] = gq[4] | (gq[5] << 24);
-                    row[4] = (gq[5] >> 8) | (gq[6] << 16);
-                    row[5] = (gq[6] >> 16) | (gq[7] << 8);
+                    row[3] = (gq[4] & 0xFFFFFFu) | (gq[5] << 24);
+                    row[4] = ((gq[5] >> 8) & 0xFFFFu) | (gq[6] << 16);
+                    row[5] = ((gq[6] >> 16) & 0xFFu) | (gq[7] << 8);
                 }
             }
             __syncwarp();   // sbuf is rewritten by the next iteration
