@@ -175,6 +175,8 @@ struct Emu {
     u32 ctrl, mask, status, oam_addr, nmi;
     u32 log_n, log_ctl;
     u32 now;
+    u32 pend;     // PPU dots run since frame_dot (not yet settled) during step_until
+    u32 resched;  // MMC3: a store changed what the scanline counter does; the next event is recomputed
     u32 dma;
     u32 slot;     // presentation slot of the frame being emulated
     u32 prg_bank; // UxROM
@@ -228,6 +230,8 @@ struct Emu {
         log_n = rw(R_LOGN) & 0xFFFF;
         dma = 0;
         now = 0;
+        pend = 0;
+        resched = 0;
     }
     __device__ __forceinline__ void store() {
         ww(R_PC_SP_P, pc | (sp << 16) | (p << 24));
@@ -478,19 +482,22 @@ struct Emu {
         const u32 s0 = rw(R_S0) & kS0DotMask;
         if (s0 != 0) next = min(next, dist(s0));
         if constexpr (BOARD == kMmc3) {
-            const u32 line = cur / kDots, dot = cur % kDots;
-            u32 clock;
-            if (line < 240) {
-                clock = dot < kMmc3VisibleClock ? kMmc3VisibleClock - dot
-                      : line + 1 < 240 ? kDots - dot + kMmc3VisibleClock
-                                       : (261 - line) * kDots + kMmc3PreClock - dot;
-            } else if (line < 261) {
-                clock = (261 - line) * kDots + kMmc3PreClock - dot;
-            } else {
-                clock = dot < kMmc3PreClock ? kMmc3PreClock - dot : kDots - dot + kMmc3VisibleClock;
+            // Only the scanline-counter clock that raises the IRQ is an event: the clocks before it change the
+            // counter alone and settle applies them in one pass. Nothing changes what they do but a store to
+            // $2000 / $2001 or to the IRQ registers, and those settle first and reschedule (step6502).
+            if ((mask & 0x18u) != 0 && (ctrl & 0x38u) != 0x18u && mreg(13) != 0) {
+                const u32 c = mreg(12), lat = mreg(11);
+                const u32 c1 = (c == 0 || mreg(14) != 0) ? lat : c - 1;   // the counter after the next clock
+                const u32 line = cur / kDots, dot = cur % kDots;
+                // this frame's clocks: index 0..239 the visible lines, 240 the pre-render line; i0 = the next one
+                const u32 i0 = line < 240 ? line + (dot >= kMmc3VisibleClock ? 1u : 0u)
+                                          : (line < 261 || dot < kMmc3PreClock) ? 240u : 241u;
+                const u32 i = i0 + c1;   // the (c1 + 1)-th clock from here leaves the counter at 0
+                if (i <= 240) {
+                    const u32 t = i < 240 ? i * kDots + kMmc3VisibleClock : 261u * kDots + kMmc3PreClock;
+                    next = min(next, t - cur);
+                }
             }
-            if (cur + clock >= kFrameDots) clock -= skip;
-            next = min(next, clock);
         }
         return next;
     }
@@ -1020,13 +1027,22 @@ struct Emu {
                 break;
             }
         }
+        if constexpr (BOARD == kMmc3) {
+            // $2000 / $2001 (and mirrors) or the IRQ registers: the counter's clocks up to this instruction run
+            // under the old values first, exactly as when every clock was its own event
+            if (store && ((ea & 0xE006u) == 0x2000u || ea >= 0xC000u)) {
+                if (pend != 0) { settle(pend); pend = 0; }
+                resched = 1;
+            }
+        }
         if (store) wr(ea, wv);
         cycles += cyc;
         return Step{cyc, op, pc0, false};
     }
 
     // One instruction with NMI / IRQ entry, frame-log stamps, DMA stall and DMC steals (patch:834-861).
-    __device__ __forceinline__ Step console_step(u32 pending, u32& ppu_cycles) {
+    __device__ __forceinline__ Step console_step(u32& ppu_cycles) {
+        const u32 pending = pend;
         const u64 before = cycles;
         if (nmi) {
             nmi = 0;
@@ -1065,7 +1081,9 @@ struct Emu {
     // execute, so lanes that skipped a block wait for the others and the warp runs one instruction body per turn.
     // Every lane's own state advances exactly as in the sequential loop.
     __device__ __forceinline__ u32 step_until(u64 target, bool run) {
-        u32 fault = 0, pending = 0;
+        u32 fault = 0;
+        pend = 0;
+        resched = 0;
         u32 to_event = run ? dots_to_event() : 0u;
         u32 instructions = 0;
         bool going = run;
@@ -1073,27 +1091,31 @@ struct Emu {
             const u32 lead = __reduce_min_sync(0xFFFFFFFFu, going ? pc : 0x10000u);
             if (!going || pc != lead) continue;
             if (instructions >= kBudget) { going = false; continue; }
-            if (pending >= to_event) {
-                settle(pending);
-                pending = 0;
+            if (pend >= to_event) {
+                settle(pend);
+                pend = 0;
                 to_event = dots_to_event();
                 if (frame * kFrameDots + frame_dot >= target) { going = false; continue; }
             }
             u32 pc_cycles;
-            const Step st = console_step(pending, pc_cycles);
+            const Step st = console_step(pc_cycles);
             if (st.illegal) { fault = (st.pc << 8) | st.opcode; going = false; continue; }
-            pending += pc_cycles;
+            pend += pc_cycles;
             ++instructions;
+            if constexpr (BOARD == kMmc3) {
+                if (resched) { resched = 0; to_event = dots_to_event(); }   // from the settled frame_dot
+            }
             if (st.opcode == 0x4Cu && pc == st.pc) {
-                settle(pending);
-                pending = 0;
+                settle(pend);
+                pend = 0;
                 if (frame * kFrameDots + frame_dot >= target) { going = false; continue; }
                 fast_forward();
                 to_event = dots_to_event();
                 if (frame * kFrameDots + frame_dot >= target) going = false;
             }
         }
-        if (pending != 0) settle(pending);
+        if (pend != 0) settle(pend);
+        pend = 0;
         return fault;
     }
 
