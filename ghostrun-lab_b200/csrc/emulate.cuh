@@ -303,6 +303,7 @@ struct Emu {
         addr &= 0x1FFFu;
         if constexpr (board_paged(BOARD)) addr = (rw(R_CHRPG + (addr >> 10)) + (addr & 0x3FFu)) & 0x1FFFu;
         chr_ram()[addr] = static_cast<u8>(v);
+        ww(R_CHRD, 1u);
     }
     __device__ __forceinline__ u32 nt_off(u32 addr) const {
         if constexpr (board_paged(BOARD)) return nt_off_map(mirroring(), addr);
@@ -441,6 +442,24 @@ struct Emu {
     // After step_until (all 32 lanes): the nametable RAM, OAM (and CHR-RAM) of every lane that froze a frame into
     // presentation slot `slot`, copied by the whole warp. Nothing runs between the vblank and the end of the frame's
     // step_until (the frame's target is the vblank dot), so the memories are still as frozen.
+    // At a launch's start (all 32 lanes): envs whose CHR-RAM was written since their shared CHR snapshot take a new
+    // one. No slot of the frames to come points at the old one yet, and earlier slots have been drawn.
+    __device__ __forceinline__ void refresh_shared_chr(bool valid) {
+        if (!S.chr_shared || C.chr) return;
+        u32 pend = __ballot_sync(0xFFFFFFFFu, valid && rw(R_CHRD) != 0u);
+        while (pend) {
+            const u32 L = __ffs(pend) - 1;
+            pend &= pend - 1;
+            const u32 eL = __shfl_sync(0xFFFFFFFFu, e, L);
+            const uint4* cv = reinterpret_cast<const uint4*>(S.chr_ram + static_cast<u64>(eL) * kChrRamBytes);
+            uint4* dc = reinterpret_cast<uint4*>(S.chr_shared + static_cast<u64>(eL) * kChrRamBytes);
+#pragma unroll 4
+            for (u32 i = lane; i < kChrRamBytes / 16; i += 32) dc[i] = cv[i];
+        }
+        __syncwarp();
+        if (valid) ww(R_CHRD, 0u);
+    }
+
     __device__ __forceinline__ void snapshot_frozen() {
         u32 pend = __ballot_sync(0xFFFFFFFFu, froze != 0);
         while (pend) {
@@ -457,10 +476,15 @@ struct Emu {
             dnt[lane] = q0; dnt[lane + 32] = q1; dnt[lane + 64] = q2; dnt[lane + 96] = q3;
             doam[lane] = o0; doam[lane + 32] = o1;
             if (S.snap_chr && !C.chr) {
-                const uint4* cv = reinterpret_cast<const uint4*>(S.chr_ram + static_cast<u64>(eL) * kChrRamBytes);
-                uint4* dc = reinterpret_cast<uint4*>(S.snap_chr + sl * kChrRamBytes);
+                // no CHR-RAM write since the shared snapshot: the slot points at it, else it takes its own copy
+                const bool shared = S.chr_shared && sh.regs[R_CHRD][L] == 0u;
+                if (lane == 0 && S.chr_ref) S.chr_ref[sl] = shared ? 1u : 0u;
+                if (!shared) {
+                    const uint4* cv = reinterpret_cast<const uint4*>(S.chr_ram + static_cast<u64>(eL) * kChrRamBytes);
+                    uint4* dc = reinterpret_cast<uint4*>(S.snap_chr + sl * kChrRamBytes);
 #pragma unroll 4
-                for (u32 i = lane; i < kChrRamBytes / 16; i += 32) dc[i] = cv[i];
+                    for (u32 i = lane; i < kChrRamBytes / 16; i += 32) dc[i] = cv[i];
+                }
             }
         }
         froze = 0;
@@ -1127,7 +1151,11 @@ struct Emu {
         const u64 a0 = static_cast<u64>(e) * 4 + fs, b0 = static_cast<u64>(e) * 4 + slot;
         copy16(S.snap_nt + b0 * kNtBytes, S.snap_nt + a0 * kNtBytes, kNtBytes);
         copy16(S.snap_oam + b0 * kOamBytes, S.snap_oam + a0 * kOamBytes, kOamBytes);
-        if (S.snap_chr && !C.chr) copy16(S.snap_chr + b0 * kChrRamBytes, S.snap_chr + a0 * kChrRamBytes, kChrRamBytes);
+        if (S.snap_chr && !C.chr) {
+            const bool shared = S.chr_ref && S.chr_ref[a0] != 0u;
+            if (S.chr_ref) S.chr_ref[b0] = shared ? 1u : 0u;
+            if (!shared) copy16(S.snap_chr + b0 * kChrRamBytes, S.snap_chr + a0 * kChrRamBytes, kChrRamBytes);
+        }
         S.slot_bank[b0] = S.slot_bank[a0];
         ww(R_FSLOT, slot);
     }

@@ -324,7 +324,8 @@ struct EnvArgs {
 static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, bool chr_ram, u32 tid = 0, u32 nt = 1) {
     const u32* rr = reinterpret_cast<const u32*>(rec + kRecRegs);
     for (u32 w = tid; w < static_cast<u32>(kRegWords); w += nt)
-        S.regs[static_cast<u64>(w) * S.Np + e] = w == static_cast<u32>(R_FSLOT) ? 0u : rr[w];
+        S.regs[static_cast<u64>(w) * S.Np + e] = w == static_cast<u32>(R_FSLOT) ? 0u
+                                                : w == static_cast<u32>(R_CHRD) ? 1u : rr[w];   // shared CHR stale
     const u32* ram = reinterpret_cast<const u32*>(rec + kRecRam);
     for (u32 i = tid; i < kRamWords; i += nt) S.ram[static_cast<u64>(i) * S.Np + e] = ram[i];
     const u32* pr = reinterpret_cast<const u32*>(rec + kRecPrgRam);
@@ -343,7 +344,10 @@ static __device__ void scatter_record(const StateView& S, u32 e, const u8* rec, 
     cp(S.snap_nt + sl * kNtBytes, rec + kRecSnapNt, kNtBytes);
     cp(S.snap_oam + sl * kOamBytes, rec + kRecSnapOam, kOamBytes);
     if (chr_ram && S.snap_chr) cp(S.snap_chr + sl * kChrRamBytes, rec + kRecChrRam, kChrRamBytes);
-    if (tid == 0) S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
+    if (tid == 0) {
+        S.slot_bank[sl] = static_cast<u8>((rr[R_PPU2] >> 8) & kLcBank);
+        if (S.chr_ref) S.chr_ref[sl] = 0;
+    }
 }
 
 // The snapshot record an episode restarts from: a saved level start, the boot snapshot after k idle frames, or the
@@ -500,6 +504,7 @@ __global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameAr
         Emu<BOARD> m(A.st, g.cart, valid ? ge : g.e0, lane, sh, dtab, prg_s);
         m.froze = 0;
         if (valid) { m.stage_in(); m.load(); }
+        m.refresh_shared_chr(valid);
         u32 fault = valid ? A.fault[ge] : 0u;
         u64 target = valid ? A.target[ge] : 0ull;
         u32 ep_frame = valid ? A.ep_frame[ge] : 0u;
@@ -679,7 +684,10 @@ static __global__ void __launch_bounds__(128) k_restore(const __grid_constant__ 
                     uint4* dc = reinterpret_cast<uint4*>(A.st.snap_chr + s4 * kChrRamBytes);
                     for (u32 i = threadIdx.x; i < 4 * kChrRamBytes / 16; i += blockDim.x) dc[i] = sc[i];
                 }
-                if (threadIdx.x < 4) A.st.slot_bank[s4 + threadIdx.x] = g.tm_bank[t4 + threadIdx.x];
+                if (threadIdx.x < 4) {
+                    A.st.slot_bank[s4 + threadIdx.x] = g.tm_bank[t4 + threadIdx.x];
+                    if (A.st.chr_ref) A.st.chr_ref[s4 + threadIdx.x] = 0;   // the template's copies are the slots' own
+                }
             }
             if (!A.no_render) {   // the first observation: colour numbers, or 6-bit packed (4 pixels -> 3 bytes)
                 const u32* px = reinterpret_cast<const u32*>(g.tm_pix + t4 * kObsPixels);
@@ -767,10 +775,14 @@ static __global__ void __launch_bounds__(128) k_tmpl_capture(const __grid_consta
         const uint4* so = reinterpret_cast<const uint4*>(A.st.snap_oam + s4 * kOamBytes);
         uint4* doam = reinterpret_cast<uint4*>(g.tm_oam + t4 * kOamBytes);
         for (u32 i = threadIdx.x; i < 4 * kOamBytes / 16; i += blockDim.x) doam[i] = so[i];
-        if (chr_ram && A.st.snap_chr) {
-            const uint4* sc = reinterpret_cast<const uint4*>(A.st.snap_chr + s4 * kChrRamBytes);
-            uint4* dc = reinterpret_cast<uint4*>(g.tm_chr + t4 * kChrRamBytes);
-            for (u32 i = threadIdx.x; i < 4 * kChrRamBytes / 16; i += blockDim.x) dc[i] = sc[i];
+        if (chr_ram && A.st.snap_chr) {   // each slot's CHR as drawn (its own copy or the env's shared one)
+            for (u32 f = 0; f < 4; ++f) {
+                const bool shared = A.st.chr_ref && A.st.chr_ref[s4 + f];
+                const uint4* sc = reinterpret_cast<const uint4*>(
+                    shared ? A.st.chr_shared + static_cast<u64>(ge) * kChrRamBytes : A.st.snap_chr + (s4 + f) * kChrRamBytes);
+                uint4* dc = reinterpret_cast<uint4*>(g.tm_chr + (t4 + f) * kChrRamBytes);
+                for (u32 i = threadIdx.x; i < kChrRamBytes / 16; i += blockDim.x) dc[i] = sc[i];
+            }
         }
         if (threadIdx.x < 4) g.tm_bank[t4 + threadIdx.x] = A.st.slot_bank[s4 + threadIdx.x];
     }

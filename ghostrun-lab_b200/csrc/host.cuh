@@ -50,6 +50,10 @@ inline StateView alloc_state_view(DevMem& M, u32 Np, bool chr_ram, bool saved) {
     S.snap_oam = M.allocn<u8>(static_cast<std::size_t>(4) * kOamBytes * Np, saved);
     S.snap_chr = chr_ram ? M.allocn<u8>(static_cast<std::size_t>(4) * kChrRamBytes * Np, saved) : nullptr;
     S.slot_bank = M.allocn<u8>(static_cast<std::size_t>(4) * Np, saved);
+    if (chr_ram && saved) {   // the main state only (scratch views copy every frame)
+        S.chr_shared = M.allocn<u8>(static_cast<std::size_t>(kChrRamBytes) * Np, saved);
+        S.chr_ref = M.allocn<u8>(static_cast<std::size_t>(4) * Np, saved);
+    }
     return S;
 }
 

@@ -74,6 +74,7 @@ enum RegWord : int {
     R_DMC_B,                 // rate | buffer_full << 8
     R_DMC_EV,                // 2 words: DMC event cycle
     R_FSLOT = R_DMC_EV + 2,  // presentation slot holding the last frozen frame (0..3)
+    R_CHRD,                  // CHR-RAM carts: 1 = CHR-RAM written since the env's shared CHR snapshot was taken
     kRegWords
 };
 
@@ -137,6 +138,10 @@ struct StateView {
     u8* snap_nt;     // [Np][4][2048] nametable RAM frozen at each frame's vblank
     u8* snap_oam;    // [Np][4][256]
     u8* snap_chr;    // [Np][4][8192] (CHR-RAM carts)
+    // CHR-RAM carts: one shared snapshot per env, taken when a launch starts with CHR-RAM written since the last one;
+    // a frame frozen with no CHR-RAM write since then points at it (chr_ref = 1) instead of copying 8 KB
+    u8* chr_shared;  // [Np][8192], nullptr: every slot keeps its own copy
+    u8* chr_ref;     // [Np][4]
     u8* slot_bank;   // [Np][4] frame-log bank shown by presentation slot f
 };
 

@@ -161,6 +161,12 @@ struct Renderer {
                            (W.pal[2] & 0x3F3F3F00u) | bd, (W.pal[3] & 0x3F3F3F00u) | bd);
     }
     __device__ __forceinline__ u32 pal_byte(u32 i) const { return reinterpret_cast<const u8*>(W.pal)[i]; }
+    // the CHR-RAM a presentation slot was frozen with (its own copy or the env's shared snapshot); CHR ROM: nullptr
+    __device__ __forceinline__ const u8* slot_chr(u32 ge, u64 sl) const {
+        if (A.cart.chr != nullptr || !A.st.snap_chr) return nullptr;
+        if (A.st.chr_ref && A.st.chr_ref[sl]) return A.st.chr_shared + static_cast<u64>(ge) * kChrRamBytes;
+        return A.st.snap_chr + sl * kChrRamBytes;
+    }
     __device__ __forceinline__ static constexpr bool paged() { return board_paged(BOARD); }
 
     __device__ __forceinline__ u32 nt_rd(u32 mir, u32 addr) const {
@@ -672,7 +678,7 @@ struct Renderer {
     }
     __device__ void draw_fast(u32 ge, u32 f, const FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
         const u64 sl = static_cast<u64>(ge) * 4 + f;
-        chr_ram = (A.cart.chr == nullptr && A.st.snap_chr) ? A.st.snap_chr + sl * kChrRamBytes : nullptr;
+        chr_ram = slot_chr(ge, sl);
         {   // the frame's nametable into shared memory, its OAM into registers (2 entries per lane)
             const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
             uint4* nts = reinterpret_cast<uint4*>(W.nt);
@@ -864,7 +870,7 @@ struct Renderer {
         ev = h + kLogHdr;
         count = min(h[0] & ~kLogOverflow, kLogEv);
         kook = (h[15] & kLogKook) ? 1 : 0;
-        chr_ram = (A.cart.chr == nullptr && A.st.snap_chr) ? A.st.snap_chr + sl * kChrRamBytes : nullptr;
+        chr_ram = slot_chr(ge, sl);
         {   // the frame's nametable into shared memory, its OAM into registers (2 entries per lane)
             const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
             uint4* nts = reinterpret_cast<uint4*>(W.nt);
