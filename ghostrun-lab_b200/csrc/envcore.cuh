@@ -900,12 +900,19 @@ __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_co
     for (u32 k = blockIdx.x * kRenderWarps + wid; k < items; k += gridDim.x * kRenderWarps) {
         u32 ge, f;
         if (!render_item(R, k, ge, f)) continue;
-        rd.walk_frame(ge, f, RW.fw);
         const u64 sl = static_cast<u64>(ge) * 4 + f;
-        if (lane == 0) R.seqf[sl] = RW.fw.seq ? 1u : 0u;
-        if (!RW.fw.seq) {
+        if constexpr (Renderer<BOARD>::kSplitLines) {   // the walk draws the lines with mid-line writes itself
             u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
-            rd.draw_fast(ge, f, RW.fw, out, R.emph + sl * kObsH, R.packed != nullptr);
+            rd.walk_frame(ge, f, RW.fw, out, R.packed != nullptr);
+            if (lane == 0) R.seqf[sl] = RW.fw.seq ? 1u : 0u;
+            if (!RW.fw.seq) rd.draw_fast(ge, f, RW.fw, out, R.emph + sl * kObsH, R.packed != nullptr);
+        } else {
+            rd.walk_frame(ge, f, RW.fw, nullptr, false);
+            if (lane == 0) R.seqf[sl] = RW.fw.seq ? 1u : 0u;
+            if (!RW.fw.seq) {
+                u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
+                rd.draw_fast(ge, f, RW.fw, out, R.emph + sl * kObsH, R.packed != nullptr);
+            }
         }
         __syncwarp();
     }

@@ -55,6 +55,7 @@ struct FrameWalk {   // per frame, shared memory
     uint4 spal[kWalkVers];       // sprite sub-palettes & 0x3F
     u32 chr[kWalkVers][8];       // CHR pages per version
     u32 seq;                     // 1: the frame takes the sequential path (Renderer::draw)
+    u32 split[8];                // bit l: line l was drawn exactly by the walk (a write inside its drawn part)
 };
 
 struct RenderArgs {
@@ -142,6 +143,8 @@ struct Renderer {
     const u8* chr_ram;   // per-frame CHR-RAM snapshot, nullptr on CHR-ROM carts
     u32 spA, spB;        // OAM entries lane and lane + 32: y | tile << 8 | attr << 16 | x << 24
     RState s;
+    int xs_line;         // the last line the walk drew exactly, -1 none; its final shift registers:
+    u32 xs_sh0, xs_sh1, xs_at;
 
     __device__ Renderer(const RenderArgs& a, u32 ln, const u32* cx, const u32* sp, RWarp& w)
         : A(a), lane(ln), chrx(cx), spread(sp), W(w) {}
@@ -168,6 +171,7 @@ struct Renderer {
         return A.st.snap_chr + sl * kChrRamBytes;
     }
     __device__ __forceinline__ static constexpr bool paged() { return board_paged(BOARD); }
+    static constexpr bool kSplitLines = BOARD == kMmc3;   // the walk draws mid-line-write lines itself
 
     __device__ __forceinline__ u32 nt_rd(u32 mir, u32 addr) const {
         if constexpr (paged()) return W.nt[nt_off_map(mir, addr)];
@@ -570,18 +574,159 @@ struct Renderer {
         }
         return th | nty | ((y & 7u) << 12) | ((y >> 3) << 5);
     }
+    // The frame's nametable into shared memory, its OAM into registers (2 entries per lane), its CHR-RAM (all lanes).
+    __device__ void load_frame(u32 ge, u32 f) {
+        const u64 sl = static_cast<u64>(ge) * 4 + f;
+        chr_ram = slot_chr(ge, sl);
+        const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
+        uint4* nts = reinterpret_cast<uint4*>(W.nt);
+        const uint4 q0 = ntg[lane], q1 = ntg[lane + 32], q2 = ntg[lane + 64], q3 = ntg[lane + 96];
+        const u32* oamw = reinterpret_cast<const u32*>(A.st.snap_oam + sl * kOamBytes);
+        spA = oamw[lane];
+        spB = oamw[lane + 32];
+        __syncwarp();
+        nts[lane] = q0; nts[lane + 32] = q1; nts[lane + 64] = q2; nts[lane + 96] = q3;
+        __syncwarp();
+    }
+
+    // Line l with a write inside its drawn part, drawn exactly by the whole warp during the walk (all lanes hold
+    // the walk's state w): the sequential renderer's state at the start of line l from the walk (registers,
+    // palette and CHR-page versions, the frame log cursor), the shift registers of the last line drawn with
+    // rendering on (fetches 32 / 33 of that line, or the exact ones of a line drawn here), the sprites fetched at
+    // the end of line l - 1; then exact_line, CopySprites, greyscale and the row's output as in draw. Returns with
+    // the registers the line's writes left in s (the caller hands them back to the walk).
+    __device__ void split_line(FrameWalk& F, const Walk& w, int l, u8* obs_out, bool pack6) {
+        s.v = w.v; s.t = w.t; s.x = w.x; s.ctrl = w.ctrl; s.mask = w.mask; s.mirroring = w.mir;
+        if (lane < 8) { W.pal[lane] = F.pal[w.pv][lane]; W.chr[lane] = F.chr[w.cv][lane]; }
+        __syncwarp();
+        if (lane == 0) make_bgp();
+        ev = w.ev; count = w.count; kook = w.kook;
+        s.cursor = w.cursor; s.next_t = w.next_t;
+        s.lazy = 0; s.lz_saved = 0; s.sh0 = s.sh1 = s.at = 0;
+        int j = l - 1;
+        while (j >= 0 && !(F.rec[j].y & 0x18u)) --j;
+        if (j >= 0 && j == xs_line) {
+            s.sh0 = xs_sh0; s.sh1 = xs_sh1; s.at = xs_at;
+        } else if (j >= 0) {
+            const uint2 rj = F.rec[j];
+            s.lazy = 1; s.lz_v = rj.x & 0x7FFFu; s.lz_ctrl = ((rj.x >> 18) & 7u) << 3; s.lz_mir = (rj.x >> 21) & 0xFu;
+            if (lane < 8) W.lzchr[lane] = F.chr[(rj.y >> 12) & 3u][lane];
+            s.lz_saved = 1;
+        }
+        // the sprites drawn on line l: fetched at the end of line l - 1 and refreshed there
+        s.fb = 0; s.nd = 0; s.nf = 0; s.spork = 0;
+        if (l >= 1) {
+            const uint2 re = F.rec[l - 1];
+            if ((re.y & 0x18u) && (re.y & (1u << 16))) {
+                const u32 c = ((re.x >> 18) & 7u) << 3;
+                const u32 hgt = (c & 0x20u) ? 16u : 8u;
+                const int e = l - 1;
+                const bool in0 = static_cast<u32>(e - static_cast<int>(spA & 0xFFu)) < hgt;
+                const bool in1 = static_cast<u32>(e - static_cast<int>(spB & 0xFFu)) < hgt;
+                const u32 b0 = __ballot_sync(0xFFFFFFFFu, in0), b1 = __ballot_sync(0xFFFFFFFFu, in1);
+                if (b0 | b1) {
+                    RSprites& d = W.spr[1];
+                    const u32* pages = F.chr[(re.y >> 12) & 3u];
+                    const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
+                    const u32 lt = (1u << lane) - 1u;
+                    const u32 r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const bool in = half ? in1 : in0;
+                        const u32 r = half ? r1 : r0;
+                        if (in && r < 8) {
+                            const u32 sp = half ? spB : spA;
+                            const u32 tile = (sp >> 8) & 0xFFu, attr = (sp >> 16) & 0xFFu, xx = sp >> 24;
+                            const u32 t = static_cast<u32>(e - static_cast<int>(sp & 0xFFu));
+                            u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+                            if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (c & 0x20u) >> 1; vadr -= t & 8u; }
+                            else { vadr += t; vadr += t & 8u; }
+                            u32 cw = chr_sel(pages, vadr & 0x1FFFu);
+                            if (attr & 0x40u) cw = nib_reverse(cw);
+                            d.cw[r] = cw;
+                            d.meta[r] = (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8);
+                        }
+                    }
+                    s.nd = min(__popc(b0) + __popc(b1), 8);
+                    s.spork = 1;
+                }
+                const uint4 sp4 = F.spal[(re.y >> 20) & 3u];
+                s.spal[0] = sp4.x; s.spal[1] = sp4.y; s.spal[2] = sp4.z; s.spal[3] = sp4.w;
+            }
+        }
+        s.sphitx = 0x100u; s.blurp = 0; s.hit = 0; s.sphitmask = 0; s.hit_x = 0;
+        __syncwarp();
+        exact_line(l);
+        xs_line = l; xs_sh0 = s.sh0; xs_sh1 = s.sh1; xs_at = s.at;
+        const uint2 q = reinterpret_cast<const uint2*>(W.px)[lane];
+        u32 w0 = q.x, w1 = q.y;
+        if ((s.mask & 0x10u) && s.spork) {   // CopySprites (patch:1615-1640)
+            const RSprites& d = W.spr[1];
+            u32 snib = 0, sany = 0, sbeh = 0;
+            const int base = static_cast<int>(lane) * 8;
+            for (int i = static_cast<int>(s.nd) - 1; i >= 0; --i) {
+                const u32 meta = d.meta[i];
+                const int dx = static_cast<int>(meta >> 8) - base;
+                if (dx <= -8 || dx >= 8) continue;
+                const u32 cw = d.cw[i];
+                const u32 win = dx >= 0 ? (cw << (4 * dx)) : (cw >> (4 * -dx));
+                const u32 om = ((win | (win >> 1)) & 0x11111111u) * 0xFu;
+                const u32 pw = (meta & 3u) * 0x44444444u;
+                snib = (snib & ~om) | ((win | pw) & om);
+                sany |= om;
+                sbeh = (meta & 4u) ? (sbeh | om) : (sbeh & ~om);
+            }
+            if (lane == 0 && !(s.mask & 0x04u)) sany = 0;
+            if (sany) {
+                const u32 c0 = pal_lookup4(snib, s.spal[0], s.spal[1], s.spal[2], s.spal[3]);
+                const u32 c1 = pal_lookup4(snib >> 16, s.spal[0], s.spal[1], s.spal[2], s.spal[3]);
+                const u32 any0 = nib_to_bytes(sany), any1 = nib_to_bytes(sany >> 16);
+                const u32 beh0 = nib_to_bytes(sbeh), beh1 = nib_to_bytes(sbeh >> 16);
+                const u32 tr0 = ((w0 & 0x40404040u) >> 6) * 0xFFu, tr1 = ((w1 & 0x40404040u) >> 6) * 0xFFu;
+                const u32 use0 = any0 & (~beh0 | tr0), use1 = any1 & (~beh1 | tr1);
+                w0 = (w0 & ~use0) | (c0 & use0);
+                w1 = (w1 & ~use1) | (c1 & use1);
+            }
+        }
+        const u32 keep = ((s.mask & 1u) && (s.mask & 0x18u)) ? 0x30303030u : 0x3F3F3F3Fu;
+        w0 &= keep;
+        w1 &= keep;
+        if (l >= kObsY0) {
+            const int y = l - kObsY0;
+            if (!pack6) {
+                if (lane >= 1 && lane <= 30)
+                    reinterpret_cast<uint2*>(obs_out + static_cast<u64>(y) * kObsW)[lane - 1] = make_uint2(w0, w1);
+            } else {
+                const u32 g0 = pack_group6(w0), g1 = pack_group6(w1);
+                const u32 n0 = __shfl_down_sync(0xFFFFFFFFu, g0, 1), n1 = __shfl_down_sync(0xFFFFFFFFu, g1, 1);
+                if ((lane & 1u) && lane <= 29) {
+                    u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3)) + 3 * ((lane - 1) >> 1);
+                    row[0] = g0 | (g1 << 24);
+                    row[1] = (g1 >> 8) | (n0 << 16);
+                    row[2] = (n0 >> 16) | (n1 << 8);
+                }
+            }
+        }
+        __syncwarp();
+    }
+
     // ---- phase 1 for frame f of env ge (the whole warp): lane 0 replays the frame log's events; every stretch of
     // lines without events is recorded by the 32 lanes at once, v from the closed form above (the record of such a
     // line is its start state, unchanged through the line).
-    __device__ void walk_frame(u32 ge, u32 f, FrameWalk& F) const {
+    __device__ void walk_frame(u32 ge, u32 f, FrameWalk& F, u8* obs_out, bool pack6) {
         constexpr int kLines = kObsY0 + kObsH;
+        if constexpr (kSplitLines) {   // the exact lines need the frame's memories now; the others load in draw_fast
+            load_frame(ge, f);
+            if (lane < 8) F.split[lane] = 0;
+            xs_line = -1;
+        }
         Walk w;
         int l = 0;
         bool done = false;
         if (lane == 0) walk_begin(ge, f, F, w);
         for (;;) {
             int run = 0;
-            u32 v = 0, xc = 0, ry = 0, th = 0, ren = 0;
+            u32 v = 0, xc = 0, ry = 0, th = 0, ren = 0, split = 0;
             if (lane == 0 && !done) {
                 if (w.seq) {
                     done = true;
@@ -596,6 +741,10 @@ struct Renderer {
                     ry = w.mask | (w.pv << 8) | (w.cv << 12) | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20);
                     th = w.t & 0x041Fu;
                     ren = (w.mask & 0x18u) ? 1u : 0u;
+                    // after the stretch: a line with a write inside its drawn part is drawn here, exactly (MMC3,
+                    // whose IRQ handlers split the screen; the other boards leave such frames to k_render_seq)
+                    const int ls = l + run;
+                    if constexpr (kSplitLines) split = (ls < kLines && w.next_t < ls * 341 - 16 + 272) ? 1u : 0u;
                 }
             }
             run = __shfl_sync(0xFFFFFFFFu, run, 0);
@@ -605,14 +754,46 @@ struct Renderer {
             ry = __shfl_sync(0xFFFFFFFFu, ry, 0);
             th = __shfl_sync(0xFFFFFFFFu, th, 0);
             ren = __shfl_sync(0xFFFFFFFFu, ren, 0);
+            if constexpr (kSplitLines) split = __shfl_sync(0xFFFFFFFFu, split, 0);
             for (int k = static_cast<int>(lane); k < run; k += 32)
                 F.rec[l0 + k] = make_uint2(v_after_lines(v, static_cast<u32>(k), th, ren != 0) | xc, ry);
             if (lane == 0 && !done) {
                 w.v = v_after_lines(w.v, static_cast<u32>(run), th, ren != 0);
                 l += run;
-                if (l < kLines) walk_line(w, F, l++);
-                if (l >= kLines || w.seq) done = true;
             }
+            if (kSplitLines && split) {
+                const int ls = l0 + run;
+                Walk wb;   // the leader's state, on every lane
+                wb.ctrl = __shfl_sync(0xFFFFFFFFu, w.ctrl, 0); wb.mask = __shfl_sync(0xFFFFFFFFu, w.mask, 0);
+                wb.x = __shfl_sync(0xFFFFFFFFu, w.x, 0); wb.v = __shfl_sync(0xFFFFFFFFu, w.v, 0);
+                wb.t = __shfl_sync(0xFFFFFFFFu, w.t, 0); wb.mir = __shfl_sync(0xFFFFFFFFu, w.mir, 0);
+                wb.pv = __shfl_sync(0xFFFFFFFFu, w.pv, 0); wb.cv = __shfl_sync(0xFFFFFFFFu, w.cv, 0);
+                wb.cursor = __shfl_sync(0xFFFFFFFFu, w.cursor, 0); wb.count = __shfl_sync(0xFFFFFFFFu, w.count, 0);
+                wb.kook = __shfl_sync(0xFFFFFFFFu, w.kook, 0); wb.next_t = __shfl_sync(0xFFFFFFFFu, w.next_t, 0);
+                wb.ev = reinterpret_cast<const u32*>(__shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(w.ev), 0));
+                __syncwarp();   // the leader's derive of this line's palette version is visible
+                split_line(F, wb, ls, obs_out, pack6);
+                if (lane == 0) {
+                    // the line's writes into the walk's copy-on-write tables; the exact registers replace the walk's
+                    while (w.cursor < s.cursor && !w.seq) walk_apply(w, F, true);
+                    w.v = s.v; w.t = s.t; w.x = s.x; w.ctrl = s.ctrl; w.mask = s.mask; w.mir = s.mirroring;
+                    const int start = ls * 341 - 16;
+                    const u32 rx = w.v | (w.x << 15) | (((w.ctrl >> 3) & 7u) << 18) | ((w.mir & 0xFu) << 21);
+                    const u32 ryl = w.mask | (w.pv << 8) | (w.cv << 12);
+                    const u32 fetch_mask = w.mask;
+                    while (w.next_t < start + 278 && !w.seq) walk_apply(w, F, true);
+                    if (w.mask & 0x18u) w.v = (w.v & 0xFBE0u) | (w.t & 0x041Fu);
+                    while (w.next_t < start + 341 && !w.seq) walk_apply(w, F, true);
+                    if (!w.pused) { derive(F, w.pv); w.pused = true; }
+                    if (!(fetch_mask & 0x18u) && (w.mask & 0x10u)) w.seq = 1;
+                    F.rec[ls] = make_uint2(rx, ryl | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20));
+                    F.split[ls >> 5] |= 1u << (ls & 31);
+                    l = ls + 1;
+                }
+            } else if (lane == 0 && !done) {
+                if (l < kLines) walk_line(w, F, l++);
+            }
+            if (lane == 0 && !done && (l >= kLines || w.seq)) done = true;
             if (__shfl_sync(0xFFFFFFFFu, done ? 1u : 0u, 0) != 0u) break;
         }
         if (lane == 0) F.seq = w.seq;
@@ -677,19 +858,7 @@ struct Renderer {
         return (bg & ~use) | (c & use);
     }
     __device__ void draw_fast(u32 ge, u32 f, const FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
-        const u64 sl = static_cast<u64>(ge) * 4 + f;
-        chr_ram = slot_chr(ge, sl);
-        {   // the frame's nametable into shared memory, its OAM into registers (2 entries per lane)
-            const uint4* ntg = reinterpret_cast<const uint4*>(A.st.snap_nt + sl * kNtBytes);
-            uint4* nts = reinterpret_cast<uint4*>(W.nt);
-            const uint4 q0 = ntg[lane], q1 = ntg[lane + 32], q2 = ntg[lane + 64], q3 = ntg[lane + 96];
-            const u32* oamw = reinterpret_cast<const u32*>(A.st.snap_oam + sl * kOamBytes);
-            spA = oamw[lane];
-            spB = oamw[lane + 32];
-            __syncwarp();
-            nts[lane] = q0; nts[lane + 32] = q1; nts[lane + 64] = q2; nts[lane + 96] = q3;
-            __syncwarp();
-        }
+        if constexpr (!kSplitLines) load_frame(ge, f);   // (boards with exact lines staged it in walk_frame)
         const u32 g = lane >> 3, j = lane & 7u;
         const u32 lt = (1u << lane) - 1u;
         uint2* sbuf = reinterpret_cast<uint2*>(W.px);   // [4 lines][8 sprites] (colour nibbles, meta)
@@ -835,7 +1004,10 @@ struct Renderer {
 #pragma unroll
             for (int q = 0; q < 8; ++q) px[q] &= keep;
             const int y = l - kObsY0;
-            if (!pack6) {
+            bool exact = false;
+            if constexpr (kSplitLines) exact = ((F.split[l >> 5] >> (l & 31)) & 1u) != 0u;   // drawn by the walk
+            if (exact) {
+            } else if (!pack6) {
                 uint4* row = reinterpret_cast<uint4*>(obs_out + static_cast<u64>(y) * kObsW + 32u * j);
                 row[0] = make_uint4(px[0], px[1], px[2], px[3]);
                 if (j < 7) row[1] = make_uint4(px[4], px[5], px[6], px[7]);
