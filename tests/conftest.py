@@ -28,7 +28,8 @@ def oracle_lib() -> Path:
 
 
 def reference_host_lib():
-    """The reference's own controller / reward10 host library (oracle/_ref, compiled from /root/reference), or None."""
+    """The reference's own controller / reward10 host library (oracle/_ref, compiled from the reference tree when it is
+    present), or None."""
     lib = ORACLE / '_ref' / 'librl_host.so'
     if not lib.exists() and Path('/root/reference/rl/csrc/host_api.cpp').exists():
         subprocess.run(['make', '-C', str(ORACLE), 'ref'], check=True, capture_output=True)

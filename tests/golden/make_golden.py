@@ -8,7 +8,7 @@
                          RAM reader and each synthetic game's seeded weights, on seeded random RAM traces of the
                          template's reward bytes ($10-$17).
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref REFERENCE_TREE]
 """
 from __future__ import annotations
 
