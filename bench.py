@@ -252,6 +252,11 @@ def render_traffic_per_env_frame():
     return None
 
 
+def rank_seed_for_stem(seed):
+    from shard import rank_seed
+    return rank_seed(seed, 0)
+
+
 def stem_arm(args):
     """The policy's input stem (rl_stem_fwd, tcgen05) on B = --envs samples of 6-bit packed pictures: samples/s.
     Roofline: HBM bytes (packed pictures + emphasis in, bf16 features out) per call / its CUDA-event time."""
@@ -296,6 +301,32 @@ def stem_arm(args):
     torch.cuda.synchronize()
     bwd_ms = b0.elapsed_time(b1) / K
     bwd_bytes = in_bytes + gout.numel() * 2
+    # the same on pictures the env drew (synth00, aged 64 decisions): runs of equal colours make the palette gathers
+    # broadcasts instead of bank conflicts
+    from rlenv import RlEnv
+    env = RlEnv({GAME: B}, device=dev, seed=rank_seed_for_stem(args.seed), sticky=True, idle_max=30, dropout=True)
+    env_px = torch.empty(B, 4, 224, 180, dtype=torch.uint8, device=dev)
+    env.bind_obs_pack6(env_px)
+    env.start()
+    for _ in range(64):
+        env.actions.copy_(torch.randint(0, 81, (B,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        env.step()
+    env_emph = env.emph.clone()
+    del env
+    for _ in range(W):
+        fused_stem(env_px, env_emph, pal, w, b, packed=True, check=False)
+        stem_backward(gout, env_px, env_emph, pal4, packed=True, check=False)
+    torch.cuda.synchronize()
+    r0, r1, r2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    r0.record()
+    for _ in range(K):
+        fused_stem(env_px, env_emph, pal, w, b, packed=True, check=False)
+    r1.record()
+    for _ in range(K):
+        stem_backward(gout, env_px, env_emph, pal4, packed=True, check=False)
+    r2.record()
+    torch.cuda.synchronize()
+    env_fwd_ms, env_bwd_ms = r0.elapsed_time(r1) / K, r1.elapsed_time(r2) / K
     # e2e: the learner's view - the packed rollout slice from pinned host memory, the stem, a per-channel mean back
     host6 = obs6.cpu().pin_memory()
     hoste = emph.cpu().pin_memory()
@@ -321,6 +352,9 @@ def stem_arm(args):
                 roofline=dict(bound='hbm', achieved=round(achieved, 1), peak=peak, unit='GB/s', frac=round(achieved / peak, 4),
                               traffic=None, kernel='k_stem_fwd<packed>', bytes_per_call=in_bytes + out_bytes,
                               peak_source=f'{kind} (MEASURED_PEAKS.json hbm_gbs)' if kind == 'measured' else 'fallback'),
+                env_pictures=dict(note='the same calls on pictures the env drew (synth00, 64 decisions in)',
+                                  fwd_ms=round(env_fwd_ms, 4), bwd_ms=round(env_bwd_ms, 4),
+                                  fwd_frac=round((in_bytes + out_bytes) / (env_fwd_ms / 1e3) / 1e9 / peak, 4)),
                 backward=dict(ms=round(bwd_ms, 4), samples_per_s=round(B / (bwd_ms / 1e3), 1),
                               achieved_gbs=round(bwd_bytes / (bwd_ms / 1e3) / 1e9, 1),
                               frac=round(bwd_bytes / (bwd_ms / 1e3) / 1e9 / peak, 4), bytes_per_call=bwd_bytes,
