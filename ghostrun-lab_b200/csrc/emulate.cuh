@@ -136,6 +136,21 @@ __device__ __forceinline__ u32 v_inc_y(u32 v) {
     }
     return v & 0x7FFFu;
 }
+// v after k line ends without events (k <= 240): the vertical increment k times (coarse Y 29 -> 0 toggles the
+// vertical nametable, 31 -> 0 does not), the horizontal bits from t (th) once k >= 1; rendering off: v stays.
+__device__ __forceinline__ u32 v_after_lines(u32 v, u32 k, u32 th, bool ren) {
+    if (k == 0 || !ren) return v;
+    u32 y = ((v >> 5) & 31u) * 8u + ((v >> 12) & 7u);
+    u32 nty = v & 0x800u;
+    y += k;
+    if (y - k < 240u) {
+        if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
+    } else if (y >= 256u) {
+        y -= 256u;
+        if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
+    }
+    return th | nty | ((y & 7u) << 12) | ((y >> 3) << 5);
+}
 
 // ------------------------------------------------------------------------------------------------ emulator
 
@@ -427,10 +442,8 @@ struct Emu {
         const u32 shown = log_ctl & kLcBank;
         u32* h = writing_bank();
         const u32* old = log_bank(shown);
-        if (true) {
-            h[0] = (h[0] & kLogOverflow) | log_n;
-            h[15] = (h[15] & ~7u) | emphasis(h, old[15] & 7u);
-        }
+        h[0] = (h[0] & kLogOverflow) | log_n;
+        h[15] = (h[15] & ~7u) | emphasis(h, old[15] & 7u);
         const u32 nb = (shown + 1u) & kLcBank;
         log_ctl = (log_ctl & ~kLcBank) | nb;
         const u64 sl = static_cast<u64>(e) * 4 + slot;
@@ -1185,7 +1198,7 @@ struct S0State {
     u32 sh0, sh1, at;          // tile shift registers after the last drawn tiles
     u32 lazy, lz_v, lz_ctrl;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
     u32 lz_chr[8], lz_mirroring;
-    u32 fetched_n, blurp, f_lo0, f_hi0, f_attr0, f_x0;
+    u32 blurp, f_lo0, f_hi0, f_attr0, f_x0;
     u32 sphitx, sphitdata, hit, hit_x;
 };
 
@@ -1343,28 +1356,26 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
     s.sh0 = s.sh1 = s.at = 0;
     s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mirroring = 0;
     for (int i = 0; i < 8; ++i) s.lz_chr[i] = 0;
-    s.fetched_n = 0; s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
+    s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
     s.sphitx = 0x100u; s.sphitdata = 0; s.hit = 0; s.hit_x = 0;
     while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply(s, ev, s.cursor++, false);
     if (s.mask & 0x18u) s.v = s.t;
     const int last = first + 15 < 239 ? first + 15 : 239;
     int l = 0;
-    // lines above sprite 0 with no write anywhere in them: only the PPU address moves
+    // lines above sprite 0 with no write anywhere in them: only the PPU address moves, in closed form (the lines
+    // 0..k-1 whose ends come at or before the next event; events before -16 are applied, so next + 16 >= 0)
     {
-        const int next_ev = s.cursor < c.count ? fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) : 0x7FFFFFFF;
-        if (s.mask & 0x18u) {
-            while (l < first - 1 && (l + 1) * 341 - 16 <= next_ev) {
-                s.lazy = 1; s.lz_v = s.v; s.lz_ctrl = s.ctrl;
-                s.v = (v_inc_y(v_inc_x_n(s.v, 34)) & 0xFBE0u) | (s.t & 0x041Fu);
-                ++l;
-            }
-            if (s.lazy) {
-                s.lz_mirroring = s.mirroring;
-                for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
-            }
-        } else {
-            while (l < first - 1 && (l + 1) * 341 - 16 <= next_ev) ++l;
+        const int k = s.cursor < c.count
+                          ? min(first - 1, max(0, fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) + 16) / 341)
+                          : first - 1;
+        if (k > 0 && (s.mask & 0x18u)) {
+            const u32 th = s.t & 0x041Fu;
+            s.lazy = 1; s.lz_ctrl = s.ctrl; s.lz_mirroring = s.mirroring;
+            for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
+            s.lz_v = v_after_lines(s.v, static_cast<u32>(k - 1), th, true);
+            s.v = v_after_lines(s.v, static_cast<u32>(k), th, true);
         }
+        l = k;
     }
     for (; l <= last; ++l) {
         const int start = l * 341 - 16;
@@ -1408,6 +1419,7 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
             const u32 hgt = (s.ctrl & 0x20u) ? 16u : 8u;
             const u32 vofs = ((s.ctrl & 0x08u) && !(s.ctrl & 0x20u)) ? 0x1000u : 0u;
             const u32 tt = static_cast<u32>(l - static_cast<int>(oy));
+            // blurp: sprite 0 is in range of line l + 1 (the count of other fetched sprites never changes the check)
             s.blurp = 0;
             if (tt < hgt) {
                 s.blurp = 1;
@@ -1418,17 +1430,12 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
                 s.f_lo0 = s0_chr<BOARD>(c, s.chr, vadr);
                 s.f_hi0 = s0_chr<BOARD>(c, s.chr, vadr + 8u);
                 s.f_attr0 = oattr; s.f_x0 = ox;
-                s.fetched_n = 1;
-            } else {
-                u32 any = 0;
-                for (u32 n = 1; n < 64 && !any; ++n) any = static_cast<u32>(l - static_cast<int>(oamb(4 * n))) < hgt;
-                s.fetched_n = any;
             }
         }
         while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply(s, ev, s.cursor++, true);
         if (s.mask & 0x18u) s.v = (s.v & 0xFBE0u) | (s.t & 0x041Fu);
         while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply(s, ev, s.cursor++, true);
-        if ((s.mask & 0x10u) && s.fetched_n && s.blurp && !s.hit) {
+        if ((s.mask & 0x10u) && s.blurp && !s.hit) {
             const u32 j = s.f_lo0 | s.f_hi0;
             if (j) { s.sphitx = s.f_x0; s.sphitdata = (s.f_attr0 & 0x40u) ? (__brev(j) >> 24) : j; }
         }

@@ -111,11 +111,8 @@ struct Sig {
 
 // The synthetic template's RAM -> Signals ($10-$11 progress, $12 level, $13 lives, $14-$16 BCD score, $17 mode).
 static __device__ Sig observe_synth(const StateView& S, u32 e) {
-    const u8* r8 = reinterpret_cast<const u8*>(S.ram);
-    auto rb = [&](u32 a) -> u32 { return r8[((static_cast<u64>(a >> 2) * S.Np + e) << 2) | (a & 3u)]; };
     const u32 w10 = S.ram[static_cast<u64>(0x10 >> 2) * S.Np + e];   // $10-$13
     const u32 w14 = S.ram[static_cast<u64>(0x14 >> 2) * S.Np + e];   // $14-$17
-    (void)rb;
     Sig s;
     const u32 mode = w14 >> 24;
     s.in_play = mode == 1;

@@ -559,21 +559,6 @@ struct Renderer {
         if (!(fetch_mask & 0x18u) && (w.mask & 0x10u)) w.seq = 1;
         F.rec[l] = make_uint2(rx, ry | ((w.mask & 0x10u) ? (1u << 16) : 0u) | (w.pv << 20));
     }
-    // v after k line ends without events (k <= 240): the vertical increment k times (coarse Y 29 -> 0 toggles the
-    // vertical nametable, 31 -> 0 does not), the horizontal bits from t (th) once k >= 1; rendering off: v stays.
-    __device__ __forceinline__ static u32 v_after_lines(u32 v, u32 k, u32 th, bool ren) {
-        if (k == 0 || !ren) return v;
-        u32 y = ((v >> 5) & 31u) * 8u + ((v >> 12) & 7u);
-        u32 nty = v & 0x800u;
-        y += k;
-        if (y - k < 240u) {
-            if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
-        } else if (y >= 256u) {
-            y -= 256u;
-            if (y >= 240u) { y -= 240u; nty ^= 0x800u; }
-        }
-        return th | nty | ((y & 7u) << 12) | ((y >> 3) << 5);
-    }
     // The frame's nametable into shared memory, its OAM into registers (2 entries per lane), its CHR-RAM (all lanes).
     __device__ void load_frame(u32 ge, u32 f) {
         const u64 sl = static_cast<u64>(ge) * 4 + f;
