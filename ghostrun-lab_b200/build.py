@@ -17,7 +17,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 OUT = HERE / 'librlenv_b200.so'
 BUILD = HERE / '_build'
-UNITS = ['rlenv_b200.cu', 'board_nrom.cu', 'board_uxrom.cu', 'board_mmc1.cu', 'board_mmc3.cu', 'board_cnrom.cu', 'stem.cu']
+UNITS = ['rlenv_b200.cu', 'board_nrom.cu', 'board_uxrom.cu', 'board_mmc1.cu', 'board_mmc3.cu', 'board_cnrom.cu', 'board_mmc2.cu', 'stem.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc' if Path('/usr/local/cuda/bin/nvcc').exists() else 'nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-O3', '-std=c++17', '-lineinfo', '-fmad=false',
          '--expt-relaxed-constexpr', '-Xcompiler', '-fPIC', '-Xcompiler', '-ffp-contract=off']

@@ -1,0 +1,6 @@
+// MMC2 specialisation of the emulator, renderer and launch sequence (compiled as its own unit).
+#include "host.cuh"
+
+namespace gr {
+GR_BOARD_TEMPLATES(, kMmc2)
+}  // namespace gr

@@ -373,6 +373,10 @@ struct Emu {
             for (u32 i = 0; i < 4; ++i) c0 |= ((rw(R_CHRPG + i) >> 10) & 0xFFu) << (i * 8);
             for (u32 i = 0; i < 4; ++i) c1 |= ((rw(R_CHRPG + 4 + i) >> 10) & 0xFFu) << (i * 8);
             w0.w = c0; w1.x = c1; w1.y = mirroring();
+            if constexpr (BOARD == kMmc2) {   // latches in h[5], the four CHR registers in h[6] (patch:1034-1040)
+                w1.y |= ((mreg(6) & 1u) << 8) | ((mreg(7) & 1u) << 16);
+                w1.z = rw(R_MREG);
+            }
         }
         const uint4* pp = reinterpret_cast<const uint4*>(pal());
         const uint4 pa = pp[0], pb = pp[1];
@@ -504,6 +508,7 @@ struct Emu {
     }
 
     __device__ __forceinline__ Hit0 sprite0_eval() const;
+    __device__ __forceinline__ void mmc2_resolve();
 
     // -------- PPU settle (patch:2114-2240)
     __device__ __forceinline__ u32 dots_to_event() const {
@@ -569,6 +574,7 @@ struct Emu {
             if (crossed(kVblankFlagDot)) status |= 0x80u;
             if (crossed(kVblankDot)) {
                 if (ctrl & 0x80u) nmi = 1;
+                if constexpr (BOARD == kMmc2) mmc2_resolve();
                 log_freeze();
             }
             if (crossed(kStatusClearDot)) status &= 0x1Fu;
@@ -618,12 +624,14 @@ struct Emu {
                         rb = ppu_mem_rd(pa - 0x1000u);
                     } else {
                         value = rb;
+                        ppu_address(pa);   // the buffer refills through the bank the address picks
                         rb = ppu_mem_rd(pa);
                     }
                     set_field(R_PPU2, 0, 0xFF, rb);
                     const u32 nv = (v16 + ((ctrl & 4u) ? 32u : 1u)) & 0x7FFFu;
                     ww(R_VT, (vt & 0xFFFF0000u) | nv);
                     log_event(kEvDataRead, 0, 0);
+                    ppu_address(nv & 0x3FFFu);
                     set_field(R_PPU1, 24, 0xFF, value);
                     return value;
                 }
@@ -692,6 +700,35 @@ struct Emu {
         for (u32 s = 0; s < 8; ++s) ww(R_CHRPG + s, ((mreg(0) * 8u + s) & C.chr_page_mask) << 10);
     }
 
+    // MMC2 (patch:3027-3035 paged::sync): the switchable 8 KB page at $8000 and the last three; each 4 KB CHR half
+    // from the register its latch picks ($FD: 0 / 2, $FE: 1 / 3); register 5 set = vertical mirroring.
+    __device__ __forceinline__ void mmc2_chr4(u32 half) {
+        const u32 b = mreg(2u * half + (mreg(6u + half) & 1u));
+        for (u32 i = 0; i < 4; ++i) ww(R_CHRPG + 4 * half + i, ((4 * b + i) & C.chr_page_mask) << 10);
+    }
+    __device__ __forceinline__ void mmc2_sync() {
+        auto prg8 = [&](u32 s, u32 b) { ww(R_PRGPG + s, (b & C.prg_page_mask) << 13); };
+        prg8(0, mreg(4)); prg8(1, ~2u); prg8(2, ~1u); prg8(3, ~0u);
+        mmc2_chr4(0);
+        mmc2_chr4(1);
+        if (C.arrangement != 2) set_field(R_PPU2, 24, 0xFF, mreg(5) ? kPageVertical : kPageHorizontal);
+    }
+    // The VRAM address the CPU puts on the PPU bus ($2006 / $2007): MMC2's latch hook ($0FD0-$0FEF / $1FD0-$1FEF,
+    // patch:3195-3222), the change logged while a frame is drawn (patch:615-636 bus_ppu_address).
+    __device__ __forceinline__ void ppu_address(u32 addr) {
+        if constexpr (BOARD == kMmc2) {
+            const u32 high = (addr >> 8) & 0x3Fu, low = addr & 0xF0u;
+            if (high >= 0x20u || (high & 0x0Fu) != 0x0Fu || (low != 0xD0u && low != 0xE0u)) return;
+            const u32 half = high >> 4, latch = low == 0xE0u ? 1u : 0u;
+            const u32 before = mreg(6u + half);
+            set_mreg(6u + half, latch);
+            mmc2_chr4(half);
+            if (before != latch) log_event(kEvMmc2, latch, 6u + half);
+        } else {
+            (void)addr;
+        }
+    }
+
     __device__ __forceinline__ void board_write(u32 addr, u32 v) {
         if constexpr (BOARD == kCnrom) {
             (void)addr;   // the bank latch (no bus conflicts: an iNES 1.0 image declares none)
@@ -718,6 +755,17 @@ struct Emu {
                 default: set_mreg(13, 1); return;
             }
             mmc3_sync();
+        } else if constexpr (BOARD == kMmc2) {   // patch:3147-3156
+            switch (addr & 0xF000u) {
+                case 0xA000u: set_mreg(4, v & 0x0Fu); break;
+                case 0xB000u: set_mreg(0, v & 0x1Fu); break;
+                case 0xC000u: set_mreg(1, v & 0x1Fu); break;
+                case 0xD000u: set_mreg(2, v & 0x1Fu); break;
+                case 0xE000u: set_mreg(3, v & 0x1Fu); break;
+                case 0xF000u: set_mreg(5, (v & 1u) ^ 1u); break;
+                default: return;   // $8000-$9FFF: no register
+            }
+            mmc2_sync();
         }
     }
 
@@ -729,12 +777,18 @@ struct Emu {
                 u32 before[8];
                 for (int i = 0; i < 8; ++i) before[i] = rw(R_CHRPG + i);
                 const u32 mir = mirroring();
+                const u32 creg = rw(R_MREG);   // registers 0-3 (MMC2's CHR registers)
                 board_write(addr, v);
                 for (u32 i = 0; i < 8; ++i) {
                     const u32 pg = rw(R_CHRPG + i);
                     if (pg != before[i]) log_event(kEvChr, pg >> 10, i);
                 }
                 if (mirroring() != mir) log_event(kEvMirror, mirroring(), 0);
+                if constexpr (BOARD == kMmc2) {   // the CHR registers the write changed (patch:661-665)
+                    const u32 now_c = rw(R_MREG);
+                    for (u32 i = 0; i < 4; ++i)
+                        if (((now_c ^ creg) >> (8 * i)) & 0xFFu) log_event(kEvMmc2, (now_c >> (8 * i)) & 0xFFu, i);
+                }
             } else {
                 board_write(addr, v);
             }
@@ -788,6 +842,7 @@ struct Emu {
                         ww(R_PPU1, p1 & 0xFF00FFFFu);
                     }
                     ww(R_VT, vv | (t << 16));
+                    if (w != 0) ppu_address(vv);
                     break;
                 }
                 case 7: {
@@ -799,6 +854,7 @@ struct Emu {
                     else log_event(kEvDataWrite, 0, 0);
                     const u32 nv = (v16 + ((ctrl & 4u) ? 32u : 1u)) & 0x7FFFu;
                     ww(R_VT, (vt & 0xFFFF0000u) | nv);
+                    ppu_address(nv & 0x3FFFu);
                     break;
                 }
                 default: break;
@@ -1200,6 +1256,8 @@ struct S0State {
     u32 lz_chr[8], lz_mirroring;
     u32 blurp, f_lo0, f_hi0, f_attr0, f_x0;
     u32 sphitx, sphitdata, hit, hit_x;
+    u32 latch[2], creg[4];     // MMC2: the latches and CHR registers of the replay
+    u32 lz_chr33[8];           // MMC2: the pages fetch 33 of the lazy line went through (a fetch-32 flip moves them)
 };
 
 template <u32 BOARD>
@@ -1229,6 +1287,30 @@ __device__ __forceinline__ u32 s0_fetch(const S0Ctx& c, u32 ctrl, const u32* chr
     return s0_chr<BOARD>(c, chr_pages, vadr) | (s0_chr<BOARD>(c, chr_pages, vadr + 8u) << 8) | (cc << 16);
 }
 
+// MMC2 in the replay (patch:1385-1402): a half's four 1 KB pages from the register its latch picks; the hook on a
+// fetched pattern address in $0FD0-$0FEF / $1FD0-$1FEF puts that half on its $FD or $FE bank.
+// The low-plane pattern address of the tile fetch at PPU address v.
+template <u32 BOARD>
+__device__ __forceinline__ u32 s0_tile_addr(const S0Ctx& c, u32 ctrl, u32 mirroring, u32 v) {
+    u32 tile;
+    if constexpr (board_paged(BOARD)) tile = c.nt[nt_off_map(mirroring, 0x2000u | (v & 0x0FFFu))];
+    else tile = c.nt[nt_off_header(c.arrangement, 0x2000u | (v & 0x0FFFu))];
+    return (tile << 4) + (((ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
+}
+
+__device__ __forceinline__ void s0_mmc2_select(S0State& s, u32 half) {
+    const u32 bank = s.creg[2 * half + s.latch[half]];
+    for (u32 i = 0; i < 4; ++i) s.chr[4 * half + i] = (bank * 4 + i) & 0xFFu;
+}
+__device__ __forceinline__ void s0_mmc2_hook(S0State& s, u32 addr) {
+    const u32 high = (addr >> 8) & 0xFFu, low = addr & 0xF0u;
+    if (high >= 0x20u || (high & 0x0Fu) != 0x0Fu || (low != 0xD0u && low != 0xE0u)) return;
+    const u32 half = high >> 4;
+    s.latch[half] = low == 0xE0u ? 1u : 0u;
+    s0_mmc2_select(s, half);
+}
+
+template <u32 BOARD>
 __device__ __forceinline__ void s0_apply(S0State& s, const u32* ev, u32 i, bool drawing) {
     const u32 w1 = ev[2 * i + 1];
     const u32 value = w1 & 0xFFu, aux = (w1 >> 8) & 0xFFu;
@@ -1252,6 +1334,12 @@ __device__ __forceinline__ void s0_apply(S0State& s, const u32* ev, u32 i, bool 
         case kEvPalette: s.v = (s.v + inc) & 0x7FFFu; break;
         case kEvChr: s.chr[aux & 7u] = value; break;
         case kEvMirror: s.mirroring = value; break;
+        case kEvMmc2:
+            if constexpr (BOARD == kMmc2) {
+                if (aux < 4u) { s.creg[aux] = value; s0_mmc2_select(s, aux >> 1); }
+                else if (aux == 6u || aux == 7u) { s.latch[aux - 6u] = value & 1u; s0_mmc2_select(s, aux - 6u); }
+            }
+            break;
         default: break;
     }
 }
@@ -1260,7 +1348,8 @@ template <u32 BOARD>
 __device__ void s0_materialize(const S0Ctx& c, S0State& s) {
     if (!s.lazy) return;
     const u32 f32 = s0_fetch<BOARD>(c, s.lz_ctrl, s.lz_chr, s.lz_mirroring, v_inc_x_n(s.lz_v, 32));
-    const u32 f33 = s0_fetch<BOARD>(c, s.lz_ctrl, s.lz_chr, s.lz_mirroring, v_inc_x_n(s.lz_v, 33));
+    const u32 f33 = s0_fetch<BOARD>(c, s.lz_ctrl, BOARD == kMmc2 ? s.lz_chr33 : s.lz_chr, s.lz_mirroring,
+                                    v_inc_x_n(s.lz_v, 33));
     s.sh0 = ((f32 & 0xFFu) << 8) | (f33 & 0xFFu);
     s.sh1 = (((f32 >> 8) & 0xFFu) << 8) | ((f33 >> 8) & 0xFFu);
     s.at = ((f32 >> 16) & 3u) | (((f33 >> 16) & 3u) << 2);
@@ -1294,7 +1383,8 @@ __device__ void s0_event_line(const S0Ctx& c, S0State& s, int kook, int l, bool 
                 }
                 outpos += 8;
             }
-            const u32 f = s0_fetch<BOARD>(c, s.ctrl, s.chr, s.mirroring, s.v);
+            const u32 f = s0_fetch<BOARD>(c, s.ctrl, s.chr, s.mirroring, s.v);   // both bytes before the hook
+            if constexpr (BOARD == kMmc2) s0_mmc2_hook(s, s0_tile_addr<BOARD>(c, s.ctrl, s.mirroring, s.v));
             s.at = ((s.at >> 2) | (((f >> 16) & 3u) << 2)) & 0xFu;
             s.sh0 = ((s.sh0 << 8) | (f & 0xFFu)) & 0xFFFFu;
             s.sh1 = ((s.sh1 << 8) | ((f >> 8) & 0xFFu)) & 0xFFFFu;
@@ -1331,11 +1421,25 @@ __device__ void s0_event_line(const S0Ctx& c, S0State& s, int kook, int l, bool 
         const u32 kind = ev[2 * s.cursor] >> 24;
         if (kind != kEvDataWrite && kind != kEvPalette)
             update(fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) + 3 * static_cast<int>((ev[2 * s.cursor] >> 17) & 0xFu) - start);
-        s0_apply(s, ev, s.cursor++, true);
+        s0_apply<BOARD>(s, ev, s.cursor++, true);
     }
     update(272);
     if (tofix) { if (s.mask & 0x18u) s.v = v_inc_y(s.v); tofix = false; }
     if (pixels) check(272);
+}
+
+// The hit found at pixel x of line l (sphitx: where the check started): the frame dot from which an instruction sees
+// the flag, FCEUmm's RefreshLine drawing one tile more while the check is pending (patch:1758-1770).
+__device__ __forceinline__ Hit0 s0_hit_at(int l, u32 x, u32 sphitx) {
+    const int hx = static_cast<int>(x), spx = static_cast<int>(sphitx);
+    int pp = hx + 17;
+    for (;; ++pp) {
+        int lastt = pp >> 3;
+        if (spx < pp - 16 && !(spx < (lastt - 2) * 8)) ++lastt;
+        if (lastt > 34) lastt = 34;
+        if (hx < (lastt - 2) * 8) break;
+    }
+    return Hit0{nesle_dot(l * 341 - 16 + pp - 12), true};
 }
 
 template <u32 BOARD>
@@ -1358,7 +1462,7 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
     for (int i = 0; i < 8; ++i) s.lz_chr[i] = 0;
     s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
     s.sphitx = 0x100u; s.sphitdata = 0; s.hit = 0; s.hit_x = 0;
-    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply(s, ev, s.cursor++, false);
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply<BOARD>(s, ev, s.cursor++, false);
     if (s.mask & 0x18u) s.v = s.t;
     const int last = first + 15 < 239 ? first + 15 : 239;
     int l = 0;
@@ -1402,17 +1506,7 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
             for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
             s.v = v_inc_y(v_inc_x_n(v0, 34));
         }
-        if (s.hit) {
-            const int hx = static_cast<int>(s.hit_x), spx = static_cast<int>(sphitx0);
-            int pp = hx + 17;
-            for (;; ++pp) {
-                int lastt = pp >> 3;
-                if (spx < pp - 16 && !(spx < (lastt - 2) * 8)) ++lastt;
-                if (lastt > 34) lastt = 34;
-                if (hx < (lastt - 2) * 8) break;
-            }
-            return Hit0{nesle_dot(l * 341 - 16 + pp - 12), true};
-        }
+        if (s.hit) return s0_hit_at(l, s.hit_x, sphitx0);
         // end of line: sprite fetch for line l + 1 (only sprite 0 matters), Fixit2, RefreshSprites
         s.sphitx = 0x100u;
         if ((s.mask & 0x18u) && l >= first - 1) {
@@ -1432,15 +1526,177 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
                 s.f_attr0 = oattr; s.f_x0 = ox;
             }
         }
-        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply(s, ev, s.cursor++, true);
+        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply<BOARD>(s, ev, s.cursor++, true);
         if (s.mask & 0x18u) s.v = (s.v & 0xFBE0u) | (s.t & 0x041Fu);
-        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply(s, ev, s.cursor++, true);
+        while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply<BOARD>(s, ev, s.cursor++, true);
         if ((s.mask & 0x10u) && s.blurp && !s.hit) {
             const u32 j = s.f_lo0 | s.f_hi0;
             if (j) { s.sphitx = s.f_x0; s.sphitdata = (s.f_attr0 & 0x40u) ? (__brev(j) >> 24) : j; }
         }
     }
     return Hit0{nesle_dot(last * 341 + 256), false};
+}
+
+// ------------------------------------------------------------------------------------------------ MMC2 latches
+// MMC2's latches move with every pattern fetch the frame makes, so its sprite-0 replay and the vblank resolve
+// (patch:1791-1815 frame_resolve_mmc2) follow the frame's fetch order. An event-free line's 34 background fetches all
+// use one pattern table, so they can only move that half's latch, and only by a $FD or $FE tile number: their effect
+// is the last such tile among fetches 0-31, 32 and 33, worked out once per run of lines with the same first fetch
+// address, table and page map (the nametable does not change during the replay).
+
+struct Mmc2Row { u32 key, o31, o32, o33; };   // flips: 0 none, 1 $FD, 2 $FE
+
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_row(const S0Ctx& c, const S0State& s, Mmc2Row& r) {
+    const u32 key = 0x80000000u | (s.v & 0x0FFFu) | ((s.ctrl & 0x10u) << 8) | ((s.mirroring & 0xFFu) << 13);
+    if (key == r.key) return;
+    r.key = key;
+    r.o31 = r.o32 = r.o33 = 0;
+    for (u32 k = 0; k < 34; ++k) {
+        const u32 vv = v_inc_x_n(s.v, k);
+        const u32 tile = c.nt[nt_off_map(s.mirroring, 0x2000u | (vv & 0x0FFFu))];
+        const u32 f = (tile == 0xFDu || tile == 0xFEu) ? tile - 0xFCu : 0u;
+        if (f) { if (k < 32) r.o31 = f; else if (k == 32) r.o32 = f; else r.o33 = f; }
+    }
+}
+
+// An event-free line drawn with rendering on: its latch moves and the lazy shift-register record (fetch 32 through
+// the pages before fetch 32's own flip, fetch 33 through those before its own), then the address steps.
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_plain_line(const S0Ctx& c, S0State& s, Mmc2Row& row, bool keep_lazy) {
+    mmc2_row<BOARD>(c, s, row);
+    const u32 bg = (s.ctrl >> 4) & 1u;
+    const u32 l32 = row.o31 ? row.o31 - 1u : s.latch[bg];
+    const u32 l33 = row.o32 ? row.o32 - 1u : l32;
+    if (keep_lazy) {
+        s.lazy = 1; s.lz_v = s.v; s.lz_ctrl = s.ctrl; s.lz_mirroring = s.mirroring;
+        s.latch[bg] = l32; s0_mmc2_select(s, bg);
+        for (int i = 0; i < 8; ++i) s.lz_chr[i] = s.chr[i];
+        s.latch[bg] = l33; s0_mmc2_select(s, bg);
+        for (int i = 0; i < 8; ++i) s.lz_chr33[i] = s.chr[i];
+    }
+    s.latch[bg] = row.o33 ? row.o33 - 1u : l33;
+    s0_mmc2_select(s, bg);
+    s.v = v_inc_y(v_inc_x_n(s.v, 34));
+}
+
+// FetchSpriteData at the end of line l with rendering on: every sprite in range (at most 8, OAM order) goes through
+// the latch hook; sprite 0's pattern bytes are kept for the hit check. `vis`: the OAM entries with y < 240.
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_sprites(const S0Ctx& c, S0State& s, int l, u64 vis) {
+    auto oamb = [&](u32 i) -> u32 { return reinterpret_cast<const u8*>(c.soam + (i >> 2) * kEnvsPerWarp)[i & 3u]; };
+    const u32 hgt = (s.ctrl & 0x20u) ? 16u : 8u;
+    const u32 vofs = ((s.ctrl & 0x08u) && !(s.ctrl & 0x20u)) ? 0x1000u : 0u;
+    u32 n = 0;
+    s.blurp = 0;
+    for (u64 m = vis; m; m &= m - 1) {
+        const u32 i = static_cast<u32>(__ffsll(static_cast<long long>(m)) - 1);
+        const u32 t = static_cast<u32>(l - static_cast<int>(oamb(4 * i)));
+        if (t >= hgt) continue;
+        if (n >= 8) break;
+        ++n;
+        const u32 tile = oamb(4 * i + 1), attr = oamb(4 * i + 2);
+        u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+        if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (s.ctrl & 0x20u) >> 1; vadr -= t & 8u; }
+        else { vadr += t; vadr += t & 8u; }
+        vadr &= 0x1FFFu;
+        if (i == 0) {   // both bytes through the bank before the hook
+            s.blurp = 1;
+            s.f_lo0 = s0_chr<BOARD>(c, s.chr, vadr);
+            s.f_hi0 = s0_chr<BOARD>(c, s.chr, vadr + 8u);
+            s.f_attr0 = attr;
+            s.f_x0 = oamb(3);
+        }
+        s0_mmc2_hook(s, vadr);
+    }
+}
+
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_begin(const S0Ctx& c, S0State& s, int kook, u64& vis) {
+    const u32* h = c.bank;
+    s.ctrl = h[1] & 0xFFu; s.mask = (h[1] >> 8) & 0xFFu; s.x = (h[1] >> 16) & 7u;
+    s.v = h[2] & 0x7FFFu; s.t = (h[2] >> 16) & 0x7FFFu;
+    for (int i = 0; i < 8; ++i) s.chr[i] = (h[3 + (i >> 2)] >> ((i & 3) * 8)) & 0xFFu;
+    s.mirroring = h[5] & 0xFFu;
+    s.latch[0] = (h[5] >> 8) & 1u; s.latch[1] = (h[5] >> 16) & 1u;
+    for (int i = 0; i < 4; ++i) s.creg[i] = (h[6] >> (8 * i)) & 0xFFu;
+    s.cursor = 0;
+    s.sh0 = s.sh1 = s.at = 0;
+    s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mirroring = 0;
+    for (int i = 0; i < 8; ++i) { s.lz_chr[i] = 0; s.lz_chr33[i] = 0; }
+    s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
+    s.sphitx = 0x100u; s.sphitdata = 0; s.hit = 0; s.hit_x = 0;
+    const u32* ev = h + kLogHdr;
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply<BOARD>(s, ev, s.cursor++, false);
+    if (s.mask & 0x18u) s.v = s.t;
+    vis = 0;
+    for (u32 i = 0; i < 64; ++i)
+        if (reinterpret_cast<const u8*>(c.soam + i * kEnvsPerWarp)[0] < 240u) vis |= 1ull << i;
+}
+
+// End of line l after its pixels: sprite fetch (rendering on), Fixit2, RefreshSprites' sprite-0 data.
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_end_of_line(const S0Ctx& c, S0State& s, int kook, int l, u64 vis) {
+    const u32* ev = c.bank + kLogHdr;
+    const int start = l * 341 - 16;
+    s.sphitx = 0x100u;
+    if (s.mask & 0x18u) mmc2_sprites<BOARD>(c, s, l, vis);
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 278) s0_apply<BOARD>(s, ev, s.cursor++, true);
+    if (s.mask & 0x18u) s.v = (s.v & 0xFBE0u) | (s.t & 0x041Fu);
+    while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 341) s0_apply<BOARD>(s, ev, s.cursor++, true);
+    if ((s.mask & 0x10u) && s.blurp && !s.hit) {
+        const u32 j = s.f_lo0 | s.f_hi0;
+        if (j) { s.sphitx = s.f_x0; s.sphitdata = (s.f_attr0 & 0x40u) ? (__brev(j) >> 24) : j; }
+    }
+}
+
+// MMC2's sprite-0 hit (patch:1740-1789 with the MMC2 fetch rules): lines above sprite 0 move only the latches and
+// the address; from the line before sprite 0 on, every line is replayed tile by tile.
+template <u32 BOARD>
+__device__ __noinline__ Hit0 sprite0_hit_mmc2(const S0Ctx c) {
+    const int kook = (c.bank[15] & kLogKook) ? 1 : 0;
+    const int first = static_cast<int>(reinterpret_cast<const u8*>(c.soam)[0]) + 1;
+    if (first >= 240) return Hit0{0, false};
+    const u32* ev = c.bank + kLogHdr;
+    S0State s;
+    u64 vis;
+    mmc2_begin<BOARD>(c, s, kook, vis);
+    Mmc2Row row;
+    row.key = 0;
+    const int last = first + 15 < 239 ? first + 15 : 239;
+    for (int l = 0; l <= last; ++l) {
+        const int start = l * 341 - 16;
+        const u32 sphitx0 = s.sphitx;
+        const bool event_line = s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272;
+        if (event_line || l >= first - 1) s0_event_line<BOARD>(c, s, kook, l, l >= first);
+        else if (s.mask & 0x18u) mmc2_plain_line<BOARD>(c, s, row, true);
+        if (s.hit) return s0_hit_at(l, s.hit_x, sphitx0);
+        mmc2_end_of_line<BOARD>(c, s, kook, l, vis);
+    }
+    return Hit0{nesle_dot(last * 341 + 256), false};
+}
+
+// The latches the frame's fetches leave (latch 0 | latch 1 << 1), replayed over the whole picture and the events
+// after it (patch:1791-1815; rl/csrc/nes_machine.cuh:107-130 runs the same replay after the vblank stop).
+template <u32 BOARD>
+__device__ __noinline__ u32 mmc2_latches(const S0Ctx c) {
+    const int kook = (c.bank[15] & kLogKook) ? 1 : 0;
+    const u32* ev = c.bank + kLogHdr;
+    S0State s;
+    u64 vis;
+    mmc2_begin<BOARD>(c, s, kook, vis);
+    Mmc2Row row;
+    row.key = 0;
+    for (int l = 0; l < 240; ++l) {
+        const int start = l * 341 - 16;
+        if (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272)
+            s0_event_line<BOARD>(c, s, kook, l, false);
+        else if (s.mask & 0x18u)
+            mmc2_plain_line<BOARD>(c, s, row, false);
+        mmc2_end_of_line<BOARD>(c, s, kook, l, vis);
+    }
+    while (s.cursor < c.count) s0_apply<BOARD>(s, ev, s.cursor++, false);
+    return s.latch[0] | (s.latch[1] << 1);
 }
 
 template <u32 BOARD>
@@ -1455,7 +1711,30 @@ __device__ __forceinline__ Hit0 Emu<BOARD>::sprite0_eval() const {
     c.chr_size = C.chr_size;
     c.chr_page_mask = C.chr_page_mask;
     c.arrangement = C.arrangement;
-    return sprite0_hit<BOARD>(c);
+    if constexpr (BOARD == kMmc2) return sprite0_hit_mmc2<BOARD>(c);
+    else return sprite0_hit<BOARD>(c);
+}
+
+// Vblank on MMC2: the latches this frame's own fetches left go back to the board (patch:1791-1815).
+template <u32 BOARD>
+__device__ __forceinline__ void Emu<BOARD>::mmc2_resolve() {
+    S0Ctx c;
+    c.bank = writing_bank();
+    c.count = log_n < kLogEv ? log_n : kLogEv;
+    c.nt = nt();
+    c.soam = &sh.oam[0][lane];
+    c.chr = C.chr;
+    c.chr_ram = nullptr;
+    c.chr_size = C.chr_size;
+    c.chr_page_mask = C.chr_page_mask;
+    c.arrangement = C.arrangement;
+    const u32 latches = mmc2_latches<BOARD>(c);
+    for (u32 half = 0; half < 2; ++half) {
+        if (mreg(6u + half) != ((latches >> half) & 1u)) {
+            set_mreg(6u + half, (latches >> half) & 1u);
+            mmc2_chr4(half);
+        }
+    }
 }
 
 }  // namespace gr

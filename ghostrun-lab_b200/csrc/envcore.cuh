@@ -898,7 +898,9 @@ __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_co
         u32 ge, f;
         if (!render_item(R, k, ge, f)) continue;
         const u64 sl = static_cast<u64>(ge) * 4 + f;
-        if constexpr (Renderer<BOARD>::kSplitLines) {   // the walk draws the lines with mid-line writes itself
+        if constexpr (BOARD == kMmc2) {   // the latches move with the fetches: the sequential renderer draws it all
+            if (lane == 0) R.seqf[sl] = 1u;
+        } else if constexpr (Renderer<BOARD>::kSplitLines) {   // the walk draws the lines with mid-line writes itself
             u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
             rd.walk_frame(ge, f, RW.fw, out, R.packed != nullptr);
             if (lane == 0) R.seqf[sl] = RW.fw.seq ? 1u : 0u;
@@ -1023,6 +1025,7 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
         m.ww(R_PPU2, board_paged(BOARD) ? (hmap << 24) : 0u);
         if constexpr (BOARD == kCnrom) m.cnrom_sync();
         if constexpr (BOARD == kMmc1) { m.set_mreg(0, 0x0C); m.mmc1_sync(); }
+        if constexpr (BOARD == kMmc2) { m.set_mreg(6, 1); m.set_mreg(7, 1); m.mmc2_sync(); }   // both on $FE
         if constexpr (BOARD == kMmc3) {
             m.set_mreg(1, 2); m.set_mreg(2, 4); m.set_mreg(3, 5); m.set_mreg(4, 6); m.set_mreg(5, 7); m.set_mreg(7, 1);
             m.set_mreg(9, g.cart.arrangement == 1 ? 1 : 0);

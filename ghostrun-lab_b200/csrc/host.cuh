@@ -92,6 +92,13 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.board = kCnrom;
         c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
         c.chr_page_mask = static_cast<u32>(chr_bytes / 1024 - 1);
+    } else if (mapper == 9) {   // MMC2 (patch:4007-4030): 8 KB PRG pages, CHR ROM only, at most 256 KB
+        if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || chr_bytes == 0 || (chr_bytes & (chr_bytes - 1)) ||
+            chr_bytes > 256 * 1024)
+            throw std::runtime_error("unsupported MMC2 image size");
+        c.board = kMmc2;
+        c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
+        c.chr_page_mask = static_cast<u32>(chr_bytes / 1024 - 1);
     } else if (mapper == 1 || mapper == 4) {
         const std::size_t cb = chr_bytes ? chr_bytes : 8192;
         if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || (cb & (cb - 1)))
@@ -100,7 +107,7 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
         c.chr_page_mask = static_cast<u32>(cb / 1024 - 1);
     } else {
-        throw std::runtime_error("unsupported mapper " + std::to_string(mapper) + " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3)");
+        throw std::runtime_error("unsupported mapper " + std::to_string(mapper) + " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3, 9 MMC2)");
     }
     return c;
 }
@@ -400,5 +407,6 @@ GR_BOARD_TEMPLATES(extern, kUxrom)
 GR_BOARD_TEMPLATES(extern, kMmc1)
 GR_BOARD_TEMPLATES(extern, kMmc3)
 GR_BOARD_TEMPLATES(extern, kCnrom)
+GR_BOARD_TEMPLATES(extern, kMmc2)
 
 }  // namespace gr

@@ -41,9 +41,9 @@ constexpr u32 kS0Evaluate = 0x80000000u, kS0Known = 0x40000000u, kS0Hit = 0x2000
 constexpr u64 kDmcIdle = ~0ull;
 
 // ---------------------------------------------------------------- boards
-enum Board : u32 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3, kCnrom = 4 };
+enum Board : u32 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3, kCnrom = 4, kMmc2 = 5 };
 // Boards with per-env page tables (CHR 1 KB pages, PRG 8 KB pages) and a nametable page map.
-__host__ __device__ constexpr bool board_paged(u32 b) { return b == kMmc1 || b == kMmc3 || b == kCnrom; }
+__host__ __device__ constexpr bool board_paged(u32 b) { return b == kMmc1 || b == kMmc3 || b == kCnrom || b == kMmc2; }
 constexpr u8 kPageVertical = 0x0A, kPageHorizontal = 0x0C, kPageSingleLow = 0x00, kPageSingleHigh = 0x0F;
 
 // ---------------------------------------------------------------- observation geometry

@@ -125,6 +125,7 @@ struct RState {
     u32 lazy, lz_v, lz_ctrl, lz_mir;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
     u32 lz_saved;        // W.lzchr holds the lazy line's CHR pages (saved at the first CHR write after that line)
     u32 nf, nd;          // sprites in the fetched / drawn buffer
+    u32 latch[2], creg[4];   // MMC2: the latches and CHR registers of the replay
     u32 cursor;
     int next_t;          // FCEUmm time of event `cursor`, INT_MAX past the last
 };
@@ -289,8 +290,29 @@ struct Renderer {
                 __syncwarp();
                 break;
             case kEvMirror: s.mirroring = value; break;
+            case kEvMmc2:
+                if constexpr (BOARD == kMmc2) {
+                    if (aux < 4u) { s.creg[aux] = value; mmc2_select(aux >> 1); }
+                    else if (aux == 6u || aux == 7u) { s.latch[aux - 6u] = value & 1u; mmc2_select(aux - 6u); }
+                }
+                break;
             default: break;
         }
+    }
+
+    // MMC2 (patch:1385-1402): a half's four 1 KB pages from the register its latch picks; a fetched pattern address
+    // in $0FD0-$0FEF / $1FD0-$1FEF puts that half on its $FD or $FE bank. Warp-uniform arguments.
+    __device__ __forceinline__ void mmc2_select(u32 half) {
+        __syncwarp();
+        if (lane < 4) W.chr[4 * half + lane] = (s.creg[2 * half + s.latch[half]] * 4 + lane) & 0xFFu;
+        __syncwarp();
+    }
+    __device__ __forceinline__ void mmc2_hook(u32 addr) {
+        const u32 high = (addr >> 8) & 0xFFu, low = addr & 0xF0u;
+        if (high >= 0x20u || (high & 0x0Fu) != 0x0Fu || (low != 0xD0u && low != 0xE0u)) return;
+        const u32 half = high >> 4;
+        s.latch[half] = low == 0xE0u ? 1u : 0u;
+        mmc2_select(half);
     }
 
     // The shift registers after the last fast line: its fetches 32 and 33.
@@ -348,7 +370,8 @@ struct Renderer {
                 const u32 ab = nt_rd(s.mirroring, base | 0x3C0u | (zz >> 2) | ((v & 0x380u) >> 4));
                 const u32 attr = (ab >> ((zz & 2u) + ((v & 0x40u) >> 4))) & 3u;
                 const u32 vadr = (tile_i << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7u));
-                const u32 p0 = chr_byte(W.chr, vadr), p1 = chr_byte(W.chr, vadr + 8u);
+                const u32 p0 = chr_byte(W.chr, vadr), p1 = chr_byte(W.chr, vadr + 8u);   // both before the hook
+                if constexpr (BOARD == kMmc2) mmc2_hook(vadr);
                 s.at = ((s.at >> 2) | (attr << 2)) & 0xFu;
                 s.sh0 = ((s.sh0 << 8) | p0) & 0xFFFFu;
                 s.sh1 = ((s.sh1 << 8) | p1) & 0xFFFFu;
@@ -406,7 +429,34 @@ struct Renderer {
             const u32 b0 = __ballot_sync(0xFFFFFFFFu, in0), b1 = __ballot_sync(0xFFFFFFFFu, in1);
             s.blurp = b0 & 1u;
             u32 n = 0;
-            if (b0 | b1) {
+            if constexpr (BOARD == kMmc2) {
+                // in OAM order, each through the pages the previous fetches' hooks left
+                if (b0 | b1) {
+                    __syncwarp();
+                    const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
+                    for (int half = 0; half < 2; ++half) {
+                        for (u32 m = half ? b1 : b0; m && n < 8; m &= m - 1) {
+                            const u32 sp = __shfl_sync(0xFFFFFFFFu, half ? spB : spA, __ffs(m) - 1);
+                            const u32 tile = (sp >> 8) & 0xFFu, attr = (sp >> 16) & 0xFFu, xx = sp >> 24;
+                            const u32 t = static_cast<u32>(l - static_cast<int>(sp & 0xFFu));
+                            u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
+                            if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (c & 0x20u) >> 1; vadr -= t & 8u; }
+                            else { vadr += t; vadr += t & 8u; }
+                            vadr &= 0x1FFFu;
+                            u32 cw = chr_sel(W.chr, vadr);
+                            if (attr & 0x40u) cw = nib_reverse(cw);
+                            if (lane == 0) {
+                                f.cw[n] = cw;
+                                f.meta[n] = (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8);
+                                if (n == 0) f.opq0 = nib_opaque8(cw);
+                            }
+                            mmc2_hook(vadr);
+                            ++n;
+                        }
+                    }
+                    __syncwarp();
+                }
+            } else if (b0 | b1) {
                 __syncwarp();   // the previous line's readers of this buffer are done
                 const u32 vofs = ((c & 0x08u) && !(c & 0x20u)) ? 0x1000u : 0u;
                 const u32 lt = (1u << lane) - 1u;
@@ -1055,6 +1105,8 @@ struct Renderer {
         s.spal[0] = s.spal[1] = s.spal[2] = s.spal[3] = 0;
         s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mir = 0; s.lz_saved = 0;
         s.nf = 0; s.nd = 0;
+        s.latch[0] = (h[5] >> 8) & 1u; s.latch[1] = (h[5] >> 16) & 1u;
+        for (int i = 0; i < 4; ++i) s.creg[i] = (h[6] >> (8 * i)) & 0xFFu;
         s.cursor = 0;
         s.next_t = time_of(0);
         while (s.next_t < -16) next_event(false);
@@ -1063,7 +1115,7 @@ struct Renderer {
         for (int l = 0; l < kObsY0 + kObsH; ++l) {
             const int start = l * 341 - 16;
             u32 w0, w1;   // this lane's 8 background pixels (colour | 0x40 transparent), byte k = pixel 8L+k
-            if (s.next_t < start + 272) {
+            if (BOARD == kMmc2 || s.next_t < start + 272) {   // MMC2: every fetch may move a latch
                 exact_line(l);
                 const uint2 q = reinterpret_cast<const uint2*>(W.px)[lane];
                 w0 = q.x; w1 = q.y;

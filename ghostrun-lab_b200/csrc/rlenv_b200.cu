@@ -36,6 +36,7 @@ void launch_phases(Env& env, const Game& gm, bool start, cudaStream_t s, const S
         case kUxrom: launch_game<kUxrom>(env, gm, start, s, sd, rg, phases); break;
         case kMmc1: launch_game<kMmc1>(env, gm, start, s, sd, rg, phases); break;
         case kCnrom: launch_game<kCnrom>(env, gm, start, s, sd, rg, phases); break;
+        case kMmc2: launch_game<kMmc2>(env, gm, start, s, sd, rg, phases); break;
         default: launch_game<kMmc3>(env, gm, start, s, sd, rg, phases); break;
     }
 }
@@ -246,6 +247,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
                 case kUxrom: boot_game<kUxrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 case kMmc1: boot_game<kMmc1>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 case kCnrom: boot_game<kCnrom>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
+                case kMmc2: boot_game<kMmc2>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
                 default: boot_game<kMmc3>(*env, gm, boot_pads[i], boot_sizes[i], idle_max, boot_slot); break;
             }
             env->games.push_back(gm);

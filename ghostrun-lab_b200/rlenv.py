@@ -10,9 +10,9 @@ Everything stays on the device; nothing is copied to the host per step. The libr
 CPU fallback. `lib_path` selects another library with the same C-ABI (the tests point it at the CPU oracle).
 
 Games: the reference's 12 commercial slugs keep their rl10 ids 0..11 (their ROMs and RAM readers are not part of this
-build), and 13 seeded synthetic games 'synth00'..'synth12' (ids 12..24) run on the synthetic cartridges of synth.py:
-game k < 12 uses board ('nrom', 'uxrom', 'mmc1', 'mmc3')[k % 4], synth12 the CNROM board, each with its own seeded
-reward weights.
+build), and 14 seeded synthetic games 'synth00'..'synth13' (ids 12..25) run on the synthetic cartridges of synth.py:
+game k < 12 uses board ('nrom', 'uxrom', 'mmc1', 'mmc3')[k % 4], synth12 the CNROM board, synth13 the MMC2 board, each
+with its own seeded reward weights.
 """
 from __future__ import annotations
 
@@ -28,7 +28,7 @@ import synth
 PKG = Path(__file__).resolve().parent
 REF_GAMES = ['smb', 'pacman', 'excitebike', 'contra', 'castlevania', 'gradius', 'zelda', 'tetris', 'tecmobowl', 'kage',
              'finalmission', 'punchout']   # rl/games_manifest.json order = rl10 game ids 0..11
-SYNTH_GAMES = [f'synth{k:02d}' for k in range(13)]   # synth12: the CNROM cart
+SYNTH_GAMES = [f'synth{k:02d}' for k in range(14)]   # synth12: the CNROM cart, synth13: the MMC2 cart
 GAMES = REF_GAMES + SYNTH_GAMES
 BOARDS = ('nrom', 'uxrom', 'mmc1', 'mmc3')
 CART_SEED, REWARD_SEED = 1000, 2000
@@ -49,6 +49,8 @@ def synth_cart(slug: str) -> synth.Cart:
     k = SYNTH_GAMES.index(slug)
     if k == 12:
         return synth.make_cart(CART_SEED + 4, 'cnrom')
+    if k == 13:
+        return synth.make_cart(CART_SEED + 5, 'mmc2')
     return synth.make_cart(CART_SEED + k % 4, BOARDS[k % 4])
 
 

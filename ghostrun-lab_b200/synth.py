@@ -16,7 +16,11 @@ tiles and a uniform random nametable. The template is the one the benchmark conf
 Board variants (mapper 2 UxROM, 1 MMC1, 4 MMC3) add the bank traffic the configs name: UxROM switches its 16 KB
 window on every level change, MMC1 rewrites its PRG bank through the serial port every 64 frames and uploads its
 CHR into CHR-RAM at reset, MMC3 arms its scanline IRQ for line 32 each frame and its IRQ handler writes a new scroll
-(a mid-frame split the renderer must replay).
+(a mid-frame split the renderer must replay). CNROM switches its 8 KB CHR bank on every level change. MMC2 (mapper 9)
+draws from both 4 KB halves through its $FD/$FE latches: the random nametable and two sprites carry $FD/$FE tiles
+that flip them mid-line, the NMI puts $0FD8/$0FE8 and $1FD8/$1FE8 on the PPU bus ($2006 + a $2007 read) by frame
+parity, every 16th frame it waits into the picture and rewrites a CHR register and $2006 there (logged mid-frame
+register and latch changes), and every level change switches the $8000 PRG page.
 
 The reward side is a 13th reward10 reader (`SYNTH_READER`): RAM $10-$17 -> Signals, with per-game seeded fp32
 weights promoted to float64 (`reward_spec`).
@@ -152,7 +156,7 @@ class Asm:
 
 # ------------------------------------------------------------------------------------------------- cartridges
 
-MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'cnrom': 3, 'mmc3': 4}
+MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'cnrom': 3, 'mmc3': 4, 'mmc2': 9}
 
 # zero page / RAM map of the template (the synthetic reward reader reads these)
 ZP_BUTTONS, ZP_TMP, ZP_LFSR, ZP_FRAME = 0x00, 0x01, 0x02, 0x04
@@ -195,6 +199,11 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
         i('LDX', 'imm', 32); i('LDY', 'imm', 0)
         a.label('chr'); i('LDA', 'indy', ZP_PTR); i('STA', 'abs', 0x2007); i('INY'); i('BNE', 'rel', 'chr')
         i('INC', 'zp', ZP_PTR + 1); i('DEX'); i('BNE', 'rel', 'chr')
+    if board == 'mmc2':
+        # PRG page 0 at $8000; CHR registers $B000 / $C000 (the $0000 half's $FD / $FE banks), $D000 / $E000 (the
+        # $1000 half's); vertical mirroring
+        for reg, v in zip((0xA000, 0xB000, 0xC000, 0xD000, 0xE000, 0xF000), [0] + list(p['creg']) + [0]):
+            i('LDA', 'imm', v); i('STA', 'abs', reg)
     if board == 'mmc3':
         # PRG mode 0, CHR mode 0; R0..R5 = 0, 2, 4, 5, 6, 7 (the first 8 KB of CHR), vertical mirroring
         for r, v in enumerate([0, 2, 4, 5, 6, 7]):
@@ -236,6 +245,16 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     i('PHA'); i('TXA'); i('PHA'); i('TYA'); i('PHA')
     i('LDA', 'imm', 0); i('STA', 'abs', 0x2003); i('LDA', 'imm', OAM_BUF >> 8); i('STA', 'abs', 0x4014)
     i('BIT', 'abs', 0x2002)
+    if board == 'mmc2':
+        # latch 0 <- $FD / $FE by frame bit 0, latch 1 by frame bit 1: $2006 puts the address on the bus, a $2007 read
+        # puts it there again (and its successor)
+        for half, bit in ((0x0F, 0), (0x1F, 1)):
+            i('LDA', 'imm', half); i('STA', 'abs', 0x2006)
+            i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 1 << bit)
+            for _ in range(4 - bit):
+                i('ASL', 'acc')
+            i('CLC'); i('ADC', 'imm', 0xD8); i('STA', 'abs', 0x2006)
+            i('LDA', 'abs', 0x2007)
     if board == 'mmc3':
         # top of the frame unscrolled; the IRQ at line 32 sets the playfield scroll
         i('LDA', 'imm', 0); i('STA', 'abs', 0x2005); i('STA', 'abs', 0x2005)
@@ -282,6 +301,9 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     if board == 'cnrom':   # CHR bank = level & 3 (written over an equal ROM byte, as a bus-conflict-safe game would)
         i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x03); i('TAX')
         i('LDA', 'absx', 'banktab'); i('STA', 'absx', 'banktab')
+    if board == 'mmc2':
+        i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x0F); i('STA', 'abs', 0xA000)
+        i('LDA', 'abs', 0x8000); i('STA', 'abs', OAM_BUF + 9)
     if board == 'uxrom':
         i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x07); i('TAX')
         i('LDA', 'absx', 'banktab'); i('STA', 'absx', 'banktab')
@@ -311,6 +333,16 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     # player sprite (sprite 1) follows progress
     i('LDA', 'zp', ZP_PROGRESS); i('LSR', 'acc'); i('STA', 'abs', OAM_BUF + 7)
     a.label('nmi_out')
+    if board == 'mmc2':
+        # every 16th frame: wait ~5,100 cycles (into the picture, about line 30), then rewrite the $FE bank of the
+        # $0000 half and put $1FD8 on the bus (the rest of the frame is drawn from that address)
+        i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 0x0F); i('BNE', 'rel', 'nosplit')
+        i('LDY', 'imm', 4)
+        a.label('dly'); i('LDX', 'imm', 255)
+        a.label('dly2'); i('DEX'); i('BNE', 'rel', 'dly2'); i('DEY'); i('BNE', 'rel', 'dly')
+        i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x0F); i('ORA', 'imm', 0x10); i('STA', 'abs', 0xC000)
+        i('LDA', 'imm', 0x1F); i('STA', 'abs', 0x2006); i('LDA', 'imm', 0xD8); i('STA', 'abs', 0x2006)
+        a.label('nosplit')
     i('PLA'); i('TAY'); i('PLA'); i('TAX'); i('PLA')
     i('RTI')
 
@@ -353,7 +385,8 @@ def _mmc1_write(a: Asm, addr: int, value: int, tag: str):
 def template_params(seed: int, board: str) -> dict:
     r = np.random.default_rng([seed, 0x5EED])
     haz_bits = int(r.integers(1, 4))           # one life lost per ~2^(8 + bits) frames
-    ctrl = 0x80 | (0x08 if board == 'mmc3' else int(r.choice([0x00, 0x08, 0x10, 0x18])))
+    ctrl = 0x80 | (0x08 if board == 'mmc3' else int(r.choice([0x08, 0x10])) if board == 'mmc2'
+                   else int(r.choice([0x00, 0x08, 0x10, 0x18])))
     emph = int(r.choice([0, 0, 0, 1, 2, 4]))
     p = dict(
         vel=int(r.integers(1, 7)),
@@ -368,6 +401,8 @@ def template_params(seed: int, board: str) -> dict:
         mask=0x1E | (emph << 5),
         irq_line=32,
     )
+    if board == 'mmc2':   # the four CHR registers ($FD/$FE banks of each half): distinct 4 KB banks of 32
+        p['creg'] = [int(b) for b in r.permutation(32)[:4]]
     return p
 
 
@@ -382,8 +417,11 @@ def make_cart(seed: int, board: str = 'nrom') -> Cart:
     spr = bytearray()
     for k in range(8):
         y = int(r.integers(0, 224)) if k != 1 else 150
-        spr += bytes([y, int(r.integers(0, 256)), int(r.integers(0, 256)) & 0xE3, int(r.integers(0, 248))])
-    prg_size = {'nrom': 32768, 'cnrom': 32768, 'uxrom': 131072, 'mmc1': 131072, 'mmc3': 262144}[board]
+        tile = int(r.integers(0, 256))
+        if board == 'mmc2' and k in (3, 4):
+            tile = 0xFD if k == 3 else 0xFE   # sprite fetches that flip a latch on their lines
+        spr += bytes([y, tile, int(r.integers(0, 256)) & 0xE3, int(r.integers(0, 248))])
+    prg_size = {'nrom': 32768, 'cnrom': 32768, 'uxrom': 131072, 'mmc1': 131072, 'mmc3': 262144, 'mmc2': 131072}[board]
     data = dict(paltab=pal, nttab=nt, sprtab=bytes(spr))
     if board == 'uxrom':
         data['banktab'] = bytes(range(8))
@@ -411,6 +449,8 @@ def make_cart(seed: int, board: str = 'nrom') -> Cart:
         chr_rom = bytes(chr_bytes) + r.integers(0, 256, 131072 - 8192, dtype=np.uint8).tobytes()
     if board == 'cnrom':   # 4 CHR banks of 8 KB
         chr_rom = bytes(chr_bytes) + r.integers(0, 256, 32768 - 8192, dtype=np.uint8).tobytes()
+    if board == 'mmc2':    # 32 banks of 4 KB
+        chr_rom = bytes(chr_bytes) + r.integers(0, 256, 131072 - 8192, dtype=np.uint8).tobytes()
     flags6 = ((mapper & 0x0F) << 4) | 0x01          # vertical mirroring
     flags7 = mapper & 0xF0
     header = b'NES\x1a' + bytes([prg_size // 16384, len(chr_rom) // 8192, flags6, flags7]) + bytes(8)

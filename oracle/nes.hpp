@@ -8,7 +8,9 @@
 //   * the frame log and the FCEUmm line replay (patch:894-1821, batch_frame.cuh),
 //   * the lazy PPU timing events, sprite-0 replay, short ("kook") frames, MMC3 clocks (patch:1822-2240),
 //   * the bus hooks that log PPU writes and board writes (patch:570-780), the DMC (patch:400-569),
-//   * the paged boards MMC1/MMC3 (patch:2841-3367) and the frame loop step_until (rl/csrc/nes_machine.cuh:67-103).
+//   * the paged boards MMC1/MMC2/MMC3 (patch:2841-3367) and the frame loop step_until
+//     (rl/csrc/nes_machine.cuh:67-103); MMC2's latches the frame's fetches leave are resolved at vblank
+//     (patch:1791-1815 frame_resolve_mmc2; rl/csrc/nes_machine.cuh:107-130 runs the same replay after the stop).
 // NeSLE's base tree is not vendored (github.com/hbofz/NeSLE @ 0b04d8b9, cloned by scripts/setup_nesle.sh:9-19), so
 // the 6502 core, the $2002/$2004/$2007 read side, OAM DMA length, the controller port, the UxROM window and cold
 // reset are restated here from public 6502/NES documentation: PARITY UNPINNED against NeSLE for those parts. The
@@ -45,8 +47,8 @@ constexpr u32 kS0Evaluate = 0x80000000u, kS0Known = 0x40000000u, kS0Hit = 0x2000
 constexpr u64 kDmcIdle = ~0ull;
 constexpr u8 kPageVertical = 0x0A, kPageHorizontal = 0x0C, kPageSingleLow = 0x00, kPageSingleHigh = 0x0F;
 
-enum Board : u8 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3, kCnrom = 4 };
-inline bool board_paged(Board b) { return b == kMmc1 || b == kMmc3 || b == kCnrom; }
+enum Board : u8 { kNrom = 0, kUxrom = 1, kMmc1 = 2, kMmc3 = 3, kCnrom = 4, kMmc2 = 5 };
+inline bool board_paged(Board b) { return b == kMmc1 || b == kMmc3 || b == kCnrom || b == kMmc2; }
 
 // ------------------------------------------------------------------------------------------------ cartridge
 
@@ -98,6 +100,14 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
             c.prg_page_mask = prg / 8192 - 1;
             c.chr_page_mask = chr / 1024 - 1;
             break;
+        case 9:   // MMC2 (patch:4007-4030 describe_mapper: 8 KB PRG pages, CHR ROM only, at most 256 KB)
+            if (prg < 32768 || prg > 512 * 1024 || (prg & (prg - 1)) || chr == 0 || (chr & (chr - 1)) ||
+                chr > 256 * 1024)
+                throw std::runtime_error("unsupported MMC2 image size");
+            c.board = kMmc2;
+            c.prg_page_mask = prg / 8192 - 1;
+            c.chr_page_mask = chr / 1024 - 1;
+            break;
         case 1:
         case 4: {
             c.board = mapper == 1 ? kMmc1 : kMmc3;
@@ -110,7 +120,7 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
         }
         default:
             throw std::runtime_error("unsupported mapper " + std::to_string(mapper) +
-                                     " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3)");
+                                     " (supported: 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3, 9 MMC2)");
     }
     return c;
 }
@@ -165,6 +175,7 @@ struct Console {
 
 namespace board {
 enum : u32 { kMmc1Control = 0, kMmc1Chr0 = 1, kMmc1Chr1 = 2, kMmc1Prg = 3, kMmc1Shift = 4, kMmc1Count = 5 };
+enum : u32 { kMmc2Prg = 4, kMmc2Mirror = 5, kMmc2Latch0 = 6, kMmc2Latch1 = 7 };   // r0-r3: CHR FD/FE, FD/FE
 enum : u32 { kMmc3Select = 8, kMmc3Mirror = 9, kMmc3PrgRam = 10, kMmc3Latch = 11, kMmc3Counter = 12,
              kMmc3Enabled = 13, kMmc3Reload = 14 };
 
@@ -201,6 +212,14 @@ inline void sync(const Cart& c, Console& m) {
         chr1(c, m, 2 ^ f, r[1] & 0xFEu); chr1(c, m, 3 ^ f, r[1] | 1u);
         chr1(c, m, 4 ^ f, r[2]); chr1(c, m, 5 ^ f, r[3]); chr1(c, m, 6 ^ f, r[4]); chr1(c, m, 7 ^ f, r[5]);
         set_mirror(c, m, (r[kMmc3Mirror] & 1) ? kPageHorizontal : kPageVertical);
+    } else if (c.board == kMmc2) {   // patch:3027-3035: the switchable 8 KB page, then the last three
+        prg8(c, m, 0, r[kMmc2Prg]);
+        prg8(c, m, 1, ~2u);
+        prg8(c, m, 2, ~1u);
+        prg8(c, m, 3, ~0u);
+        chr4(c, m, 0, r[r[kMmc2Latch0] & 1u]);
+        chr4(c, m, 1, r[2u + (r[kMmc2Latch1] & 1u)]);
+        set_mirror(c, m, r[kMmc2Mirror] ? kPageVertical : kPageHorizontal);
     }
 }
 
@@ -209,6 +228,7 @@ inline void power_on(const Cart& c, Console& m) {
     std::memset(m.regs, 0, sizeof m.regs);
     m.mirroring = header_map(c);
     if (c.board == kMmc1) m.regs[kMmc1Control] = 0x0C;
+    if (c.board == kMmc2) m.regs[kMmc2Latch0] = m.regs[kMmc2Latch1] = 1;   // both halves on their $FE bank
     if (c.board == kMmc3) {
         m.regs[1] = 2; m.regs[2] = 4; m.regs[3] = 5; m.regs[4] = 6; m.regs[5] = 7; m.regs[7] = 1;
         m.regs[kMmc3Mirror] = c.arrangement == 1 ? 1 : 0;
@@ -234,6 +254,19 @@ inline void write(const Cart& c, Console& m, u16 addr, u8 value) {
         sync(c, m);
         return;
     }
+    if (c.board == kMmc2) {   // patch:3147-3156
+        switch (addr & 0xF000) {
+            case 0xA000: r[kMmc2Prg] = value & 0x0F; break;
+            case 0xB000: r[0] = value & 0x1F; break;
+            case 0xC000: r[1] = value & 0x1F; break;
+            case 0xD000: r[2] = value & 0x1F; break;
+            case 0xE000: r[3] = value & 0x1F; break;
+            case 0xF000: r[kMmc2Mirror] = (value & 1) ^ 1; break;
+            default: return;   // $8000-$9FFF: no register
+        }
+        sync(c, m);
+        return;
+    }
     switch (addr & 0xE001) {
         case 0x8000: r[kMmc3Select] = value; break;
         case 0x8001: r[r[kMmc3Select] & 7] = value; break;
@@ -245,6 +278,20 @@ inline void write(const Cart& c, Console& m, u16 addr, u8 value) {
         default: r[kMmc3Enabled] = 1; return;
     }
     sync(c, m);
+}
+
+// MMC2 latch hook: a PPU address in $0FD0-$0FEF / $1FD0-$1FEF puts that half on its $FD or $FE bank (FCEUmm's
+// PPU_hook ranges, patch:3195-3222 mmc2_ppu_address). Returns the latch it changed + 1, or 0.
+inline u32 mmc2_address(const Cart& c, Console& m, u32 addr) {
+    const u32 high = (addr >> 8) & 0x3Fu, low = addr & 0xF0u;
+    if (high >= 0x20u || (high & 0x0Fu) != 0x0Fu || (low != 0xD0u && low != 0xE0u)) return 0;
+    const u32 half = high < 0x10u ? 0u : 1u;
+    const u8 latch = low == 0xE0u ? 1 : 0;
+    u8* r = m.regs;
+    const u8 before = r[kMmc2Latch0 + half];
+    r[kMmc2Latch0 + half] = latch;
+    chr4(c, m, half, r[2u * half + latch]);
+    return before != latch ? half + 1u : 0u;
 }
 
 // MMC3 counter clock, revision B (patch:3162-3174).
@@ -365,6 +412,10 @@ inline void fill_header(const Cart& c, const Console& m, u8 ctrl, u8 mask, u32* 
     if (board_paged(c.board)) {
         for (u32 i = 0; i < 8; ++i) h[3 + (i >> 2)] |= ((m.chr_page[i] >> 10) & 0xFFu) << ((i & 3) * 8);
         h[5] = m.mirroring;
+        if (c.board == kMmc2) {   // patch:1034-1040: latches in h[5], the four CHR registers in h[6]
+            h[5] |= (u32(m.regs[board::kMmc2Latch0] & 1u) << 8) | (u32(m.regs[board::kMmc2Latch1] & 1u) << 16);
+            h[6] = m.regs[0] | (u32(m.regs[1]) << 8) | (u32(m.regs[2]) << 16) | (u32(m.regs[3]) << 24);
+        }
     }
     for (u32 i = 0; i < 8; ++i)
         h[7 + i] = m.pal[4 * i] | (u32(m.pal[4 * i + 1]) << 8) | (u32(m.pal[4 * i + 2]) << 16) |
@@ -470,6 +521,7 @@ struct RState {
     u16 v, t;
     u8 x, ctrl, mask, mirroring;
     u8 chr[8];
+    u8 creg[4], latch[2];   // MMC2
     u8 pal[32];
     u32 sh0, sh1;
     u8 at;
@@ -496,6 +548,9 @@ inline void r_load(RState& s, const u32* h) {
     s.t = static_cast<u16>((h[2] >> 16) & 0x7FFF);
     for (int i = 0; i < 8; ++i) s.chr[i] = static_cast<u8>(h[3 + (i >> 2)] >> ((i & 3) * 8));
     s.mirroring = static_cast<u8>(h[5]);
+    s.latch[0] = static_cast<u8>((h[5] >> 8) & 1);
+    s.latch[1] = static_cast<u8>((h[5] >> 16) & 1);
+    for (int i = 0; i < 4; ++i) s.creg[i] = static_cast<u8>(h[6] >> (8 * i));
     for (int i = 0; i < 32; ++i) s.pal[i] = static_cast<u8>(h[7 + (i >> 2)] >> ((i & 3) * 8));
     s.sh0 = s.sh1 = 0;
     s.at = 0;
@@ -531,6 +586,21 @@ inline u8 r_nt(const Src& src, const RState& s, u32 addr) {
 }
 
 inline bool r_on(const RState& s) { return (s.mask & 0x18) != 0; }
+
+// MMC2 in the replay (patch:1385-1402): a half's four 1 KB pages from the register its latch picks, and the latch
+// hook on every pattern address the frame fetches.
+inline void r_mmc2_select(RState& s, u32 half) {
+    const u32 bank = s.creg[2 * half + s.latch[half]];
+    for (u32 i = 0; i < 4; ++i) s.chr[4 * half + i] = static_cast<u8>(bank * 4 + i);
+}
+inline void r_mmc2_hook(const Src& src, RState& s, u32 addr) {
+    if (src.c->board != kMmc2) return;
+    const u32 high = (addr >> 8) & 0xFF, low = addr & 0xF0;
+    if (high >= 0x20 || (high & 0x0F) != 0x0F || (low != 0xD0 && low != 0xE0)) return;
+    const u32 half = high < 0x10 ? 0 : 1;
+    s.latch[half] = low == 0xE0 ? 1 : 0;
+    r_mmc2_select(s, half);
+}
 
 inline void r_vinc(RState& s) {
     u32 v = s.v;
@@ -568,6 +638,10 @@ inline void r_apply(const Src& src, RState& s, u32 i, bool drawing) {
         case kEvPalette: s.pal[aux & 31] = static_cast<u8>(value); s.v = static_cast<u16>((s.v + inc) & 0x7FFF); break;
         case kEvChr: s.chr[aux & 7] = static_cast<u8>(value); break;
         case kEvMirror: s.mirroring = static_cast<u8>(value); break;
+        case kEvMmc2:
+            if (aux < 4) { s.creg[aux] = static_cast<u8>(value); r_mmc2_select(s, aux >> 1); }
+            else if (aux == 6 || aux == 7) { s.latch[aux - 6] = static_cast<u8>(value & 1); r_mmc2_select(s, aux - 6); }
+            break;
         default: break;
     }
 }
@@ -577,6 +651,8 @@ inline void r_begin_frame(const Src& src, RState& s) {
     if (r_on(s)) s.v = s.t;
 }
 
+// kLatchesOnly: the MMC2 resolve's replay, which needs the latches and nothing drawn (patch:1496-1526).
+template <bool kLatchesOnly = false>
 inline void r_tiles(const Src& src, RState& s, RLine& line, int last, bool pixels) {
     const int first = line.firsttile;
     const u8 backdrop = static_cast<u8>((s.pal[0] & 0x3F) | 0x40);
@@ -588,9 +664,15 @@ inline void r_tiles(const Src& src, RState& s, RLine& line, int last, bool pixel
         return;
     }
     int tile = first;
-    if (!pixels) {
+    if (!pixels && (kLatchesOnly || src.c->board != kMmc2)) {
+        // no pixels: the address moves; only the last two tiles' fetches stay in the shift registers. MMC2's
+        // latches see every pattern address, which needs only the tile number.
         for (; tile < last - 2; ++tile) {
             const u32 v = s.v;
+            if (kLatchesOnly) {
+                const u32 tidx = r_nt(src, s, 0x2000 | (v & 0x0FFF));
+                r_mmc2_hook(src, s, (tidx << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7)));
+            }
             s.v = static_cast<u16>(((v & 0x1F) == 0x1F) ? (v ^ 0x41F) : (v + 1));
         }
     }
@@ -613,7 +695,8 @@ inline void r_tiles(const Src& src, RState& s, RLine& line, int last, bool pixel
         const u32 ab = r_nt(src, s, base | 0x3C0 | (zz >> 2) | ((v & 0x380) >> 4));
         const u32 cc = (ab >> ((zz & 2) + ((v & 0x40) >> 4))) & 3;
         const u32 vadr = (tidx << 4) + (((s.ctrl & 0x10u) << 8) | ((v >> 12) & 7));
-        const u8 p0 = r_chr(src, s, vadr), p1 = r_chr(src, s, vadr + 8);
+        const u8 p0 = r_chr(src, s, vadr), p1 = r_chr(src, s, vadr + 8);   // both through the bank before the hook
+        r_mmc2_hook(src, s, vadr);
         s.at = static_cast<u8>((s.at >> 2) | (cc << 2));
         s.sh0 = (s.sh0 << 8) | p0;
         s.sh1 = (s.sh1 << 8) | p1;
@@ -642,12 +725,13 @@ inline void r_check_hit(RState& s, const RLine& line, int p) {
     }
 }
 
+template <bool kLatchesOnly = false>
 inline void r_update(const Src& src, RState& s, RLine& line, int p, bool pixels) {
     int last = p >> 3;
     if (pixels && s.sphitx != 0x100 && s.sphitx < p - 16 && !(s.sphitx < (last - 2) * 8)) ++last;
     if (last > 34) last = 34;
     if (last <= line.firsttile) return;
-    r_tiles(src, s, line, last, pixels);
+    r_tiles<kLatchesOnly>(src, s, line, last, pixels);
     if (p >= 268 && line.tofix) {
         if (r_on(s)) r_vinc(s);
         line.tofix = false;
@@ -655,6 +739,7 @@ inline void r_update(const Src& src, RState& s, RLine& line, int p, bool pixels)
     if (pixels) r_check_hit(s, line, p);
 }
 
+template <bool kLatchesOnly = false>
 inline void r_line(const Src& src, RState& s, RLine& line, int l, bool pixels) {
     const int start = l * 341 - 16;
     line.firsttile = 0;
@@ -663,10 +748,11 @@ inline void r_line(const Src& src, RState& s, RLine& line, int l, bool pixels) {
     if (pixels) std::memset(line.px, 0xFF, 256);
     while (s.cursor < src.count && ev_start(src, s.cursor) < start + 272) {
         const u32 kind = ev_kind(src, s.cursor);
-        if (kind != kEvDataWrite && kind != kEvPalette) r_update(src, s, line, ev_end(src, s.cursor) - start, pixels);
+        if (kind != kEvDataWrite && kind != kEvPalette)
+            r_update<kLatchesOnly>(src, s, line, ev_end(src, s.cursor) - start, pixels);
         r_apply(src, s, s.cursor++, true);
     }
-    r_update(src, s, line, 272, pixels);
+    r_update<kLatchesOnly>(src, s, line, 272, pixels);
     if (line.tofix) {
         if (r_on(s)) r_vinc(s);
         line.tofix = false;
@@ -698,7 +784,7 @@ inline u32 r_compose(RState& s, RLine& line) {
 inline void r_end_of_line(const Src& src, RState& s, int l, bool sprites) {
     const int start = l * 341 - 16;
     s.sphitx = 0x100;
-    if (r_on(s) && sprites) {
+    if (r_on(s) && (sprites || src.c->board == kMmc2)) {   // MMC2: every fetch moves the latches
         const u32 c = s.ctrl;
         const u32 h = (c & 0x20) ? 16 : 8;
         const u32 vofs = ((c & 0x08) && !(c & 0x20)) ? 0x1000 : 0;
@@ -717,6 +803,7 @@ inline void r_end_of_line(const Src& src, RState& s, int l, bool sprites) {
             vadr &= 0x1FFF;
             f.lo[f.n] = r_chr(src, s, vadr);
             f.hi[f.n] = r_chr(src, s, vadr + 8);
+            r_mmc2_hook(src, s, vadr);
             f.attr[f.n] = spr[2];
             f.x[f.n] = spr[3];
             ++f.n;
@@ -772,6 +859,28 @@ inline Hit0 sprite0_hit(const Cart& c, const Console& m) {
         r_end_of_line(src, s, l, l >= first - 1);
     }
     return Hit0{nesle_dot(last * 341 + 256), false};
+}
+
+// MMC2 at vblank: the latches the frame's own tile and sprite fetches left (patch:1791-1815 frame_resolve_mmc2),
+// replayed from the writing bank over the live nametable RAM and OAM (which hold what the frozen snapshots hold).
+inline void resolve_mmc2(const Cart& c, Console& m) {
+    const u32* h = log_bank_ptr(m, (m.log_bank & 1u) ^ 1u);
+    const Src src = make_src(c, m, h, m.log_count, m.nt, m.oam);
+    RState s;
+    r_load(s, h);
+    RLine line;
+    r_begin_frame(src, s);
+    for (int l = 0; l < 240; ++l) {
+        r_line<true>(src, s, line, l, false);
+        r_end_of_line(src, s, l, true);
+    }
+    while (s.cursor < src.count) r_apply(src, s, s.cursor++, false);
+    for (u32 half = 0; half < 2; ++half) {
+        if (m.regs[board::kMmc2Latch0 + half] != s.latch[half]) {
+            m.regs[board::kMmc2Latch0 + half] = s.latch[half];
+            board::chr4(c, m, half, m.regs[2 * half + s.latch[half]]);
+        }
+    }
 }
 
 // The last frozen frame as colour numbers of the 240x224 crop + per-line emphasis (rl/csrc/nes_machine.cuh:133-155).
@@ -866,6 +975,7 @@ inline void ppu_settle(const Cart& c, Console& m, u32 dots) {
         if (crossed(kVblankFlagDot)) m.status |= 0x80;
         if (crossed(kVblankDot)) {
             if (m.ctrl & 0x80) m.nmi_pending = 1;
+            if (c.board == kMmc2) resolve_mmc2(c, m);
             m.log_bank = log_freeze(m, m.log_count);
             std::memcpy(m.snap_oam, m.oam, 256);
             std::memcpy(m.snap_nt, m.nt, 2048);
@@ -908,6 +1018,16 @@ inline void ppu_mem_write(const Cart& c, Console& m, u32 addr, u8 value) {
 
 inline void vram_inc(Console& m) { m.v = static_cast<u16>((m.v + ((m.ctrl & 4) ? 32 : 1)) & 0x7FFF); }
 
+// The VRAM address the CPU puts on the PPU bus ($2006 / $2007): MMC2's latch hook, the change logged for the
+// renderer while a frame is drawn (patch:615-636 bus_ppu_address).
+inline void ppu_address(const Cart& c, Console& m, u32 addr) {
+    if (c.board != kMmc2) return;
+    if (const u32 changed = board::mmc2_address(c, m, addr)) {
+        const u32 reg = board::kMmc2Latch0 + changed - 1;
+        log_event(m, kEvMmc2, m.regs[reg], reg);
+    }
+}
+
 inline u8 cpu_read(const Cart& c, Console& m, u16 addr) {
     if (addr < 0x2000) return m.ram[addr & 0x7FF];
     if (addr < 0x4000) {
@@ -925,12 +1045,15 @@ inline u8 cpu_read(const Cart& c, Console& m, u16 addr) {
                 if (pa >= 0x3F00) {
                     value = ppu_mem_read(c, m, pa);
                     m.read_buffer = ppu_mem_read(c, m, pa - 0x1000);
+                    ppu_address(c, m, pa);
                 } else {
                     value = m.read_buffer;
+                    ppu_address(c, m, pa);   // the buffer refills through the bank the address picks
                     m.read_buffer = ppu_mem_read(c, m, pa);
                 }
                 vram_inc(m);
                 log_event(m, kEvDataRead, 0);
+                ppu_address(c, m, m.v & 0x3FFF);
                 m.open_bus = value;
                 return value;
             }
@@ -958,9 +1081,12 @@ inline void mapper_write(const Cart& c, Console& m, u16 addr, u8 value) {
         u32 before[8];
         for (int i = 0; i < 8; ++i) before[i] = m.chr_page[i];
         const u8 mir = m.mirroring;
+        const u8 creg[4] = {m.regs[0], m.regs[1], m.regs[2], m.regs[3]};
         board::write(c, m, addr, value);
         for (u32 i = 0; i < 8; ++i) if (m.chr_page[i] != before[i]) log_event(m, kEvChr, m.chr_page[i] >> 10, i);
         if (m.mirroring != mir) log_event(m, kEvMirror, m.mirroring);
+        if (c.board == kMmc2)   // the CHR registers a write changed (patch:661-665)
+            for (u32 i = 0; i < 4; ++i) if (m.regs[i] != creg[i]) log_event(m, kEvMmc2, m.regs[i], i);
         return;
     }
     board::write(c, m, addr, value);
@@ -994,7 +1120,7 @@ inline void cpu_write(const Cart& c, Console& m, u16 addr, u8 value) {
             case 6:
                 log_event(m, kEvAddr, value, m.w);
                 if (m.w == 0) { m.t = static_cast<u16>((m.t & 0x00FF) | ((value & 0x3F) << 8)); m.w = 1; }
-                else { m.t = static_cast<u16>((m.t & 0x7F00) | value); m.v = m.t; m.w = 0; }
+                else { m.t = static_cast<u16>((m.t & 0x7F00) | value); m.v = m.t; m.w = 0; ppu_address(c, m, m.v); }
                 break;
             case 7: {
                 const u32 pa = m.v & 0x3FFF;
@@ -1002,6 +1128,7 @@ inline void cpu_write(const Cart& c, Console& m, u16 addr, u8 value) {
                 if (pa >= 0x3F00) log_event(m, kEvPalette, value, pal_index(pa));
                 else log_event(m, kEvDataWrite, 0);
                 vram_inc(m);
+                ppu_address(c, m, m.v & 0x3FFF);
                 break;
             }
             default: break;
