@@ -574,7 +574,6 @@ struct Emu {
             if (crossed(kVblankFlagDot)) status |= 0x80u;
             if (crossed(kVblankDot)) {
                 if (ctrl & 0x80u) nmi = 1;
-                if constexpr (BOARD == kMmc2) mmc2_resolve();
                 log_freeze();
             }
             if (crossed(kStatusClearDot)) status &= 0x1Fu;
@@ -1209,6 +1208,9 @@ struct Emu {
         }
         if (pend != 0) settle(pend);
         pend = 0;
+        // MMC2: the latches the frozen frame's fetches left, resolved after the vblank stop (nothing runs between the
+        // two; rl/csrc/rlenv_core.cuh:161-176 does the same) by every lane that froze one, together
+        if constexpr (BOARD == kMmc2) { if (froze) mmc2_resolve(); }
         return fault;
     }
 
@@ -1581,7 +1583,7 @@ __device__ __forceinline__ void mmc2_plain_line(const S0Ctx& c, S0State& s, Mmc2
 }
 
 // FetchSpriteData at the end of line l with rendering on: every sprite in range (at most 8, OAM order) goes through
-// the latch hook; sprite 0's pattern bytes are kept for the hit check. `vis`: the OAM entries with y < 240.
+// the latch hook; sprite 0's pattern bytes are kept for the hit check. `vis`: the OAM entries to look at (mmc2_begin).
 template <u32 BOARD>
 __device__ __forceinline__ void mmc2_sprites(const S0Ctx& c, S0State& s, int l, u64 vis) {
     auto oamb = [&](u32 i) -> u32 { return reinterpret_cast<const u8*>(c.soam + (i >> 2) * kEnvsPerWarp)[i & 3u]; };
@@ -1629,9 +1631,18 @@ __device__ __forceinline__ void mmc2_begin(const S0Ctx& c, S0State& s, int kook,
     const u32* ev = h + kLogHdr;
     while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply<BOARD>(s, ev, s.cursor++, false);
     if (s.mask & 0x18u) s.v = s.t;
-    vis = 0;
-    for (u32 i = 0; i < 64; ++i)
-        if (reinterpret_cast<const u8*>(c.soam + i * kEnvsPerWarp)[0] < 240u) vis |= 1ull << i;
+    // the OAM entries that can be in range of a line (y < 240); with at most 8 of them the 8-sprite limit never
+    // binds, and only sprite 0 and the sprites whose fetch can reach a latch address (tile $FC-$FF covers both
+    // sprite heights) need a look
+    u64 all = 0, rel = 1;
+    for (u32 i = 0; i < 64; ++i) {
+        const u32 w = c.soam[i * kEnvsPerWarp];
+        if ((w & 0xFFu) < 240u) {
+            all |= 1ull << i;
+            if (((w >> 8) & 0xFFu) >= 0xFCu) rel |= 1ull << i;
+        }
+    }
+    vis = __popcll(all) <= 8 ? (all & rel) : all;
 }
 
 // End of line l after its pixels: sprite fetch (rendering on), Fixit2, RefreshSprites' sprite-0 data.
@@ -1715,12 +1726,13 @@ __device__ __forceinline__ Hit0 Emu<BOARD>::sprite0_eval() const {
     else return sprite0_hit<BOARD>(c);
 }
 
-// Vblank on MMC2: the latches this frame's own fetches left go back to the board (patch:1791-1815).
+// MMC2 after the vblank stop: the latches the frozen frame's own fetches left go back to the board (patch:1791-1815
+// frame_resolve_mmc2; rl/csrc/nes_machine.cuh:107-130 resolve_mmc2_frozen reads the frozen log the same way).
 template <u32 BOARD>
 __device__ __forceinline__ void Emu<BOARD>::mmc2_resolve() {
     S0Ctx c;
-    c.bank = writing_bank();
-    c.count = log_n < kLogEv ? log_n : kLogEv;
+    c.bank = log_bank(log_ctl & kLcBank);
+    c.count = min(c.bank[0] & ~kLogOverflow, kLogEv);
     c.nt = nt();
     c.soam = &sh.oam[0][lane];
     c.chr = C.chr;

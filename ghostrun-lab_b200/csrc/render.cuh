@@ -315,6 +315,50 @@ struct Renderer {
         mmc2_select(half);
     }
 
+    // MMC2, an event-free line drawn with rendering on: fetch c = lane through the pages its latch had then (the last
+    // $FD / $FE tile among fetches 0..c-1, else the latch the line started with; all 34 fetches use one pattern table,
+    // so one half), fetch 32 in c32; the shift registers after fetches 32 / 33 and the line's final latch are kept.
+    __device__ __forceinline__ u32 mmc2_fast_fetch(u32 v0, u32& c32) {
+        const LineFetch lf = line_fetch(v0);
+        const u32 hb = (s.ctrl >> 4) & 1u, fy = (v0 >> 12) & 7u;
+        auto at = [&](u32 c, u32& attr) {
+            const u32 cc = lf.cx0 + c, col = cc & 31u;
+            const u32 base = ((cc >> 5) & 1u) ? lf.base_b : lf.base_a;
+            const u32 ab = W.nt[base | lf.arow | (col >> 2)];
+            attr = (ab >> (lf.ashift | (col & 2u))) & 3u;
+            return static_cast<u32>(W.nt[base | lf.row | col]);
+        };
+        auto nib = [&](u32 tile, u32 latch, u32 attr) {
+            const u32 bank = s.creg[2 * hb + latch];
+            const u32 off = (((bank * 4u + (tile >> 6)) & A.cart.chr_page_mask) << 10) | ((tile & 63u) << 4) | fy;
+            return spread[__ldg(A.cart.chr + off)] | (spread[__ldg(A.cart.chr + off + 8u)] << 1) | (attr * 0x44444444u);
+        };
+        u32 a0, a32, a33;
+        const u32 t = at(lane, a0), t32 = at(32, a32), t33 = at(33, a33);
+        const u32 fm = __ballot_sync(0xFFFFFFFFu, t == 0xFDu || t == 0xFEu);
+        const u32 fe = __ballot_sync(0xFFFFFFFFu, t == 0xFEu);
+        const u32 lin = s.latch[hb];
+        const u32 below = fm & ((1u << lane) - 1u);
+        const u32 lc = below ? (fe >> (31 - __clz(below))) & 1u : lin;
+        const u32 l32 = fm ? (fe >> (31 - __clz(fm))) & 1u : lin;
+        const u32 l33 = (t32 == 0xFDu || t32 == 0xFEu) ? (t32 == 0xFEu ? 1u : 0u) : l32;
+        const u32 lout = (t33 == 0xFDu || t33 == 0xFEu) ? (t33 == 0xFEu ? 1u : 0u) : l33;
+        c32 = nib(t32, l32, a32);
+        const u32 c33 = nib(t33, l33, a33);
+        u32 lo32 = 0, hi32 = 0, lo33 = 0, hi33 = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            lo32 |= ((c32 >> (4 * k)) & 1u) << (7 - k); hi32 |= ((c32 >> (4 * k + 1)) & 1u) << (7 - k);
+            lo33 |= ((c33 >> (4 * k)) & 1u) << (7 - k); hi33 |= ((c33 >> (4 * k + 1)) & 1u) << (7 - k);
+        }
+        s.sh0 = (lo32 << 8) | lo33;
+        s.sh1 = (hi32 << 8) | hi33;
+        s.at = ((c32 >> 2) & 3u) | (((c33 >> 2) & 3u) << 2);
+        const u32 ca = nib(t, lc, a0);
+        if (lout != lin) { s.latch[hb] = lout; mmc2_select(hb); }
+        return ca;
+    }
+
     // The shift registers after the last fast line: its fetches 32 and 33.
     __device__ void materialize_shift() {
         if (!s.lazy) return;
@@ -1115,7 +1159,7 @@ struct Renderer {
         for (int l = 0; l < kObsY0 + kObsH; ++l) {
             const int start = l * 341 - 16;
             u32 w0, w1;   // this lane's 8 background pixels (colour | 0x40 transparent), byte k = pixel 8L+k
-            if (BOARD == kMmc2 || s.next_t < start + 272) {   // MMC2: every fetch may move a latch
+            if (s.next_t < start + 272) {
                 exact_line(l);
                 const uint2 q = reinterpret_cast<const uint2*>(W.px)[lane];
                 w0 = q.x; w1 = q.y;
@@ -1126,12 +1170,18 @@ struct Renderer {
                     w0 = w1 = bdw;   // rendering off: backdrop, nothing fetched, v unchanged
                 } else {
                     const u32 v0 = s.v;
-                    const LineFetch lf = line_fetch(v0);
-                    const u32 ca = line_tile(lf, lane);
+                    u32 ca, c32 = 0;
+                    if constexpr (BOARD == kMmc2) {
+                        ca = mmc2_fast_fetch(v0, c32);
+                    } else {
+                        const LineFetch lf = line_fetch(v0);
+                        ca = line_tile(lf, lane);
+                        if (lane == 31 && s.sphitx != 0x100u && s.sphitx >= 241u) c32 = line_tile(lf, 32);
+                    }
                     u32 cn = __shfl_down_sync(0xFFFFFFFFu, ca, 1);
                     // fetch 32 only feeds pixels 248..255 (right of the crop): needed for a sprite-0 check there
                     const bool need32 = s.sphitx != 0x100u && s.sphitx >= 241u;
-                    if (need32 && lane == 31) cn = line_tile(lf, 32);
+                    if (need32 && lane == 31) cn = c32;
                     const u32 sel = __funnelshift_r(ca, cn, 4 * s.x);
                     if (s.mask & 0x08u) {
                         // colour 0 of every sub-palette shows the backdrop
@@ -1156,7 +1206,9 @@ struct Renderer {
                         const u32 hits = win & s.sphitmask & lim;
                         if (hits) { s.hit = 1; s.hit_x = sx + (__ffs(hits) - 1); s.sphitx = 0x100u; }
                     }
-                    s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mir = s.mirroring; s.lz_saved = 0;
+                    if constexpr (BOARD != kMmc2) {   // MMC2 keeps its shift registers (mmc2_fast_fetch)
+                        s.lazy = 1; s.lz_v = v0; s.lz_ctrl = s.ctrl; s.lz_mir = s.mirroring; s.lz_saved = 0;
+                    }
                     s.v = v_inc_y(v_inc_x_n(v0, 34));
                 }
             }

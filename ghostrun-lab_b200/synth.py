@@ -19,7 +19,7 @@ CHR into CHR-RAM at reset, MMC3 arms its scanline IRQ for line 32 each frame and
 (a mid-frame split the renderer must replay). CNROM switches its 8 KB CHR bank on every level change. MMC2 (mapper 9)
 draws from both 4 KB halves through its $FD/$FE latches: the random nametable and two sprites carry $FD/$FE tiles
 that flip them mid-line, the NMI puts $0FD8/$0FE8 and $1FD8/$1FE8 on the PPU bus ($2006 + a $2007 read) by frame
-parity, every 16th frame it waits into the picture and rewrites a CHR register and $2006 there (logged mid-frame
+parity, every 64th frame it waits into the picture and rewrites a CHR register and $2006 there (logged mid-frame
 register and latch changes), and every level change switches the $8000 PRG page.
 
 The reward side is a 13th reward10 reader (`SYNTH_READER`): RAM $10-$17 -> Signals, with per-game seeded fp32
@@ -334,12 +334,14 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     i('LDA', 'zp', ZP_PROGRESS); i('LSR', 'acc'); i('STA', 'abs', OAM_BUF + 7)
     a.label('nmi_out')
     if board == 'mmc2':
-        # every 16th frame: wait ~5,100 cycles (into the picture, about line 30), then rewrite the $FE bank of the
-        # $0000 half and put $1FD8 on the bus (the rest of the frame is drawn from that address)
-        i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 0x0F); i('BNE', 'rel', 'nosplit')
-        i('LDY', 'imm', 4)
-        a.label('dly'); i('LDX', 'imm', 255)
-        a.label('dly2'); i('DEX'); i('BNE', 'rel', 'dly2'); i('DEY'); i('BNE', 'rel', 'dly')
+        # every 64th frame: wait ~2,400 cycles in 7-cycle instructions (into the picture, about line 10), then
+        # rewrite the $FE bank of the $0000 half and put $1FD8 on the bus (the rest of the frame is drawn from there)
+        i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 0x3F); i('BNE', 'rel', 'nosplit')
+        i('LDX', 'imm', 0); i('LDY', 'imm', 40)
+        a.label('dly')
+        for _ in range(8):
+            i('ROL', 'absx', 0x0700)
+        i('DEY'); i('BNE', 'rel', 'dly')
         i('LDA', 'zp', ZP_LEVEL); i('AND', 'imm', 0x0F); i('ORA', 'imm', 0x10); i('STA', 'abs', 0xC000)
         i('LDA', 'imm', 0x1F); i('STA', 'abs', 0x2006); i('LDA', 'imm', 0xD8); i('STA', 'abs', 0x2006)
         a.label('nosplit')
