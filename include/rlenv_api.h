@@ -16,7 +16,7 @@ extern "C" {
 
 // rl/csrc/rlenv_api.h:9-11. game_ids: rl10 game ids (0..11 the reference's commercial games, 12..23 the seeded
 // synthetic games of ghostrun-lab_b200/synth.py; a game needs its reward spec registered first, rl10_register_game).
-// roms: iNES images (mappers 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3); boot_pads: pad byte of every frame from power-on to
+// roms: iNES images (mappers 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3, 9 MMC2); boot_pads: pad byte of every frame from power-on to
 // the boot snapshot; n_envs: envs per game. sticky / dropout: 0/1; idle_max: 0..idle_max random idle frames at
 // episode starts; device: CUDA device index.
 void* rlenv_create(int ngames, const int* game_ids, const uint8_t* const* roms, const size_t* rom_sizes,
