@@ -85,10 +85,10 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.board = kUxrom;
         c.bank_mask = static_cast<u32>(prg_bytes / 16384 - 1);
         c.fixed_base = static_cast<u32>(prg_bytes - 16384);
-    } else if (mapper == 3) {   // CNROM: 16 / 32 KB PRG fixed, CHR ROM in 8 KB banks
-        if ((prg_bytes != 16384 && prg_bytes != 32768) || chr_bytes == 0 || (chr_bytes & (chr_bytes - 1)) ||
+    } else if (mapper == 3) {   // CNROM (patch:4007-4030): PRG pages 0-3 mapped, CHR ROM in 8 KB banks
+        if (prg_bytes < 16384 || prg_bytes > 512 * 1024 || !pow2 || chr_bytes == 0 || (chr_bytes & (chr_bytes - 1)) ||
             chr_bytes > 256 * 1024)
-            throw std::runtime_error("CNROM needs 16 / 32 KB PRG and a power-of-two CHR ROM up to 256 KB");
+            throw std::runtime_error("unsupported CNROM image size (PRG 16-512 KB, a power-of-two CHR ROM up to 256 KB)");
         c.board = kCnrom;
         c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);
         c.chr_page_mask = static_cast<u32>(chr_bytes / 1024 - 1);
@@ -101,7 +101,7 @@ inline HostCart parse_rom(const u8* rom, std::size_t n) {
         c.chr_page_mask = static_cast<u32>(chr_bytes / 1024 - 1);
     } else if (mapper == 1 || mapper == 4) {
         const std::size_t cb = chr_bytes ? chr_bytes : 8192;
-        if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || (cb & (cb - 1)))
+        if (prg_bytes < 32768 || prg_bytes > 512 * 1024 || !pow2 || (cb & (cb - 1)) || cb > 256 * 1024)
             throw std::runtime_error("unsupported MMC1/MMC3 image size");
         c.board = mapper == 1 ? kMmc1 : kMmc3;
         c.prg_page_mask = static_cast<u32>(prg_bytes / 8192 - 1);

@@ -208,7 +208,9 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             u8* prg = M.allocn<u8>(hc.prg.size());
             ck(cudaMemcpy(prg, hc.prg.data(), hc.prg.size(), cudaMemcpyHostToDevice), "prg");
             C.prg = prg;
-            C.prg_mask = static_cast<u32>(hc.prg.size() - 1);
+            // NROM / CNROM read the staged window through this mask: the whole 16 / 32 KB image (a 16 KB one
+            // mirrored); CNROM maps pages 0-3 of a larger image, its first 32 KB
+            C.prg_mask = static_cast<u32>(std::min<std::size_t>(hc.prg.size(), 32768) - 1);
             if (!hc.chr.empty()) {
                 u8* chr = M.allocn<u8>(hc.chr.size());
                 ck(cudaMemcpy(chr, hc.chr.data(), hc.chr.size(), cudaMemcpyHostToDevice), "chr");
@@ -226,10 +228,11 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
                 C.chrx = nullptr;
             }
             C.board = hc.board;
-            // PRG staged in the emulation blocks' shared memory: all of it on NROM (16 / 32 KB), else the last 16 KB
-            C.prg_stage_bytes = (hc.board == kNrom || hc.board == kCnrom) ? static_cast<u32>(hc.prg.size())
-                                                                           : std::min<u32>(16384u, static_cast<u32>(hc.prg.size()));
-            C.prg_stage_base = static_cast<u32>(hc.prg.size()) - C.prg_stage_bytes;
+            // PRG staged in the emulation blocks' shared memory: the whole mapped window on NROM / CNROM (the first
+            // 16 / 32 KB), else the last 16 KB
+            const bool fixed = hc.board == kNrom || hc.board == kCnrom;
+            C.prg_stage_bytes = fixed ? C.prg_mask + 1u : std::min<u32>(16384u, static_cast<u32>(hc.prg.size()));
+            C.prg_stage_base = fixed ? 0u : static_cast<u32>(hc.prg.size()) - C.prg_stage_bytes;
             C.arrangement = hc.arrangement;
             C.bank_mask = hc.bank_mask;
             C.fixed_base = hc.fixed_base;

@@ -93,8 +93,10 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
             c.bank_mask = prg / 16384 - 1;
             c.fixed_base = prg - 16384;
             break;
-        case 3:   // CNROM (patch:3995-4027 describe_mapper: 16 / 32 KB PRG, CHR ROM in 8 KB banks)
-            if ((prg != 16384 && prg != 32768) || chr == 0 || (chr & (chr - 1)) || chr > 256 * 1024)
+        case 3:   // CNROM (patch:4007-4030 describe_mapper: PRG 16 KB - 512 KB in a power-of-two count of 8 KB pages,
+                  // of which pages 0-3 are mapped; CHR ROM only, at most 256 KB)
+            if (prg < 16384 || prg > 512 * 1024 || (prg & (prg - 1)) || chr == 0 || (chr & (chr - 1)) ||
+                chr > 256 * 1024)
                 throw std::runtime_error("unsupported CNROM image size");
             c.board = kCnrom;
             c.prg_page_mask = prg / 8192 - 1;
@@ -112,7 +114,8 @@ inline Cart parse_ines(const u8* rom, std::size_t n) {
         case 4: {
             c.board = mapper == 1 ? kMmc1 : kMmc3;
             const u32 chr_bytes = chr == 0 ? 8192u : chr;
-            if (prg < 32768 || prg > 512 * 1024 || (prg & (prg - 1)) || (chr_bytes & (chr_bytes - 1)))
+            if (prg < 32768 || prg > 512 * 1024 || (prg & (prg - 1)) || (chr_bytes & (chr_bytes - 1)) ||
+                chr_bytes > 256 * 1024)
                 throw std::runtime_error("unsupported MMC1/MMC3 image size");
             c.prg_page_mask = prg / 8192 - 1;
             c.chr_page_mask = chr_bytes / 1024 - 1;

@@ -1,0 +1,25 @@
+"""The reference's known-answer tests for its emulator extensions (DMC channel and $4015, frame-log replay renderer;
+third_party/nesle-extensions.patch:4065-4207, 4355-4522), restated in tests/kat/oracle_kat.cpp against the CPU
+oracle's own functions, compiled here with g++ and run. This pins those parts of the oracle to the reference's
+expected values; the GPU parity tests then hold the product bit-exact to the oracle."""
+from __future__ import annotations
+
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_passes_the_reference_known_answer_tests(tmp_path):
+    exe = tmp_path / 'oracle_kat'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_kat.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all known-answer checks passed' in run.stdout
