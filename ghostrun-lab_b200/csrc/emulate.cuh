@@ -163,6 +163,11 @@ struct Hit0 { u32 dot; bool hit; };
 #define GR_ENVS_PER_WARP 32
 #endif
 constexpr u32 kEnvsPerWarp = GR_ENVS_PER_WARP;
+// Emulation warps per block: each stages its own consoles, the block shares one decode table and one PRG window
+#ifndef GR_FRAMES_WARPS
+#define GR_FRAMES_WARPS 1
+#endif
+constexpr u32 kFramesWarps = GR_FRAMES_WARPS;
 static_assert(kEnvsPerWarp == 4 || kEnvsPerWarp == 8 || kEnvsPerWarp == 16 || kEnvsPerWarp == 32, "envs per warp");
 
 // Shared-memory staging of one warp's consoles: register words, CPU RAM and OAM, each lane a column (word w of

@@ -467,30 +467,37 @@ static __device__ void reset_state(const GameArgs& g, const EnvArgs& A, u32 ge) 
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-// Emulation, one warp = kEnvsPerWarp envs per block, consoles staged in shared memory for the whole launch.
+// Emulation: kFramesWarps warps per block, kEnvsPerWarp envs per warp, consoles staged in shared memory for the whole
+// launch.
 // `restart` = 0: the 4 frames of a decision for envs [e0, e0+n); 1: restart frames for the listed envs.
-constexpr std::size_t kFramesSmem = sizeof(EmuShared) + 256 * sizeof(u32);   // + the cart's staged PRG window
-inline std::size_t frames_smem(const CartView& c) { return kFramesSmem + c.prg_stage_bytes; }
+// Shared memory of an emulation block: kFramesWarps console stagings, the decode table, the cart's PRG window.
+constexpr std::size_t kDtabOff = kFramesWarps * sizeof(EmuShared);
+constexpr std::size_t kFramesSmem = kDtabOff + 256 * sizeof(u32);   // + the cart's staged PRG window
+// static: the board units may compile different shapes (GR_ENVS_PER_WARP / GR_FRAMES_WARPS), each its own copy
+static inline std::size_t frames_smem(const CartView& c) { return kFramesSmem + c.prg_stage_bytes; }
+static inline u32 frames_blocks(u32 n) { return (n + kEnvsPerWarp * kFramesWarps - 1) / (kEnvsPerWarp * kFramesWarps); }
 
-// The cart's PRG window into shared memory (whole warp, 16-byte vectors).
-__device__ __forceinline__ void stage_prg(const CartView& c, u8* dst, u32 lane) {
+// The cart's PRG window into shared memory (threads tid of nthreads, 16-byte vectors).
+__device__ __forceinline__ void stage_prg(const CartView& c, u8* dst, u32 tid, u32 nthreads) {
     const uint4* src = reinterpret_cast<const uint4*>(c.prg + c.prg_stage_base);
     uint4* d = reinterpret_cast<uint4*>(dst);
-    for (u32 i = lane; i < c.prg_stage_bytes / 16; i += 32) d[i] = __ldg(src + i);
+    for (u32 i = tid; i < c.prg_stage_bytes / 16; i += nthreads) d[i] = __ldg(src + i);
 }
 
 template <u32 BOARD>
-__global__ void __launch_bounds__(32, 1) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
+__global__ void __launch_bounds__(32 * kFramesWarps, 1) k_frames(const __grid_constant__ GameArgs g, const __grid_constant__ EnvArgs A, int restart) {
     extern __shared__ __align__(16) u8 smem_raw[];
-    EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
-    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    const u32 lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;
+    EmuShared& sh = reinterpret_cast<EmuShared*>(smem_raw)[wid];
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + kDtabOff);
     u8* prg_s = smem_raw + kFramesSmem;
-    const u32 lane = threadIdx.x;
-    for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
-    stage_prg(g.cart, prg_s, lane);
-    __syncwarp();
+    for (u32 i = threadIdx.x; i < 256; i += blockDim.x) dtab[i] = kDecode.t[i];
+    stage_prg(g.cart, prg_s, threadIdx.x, blockDim.x);
+    __syncthreads();
     const u32 total = restart ? *A.list_count : g.n;
-    for (u32 base = blockIdx.x * kEnvsPerWarp; base < total; base += gridDim.x * kEnvsPerWarp) {
+    // each warp its own run of kEnvsPerWarp envs; no block-wide synchronisation from here on
+    for (u32 base = (blockIdx.x * kFramesWarps + wid) * kEnvsPerWarp; base < total;
+         base += gridDim.x * kFramesWarps * kEnvsPerWarp) {
         const u32 k = base + lane;
         u32 ge = 0;
         bool valid = lane < kEnvsPerWarp && k < total;
@@ -948,11 +955,11 @@ __global__ void __launch_bounds__(32, 1) k_chain(const __grid_constant__ GameArg
     if (g.lv_chain_ok[s] || g.lv_deaths[s] < 0 || g.lv_idle_n == 0) return;   // same for the whole block
     extern __shared__ __align__(16) u8 smem_raw[];
     EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
-    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + kDtabOff);
     u8* prg_s = smem_raw + kFramesSmem;
     const u32 lane = threadIdx.x;
     for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
-    stage_prg(g.cart, prg_s, lane);
+    stage_prg(g.cart, prg_s, lane, 32);
     const StateView& S = g.lv_scratch;
     scatter_record(S, s, g.lv_rec + static_cast<u64>(s) * kRecBytes, g.cart.chr == nullptr, lane, 32);
     __syncwarp();
@@ -994,11 +1001,11 @@ __global__ void __launch_bounds__(32) k_boot(const __grid_constant__ GameArgs g,
                                              u32 boot_n, u32 idle_n, u8* recs, u32* fault_out) {
     extern __shared__ __align__(16) u8 smem_raw[];
     EmuShared& sh = *reinterpret_cast<EmuShared*>(smem_raw);
-    u32* dtab = reinterpret_cast<u32*>(smem_raw + sizeof(EmuShared));
+    u32* dtab = reinterpret_cast<u32*>(smem_raw + kDtabOff);
     u8* prg_s = smem_raw + kFramesSmem;
     const u32 lane = threadIdx.x;
     for (int i = lane; i < 256; i += 32) dtab[i] = kDecode.t[i];
-    stage_prg(g.cart, prg_s, lane);
+    stage_prg(g.cart, prg_s, lane, 32);
     __syncwarp();
     const bool me = lane == 0;
     if (me) {

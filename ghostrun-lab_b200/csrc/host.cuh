@@ -281,7 +281,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
         ck(cudaMemsetAsync(A.list_count, 0, 4, s), "list reset");
         if (!start) {
             T.begin(kKFrames, s);
-            k_frames<B><<<(n + kEnvsPerWarp - 1) / kEnvsPerWarp, 32, frames_smem(g.cart), s>>>(g, A, 0);
+            k_frames<B><<<frames_blocks(n), 32 * kFramesWarps, frames_smem(g.cart), s>>>(g, A, 0);
             T.end(kKFrames, s);
             check_launch("k_frames");
         }
@@ -309,7 +309,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     }
     if (!(phases & kPhRestart)) return;
     ck(cudaStreamWaitEvent(side, sd.fork, 0), "fork");
-    const u32 wb = (n + kEnvsPerWarp - 1) / kEnvsPerWarp;
+    const u32 wb = frames_blocks(n);
     if (g.lv_cap > 0 && g.lv_idle_n > 0) {   // idle chains of the slots that changed, before the restores use them
         T.begin(kKFinish, side);
         k_chain<B><<<g.lv_cap, 32, frames_smem(g.cart), side>>>(g);
@@ -326,9 +326,9 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
         T.end(kKFinish, side);
         check_launch("k_archive");
     }
-    const u32 rb = start ? wb : std::min<u32>(wb, 148u * (32u / kEnvsPerWarp));
+    const u32 rb = start ? wb : std::min<u32>(wb, std::max<u32>(148u, 148u * (32u / kEnvsPerWarp) / kFramesWarps));
     T.begin(kKRestart, side);
-    k_frames<B><<<rb, 32, frames_smem(g.cart), side>>>(g, A, 1);
+    k_frames<B><<<rb, 32 * kFramesWarps, frames_smem(g.cart), side>>>(g, A, 1);
     T.end(kKRestart, side);
     check_launch("k_frames restart");
     if (!A.no_render) {
