@@ -41,6 +41,17 @@ sys.path.insert(0, str(PKG))
 METRIC = 'decisions/s (4 NES frames each)'
 UNIT = 'decisions/s'
 GAME = 'synth00'
+
+
+def nrom_workload(envs) -> str:
+    """The workload name of the synthetic-NROM line at `envs` envs per GPU: BASELINE config 2 at 8,192, config 4's
+    per-GPU size at 65,536, else config 2's workload at that size."""
+    envs = int(envs or 8192)
+    if envs == 8192:
+        return 'config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on'
+    if envs == 65536:
+        return 'config 4 (per GPU): synthetic NROM, 65536 envs/GPU, 4 frames/decision, pack6 on'
+    return f'config 2 workload at {envs} envs/GPU: synthetic NROM, 4 frames/decision, pack6 on'
 PACKED_ROW = 4 * 224 * 240 // 4 * 3   # 161,280 bytes of packed pictures per decision
 EMPH_ROW = 4 * 224
 
@@ -724,7 +735,7 @@ def gpu_arm(args):
             ms_per_step=round(ms_max / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
             data='synthetic (seeded NROM cart synth00, random moves)' if not c3 else
                  'synthetic (12 seeded games synth00-11 on NROM/UxROM/MMC1/MMC3, random moves, half holding Right)',
-            config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on' if not c3 else
+            config=dict(workload=nrom_workload(E) if not c3 else
                         f'config 3: 12 synthetic games on 4 boards, {E} envs/GPU, 16 level-start slots per game, '
                         'P(level start)=1 with Dirichlet(1) weights, pack6 on',
                         level_slots_saved=lv_info, envs_per_gpu=E,
@@ -776,7 +787,7 @@ def main():
                     steps=r['steps'], warmup=args.warmup, ms_per_step=round(1e3 * r['seconds'] / r['steps'], 3),
                     higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
                     data='synthetic (seeded NROM cart synth00, random legal moves)',
-                    config=dict(workload='config 2: synthetic NROM, 8192 envs/GPU, 4 frames/decision, pack6 on',
+                    config=dict(workload=nrom_workload(args.envs),
                                 envs_per_gpu=args.envs, envs_timed=r['envs'], frames_per_decision=4),
                     cpu_baseline=dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
                                       sample=sample, cpu=cpu_model()),
