@@ -1306,7 +1306,7 @@ __device__ __forceinline__ u32 s0_tile_addr(const S0Ctx& c, u32 ctrl, u32 mirror
 }
 
 __device__ __forceinline__ void s0_mmc2_select(S0State& s, u32 half) {
-    const u32 bank = s.creg[2 * half + s.latch[half]];
+    const u32 bank = s.creg[(2 * half + (s.latch[half & 1u] & 1u)) & 3u];   // an index within the array always
     for (u32 i = 0; i < 4; ++i) s.chr[4 * half + i] = (bank * 4 + i) & 0xFFu;
 }
 __device__ __forceinline__ void s0_mmc2_hook(S0State& s, u32 addr) {
@@ -1469,6 +1469,9 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
     for (int i = 0; i < 8; ++i) s.lz_chr[i] = 0;
     s.blurp = 0; s.f_lo0 = s.f_hi0 = s.f_attr0 = s.f_x0 = 0;
     s.sphitx = 0x100u; s.sphitdata = 0; s.hit = 0; s.hit_x = 0;
+    s.latch[0] = s.latch[1] = 0;   // MMC2 fields: unused by this replay (MMC2 has its own), defined all the same
+    for (int i = 0; i < 4; ++i) s.creg[i] = 0;
+    for (int i = 0; i < 8; ++i) s.lz_chr33[i] = 0;
     while (s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < -16) s0_apply<BOARD>(s, ev, s.cursor++, false);
     if (s.mask & 0x18u) s.v = s.t;
     const int last = first + 15 < 239 ? first + 15 : 239;

@@ -304,7 +304,7 @@ struct Renderer {
     // in $0FD0-$0FEF / $1FD0-$1FEF puts that half on its $FD or $FE bank. Warp-uniform arguments.
     __device__ __forceinline__ void mmc2_select(u32 half) {
         __syncwarp();
-        if (lane < 4) W.chr[4 * half + lane] = (s.creg[2 * half + s.latch[half]] * 4 + lane) & 0xFFu;
+        if (lane < 4) W.chr[4 * (half & 1u) + lane] = (s.creg[(2 * half + (s.latch[half & 1u] & 1u)) & 3u] * 4 + lane) & 0xFFu;
         __syncwarp();
     }
     __device__ __forceinline__ void mmc2_hook(u32 addr) {
@@ -329,7 +329,7 @@ struct Renderer {
             return static_cast<u32>(W.nt[base | lf.row | col]);
         };
         auto nib = [&](u32 tile, u32 latch, u32 attr) {
-            const u32 bank = s.creg[2 * hb + latch];
+            const u32 bank = s.creg[(2 * hb + (latch & 1u)) & 3u];
             const u32 off = (((bank * 4u + (tile >> 6)) & A.cart.chr_page_mask) << 10) | ((tile & 63u) << 4) | fy;
             return spread[__ldg(A.cart.chr + off)] | (spread[__ldg(A.cart.chr + off + 8u)] << 1) | (attr * 0x44444444u);
         };
