@@ -157,8 +157,9 @@ __device__ __forceinline__ u32 v_after_lines(u32 v, u32 k, u32 th, bool ren) {
 struct Hit0 { u32 dot; bool hit; };
 
 // Consoles per warp in the emulation kernels: lanes 0..kEnvsPerWarp-1 each run one console, the others idle. Fewer
-// consoles per warp mean fewer distinct program counters per min-PC round and a smaller shared-memory footprint, so
-// more warps are resident to hide the interpreter's dependent-instruction latency.
+// consoles per warp mean fewer distinct program counters per min-PC round and more warps, but each warp runs the
+// whole interpreter body per round: measured, 2 warps x 16 beat 1 x 32 by 3-6% on NROM / UxROM / MMC1 and lost 5% on
+// MMC3; 8 x 4 and 4 x 8 lost everywhere. A board unit sets both before including this header (board_*.cu).
 #ifndef GR_ENVS_PER_WARP
 #define GR_ENVS_PER_WARP 32
 #endif
