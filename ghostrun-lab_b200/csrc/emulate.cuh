@@ -1551,24 +1551,31 @@ __device__ __noinline__ Hit0 sprite0_hit(const S0Ctx c) {
 // ------------------------------------------------------------------------------------------------ MMC2 latches
 // MMC2's latches move with every pattern fetch the frame makes, so its sprite-0 replay and the vblank resolve
 // (patch:1791-1815 frame_resolve_mmc2) follow the frame's fetch order. An event-free line's 34 background fetches all
-// use one pattern table, so they can only move that half's latch, and only by a $FD or $FE tile number: their effect
-// is the last such tile among fetches 0-31, 32 and 33, worked out once per run of lines with the same first fetch
-// address, table and page map (the nametable does not change during the replay).
+// use one pattern table, so they can only move that half's latch, and only by a $FD or $FE tile number: the latch a
+// fetch sees is the last such tile before it, else the one the line started with. The positions of those tiles are
+// worked out once per run of lines with the same first fetch address, table and page map (the nametable does not
+// change during the replay).
 
-struct Mmc2Row { u32 key, o31, o32, o33; };   // flips: 0 none, 1 $FD, 2 $FE
+struct Mmc2Row { u32 key; u64 flips, fe; };   // bit k: fetch k reads a $FD / $FE tile; fe: which of them are $FE
 
 template <u32 BOARD>
 __device__ __forceinline__ void mmc2_row(const S0Ctx& c, const S0State& s, Mmc2Row& r) {
     const u32 key = 0x80000000u | (s.v & 0x0FFFu) | ((s.ctrl & 0x10u) << 8) | ((s.mirroring & 0xFFu) << 13);
     if (key == r.key) return;
     r.key = key;
-    r.o31 = r.o32 = r.o33 = 0;
+    r.flips = r.fe = 0;
     for (u32 k = 0; k < 34; ++k) {
         const u32 vv = v_inc_x_n(s.v, k);
         const u32 tile = c.nt[nt_off_map(s.mirroring, 0x2000u | (vv & 0x0FFFu))];
-        const u32 f = (tile == 0xFDu || tile == 0xFEu) ? tile - 0xFCu : 0u;
-        if (f) { if (k < 32) r.o31 = f; else if (k == 32) r.o32 = f; else r.o33 = f; }
+        if (tile == 0xFDu || tile == 0xFEu) r.flips |= 1ull << k;
+        if (tile == 0xFEu) r.fe |= 1ull << k;
     }
+}
+
+// The background half's latch that fetch k of the row sees (lin: the latch the line started with).
+__device__ __forceinline__ u32 mmc2_latch_before(const Mmc2Row& r, u32 k, u32 lin) {
+    const u64 m = r.flips & ((1ull << k) - 1ull);
+    return m ? static_cast<u32>((r.fe >> (63 - __clzll(static_cast<long long>(m)))) & 1ull) : lin;
 }
 
 // An event-free line drawn with rendering on: its latch moves and the lazy shift-register record (fetch 32 through
@@ -1577,8 +1584,9 @@ template <u32 BOARD>
 __device__ __forceinline__ void mmc2_plain_line(const S0Ctx& c, S0State& s, Mmc2Row& row, bool keep_lazy) {
     mmc2_row<BOARD>(c, s, row);
     const u32 bg = (s.ctrl >> 4) & 1u;
-    const u32 l32 = row.o31 ? row.o31 - 1u : s.latch[bg];
-    const u32 l33 = row.o32 ? row.o32 - 1u : l32;
+    const u32 lin = s.latch[bg];
+    const u32 l32 = mmc2_latch_before(row, 32, lin);
+    const u32 l33 = mmc2_latch_before(row, 33, lin);
     if (keep_lazy) {
         s.lazy = 1; s.lz_v = s.v; s.lz_ctrl = s.ctrl; s.lz_mirroring = s.mirroring;
         s.latch[bg] = l32; s0_mmc2_select(s, bg);
@@ -1586,9 +1594,35 @@ __device__ __forceinline__ void mmc2_plain_line(const S0Ctx& c, S0State& s, Mmc2
         s.latch[bg] = l33; s0_mmc2_select(s, bg);
         for (int i = 0; i < 8; ++i) s.lz_chr33[i] = s.chr[i];
     }
-    s.latch[bg] = row.o33 ? row.o33 - 1u : l33;
+    s.latch[bg] = mmc2_latch_before(row, 34, lin);
     s0_mmc2_select(s, bg);
     s.v = v_inc_y(v_inc_x_n(s.v, 34));
+}
+
+// Sprite-0 check on an event-free line drawn with rendering on (before mmc2_plain_line steps it): the (at most) two
+// background tiles under pixels sphitx..sphitx+7, each through the pages its fetch saw.
+template <u32 BOARD>
+__device__ __forceinline__ void mmc2_plain_hit(const S0Ctx& c, S0State& s, Mmc2Row& row) {
+    if (s.sphitx == 0x100u || !(s.mask & 0x08u)) return;
+    mmc2_row<BOARD>(c, s, row);
+    const u32 bg = (s.ctrl >> 4) & 1u, lin = s.latch[bg];
+    const u32 sx = s.sphitx;
+    const u32 q = sx + s.x, j0 = q >> 3, r = q & 7u;
+    u32 pages[8];
+    auto fetch_at = [&](u32 k) {
+        const u32 bank = s.creg[(2 * bg + mmc2_latch_before(row, k, lin)) & 3u];
+        for (u32 i = 0; i < 8; ++i) pages[i] = s.chr[i];
+        for (u32 i = 0; i < 4; ++i) pages[4 * bg + i] = (bank * 4 + i) & 0xFFu;
+        return s0_fetch<BOARD>(c, s.ctrl, pages, s.mirroring, v_inc_x_n(s.v, k));
+    };
+    const u32 fa = fetch_at(j0);
+    const u32 fb = r ? fetch_at(j0 + 1) : 0u;
+    const u32 o16 = (((fa | (fa >> 8)) & 0xFFu) << 8) | ((fb | (fb >> 8)) & 0xFFu);
+    u32 win = (o16 >> (8 - r)) & 0xFFu;                          // bit 7 - k: pixel sx + k opaque
+    if (sx < 8 && !(s.mask & 0x02u)) win &= (1u << sx) - 1u;     // left 8 pixels hidden
+    if (sx + 8 > 255) win &= (0xFF00u >> (255 - sx)) & 0xFFu;
+    const u32 hits = win & s.sphitdata;
+    if (hits) { s.hit = 1; s.hit_x = sx + (__clz(hits) - 24); s.sphitx = 0x100u; }
 }
 
 // FetchSpriteData at the end of line l with rendering on: every sprite in range (at most 8, OAM order) goes through
@@ -1670,8 +1704,9 @@ __device__ __forceinline__ void mmc2_end_of_line(const S0Ctx& c, S0State& s, int
     }
 }
 
-// MMC2's sprite-0 hit (patch:1740-1789 with the MMC2 fetch rules): lines above sprite 0 move only the latches and
-// the address; from the line before sprite 0 on, every line is replayed tile by tile.
+// MMC2's sprite-0 hit (patch:1740-1789 with the MMC2 fetch rules): an event-free line moves the latches and the
+// address and, from sprite 0's first line on, checks the two tiles under sprite 0 through the pages their fetches
+// saw; a line with a write inside its drawn part is replayed tile by tile.
 template <u32 BOARD>
 __device__ __noinline__ Hit0 sprite0_hit_mmc2(const S0Ctx c) {
     const int kook = (c.bank[15] & kLogKook) ? 1 : 0;
@@ -1688,8 +1723,12 @@ __device__ __noinline__ Hit0 sprite0_hit_mmc2(const S0Ctx c) {
         const int start = l * 341 - 16;
         const u32 sphitx0 = s.sphitx;
         const bool event_line = s.cursor < c.count && fceumm_time(ev[2 * s.cursor] & 0x1FFFFu, kook) < start + 272;
-        if (event_line || l >= first - 1) s0_event_line<BOARD>(c, s, kook, l, l >= first);
-        else if (s.mask & 0x18u) mmc2_plain_line<BOARD>(c, s, row, true);
+        if (event_line) {
+            s0_event_line<BOARD>(c, s, kook, l, l >= first);
+        } else if (s.mask & 0x18u) {
+            if (l >= first) mmc2_plain_hit<BOARD>(c, s, row);
+            mmc2_plain_line<BOARD>(c, s, row, true);
+        }
         if (s.hit) return s0_hit_at(l, s.hit_x, sphitx0);
         mmc2_end_of_line<BOARD>(c, s, kook, l, vis);
     }
