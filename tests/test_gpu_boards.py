@@ -19,3 +19,36 @@ def test_parity_paged_board(game, oracle_path, gpu_lib_path):
 def test_parity_mixed_boards(oracle_path, gpu_lib_path):
     counts = {'synth00': 8, 'synth01': 8, 'synth02': 8, 'synth03': 8, 'synth12': 8, 'synth13': 8}
     run_parity(counts, oracle_path, gpu_lib_path, steps=200, dump_every=40)
+
+
+@pytest.mark.gpu
+def test_save_load_exact_resume_latched_boards(gpu_lib_path):
+    """rlenv_save / rlenv_load (rl/csrc/rlenv.cu:270-298) carry CNROM's bank latch and MMC2's registers and $FD/$FE
+    latches: a fresh env (another seed) loaded with the state continues with the same outputs."""
+    import torch
+    from rlenv import RlEnv
+    from actions import random_legal
+    counts = {'synth12': 12, 'synth13': 12}
+    kw = dict(sticky=True, idle_max=30, dropout=True, lib_path=gpu_lib_path)
+    a = RlEnv(counts, device='cuda', seed=8, **kw)
+    a.start()
+    gen = torch.Generator().manual_seed(8)
+    for _ in range(70):   # past the MMC2 cart's first mid-frame register write (frame 64)
+        a.actions.copy_(random_legal(a.masks.cpu(), gen).cuda())
+        a.step()
+    sd = a.state_dict()
+    acts, rec = [], []
+    for t in range(40):
+        acts.append(random_legal(a.masks.cpu(), gen).cuda())
+        a.actions.copy_(acts[t])
+        a.step()
+        rec.append({k: getattr(a, k).clone() for k in ('obs', 'emph', 'reward', 'done', 'masks', 'pads', 'events')})
+    b = RlEnv(counts, device='cuda', seed=99, **kw)
+    b.start()
+    b.load_state_dict(sd)
+    for t in range(40):
+        b.actions.copy_(acts[t])
+        b.step()
+        torch.cuda.synchronize()
+        for k, v in rec[t].items():
+            assert torch.equal(getattr(b, k), v), f'resumed step {t}: {k} differs'
