@@ -158,8 +158,9 @@ struct Hit0 { u32 dot; bool hit; };
 
 // Consoles per warp in the emulation kernels: lanes 0..kEnvsPerWarp-1 each run one console, the others idle. Fewer
 // consoles per warp mean fewer distinct program counters per min-PC round and more warps, but each warp runs the
-// whole interpreter body per round: measured, 2 warps x 16 beat 1 x 32 by 3-6% on NROM / UxROM / MMC1 and lost 5% on
-// MMC3; 8 x 4 and 4 x 8 lost everywhere. A board unit sets both before including this header (board_*.cu).
+// whole interpreter body per round: measured, 2 warps x 16 beat 1 x 32 by 3-6% on NROM / UxROM / MMC1 run alone but
+// lost 5% on MMC3 and on the mixed config-3 run; 8 x 4 and 4 x 8 lost everywhere. A board unit may set both before
+// including this header (board_nrom.cu does).
 #ifndef GR_ENVS_PER_WARP
 #define GR_ENVS_PER_WARP 32
 #endif
