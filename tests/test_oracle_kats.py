@@ -23,3 +23,17 @@ def test_oracle_passes_the_reference_known_answer_tests(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all known-answer checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_mmc2_follows_the_reference_board(tmp_path):
+    """MMC2 in the oracle against the patch's board code (registers, pages, latch hook ranges and their order
+    around the $2007 buffer, frame-log events, the replay's fetch hook): tests/kat/oracle_mmc2.cpp."""
+    exe = tmp_path / 'oracle_mmc2'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_mmc2.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all MMC2 checks passed' in run.stdout
