@@ -37,3 +37,17 @@ def test_oracle_mmc2_follows_the_reference_board(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all MMC2 checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_paged_boards_follow_the_reference(tmp_path):
+    """MMC1's serial port and modes, CNROM's latch, MMC3's revision-B counter and its clock timing in the oracle
+    against the patch's board code: tests/kat/oracle_boards.cpp."""
+    exe = tmp_path / 'oracle_boards'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_boards.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all board checks passed' in run.stdout
