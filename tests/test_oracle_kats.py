@@ -51,3 +51,17 @@ def test_oracle_paged_boards_follow_the_reference(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all board checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_frame_log_follows_the_reference(tmp_path):
+    """The frame log in the oracle against the patch's recording code (event encoding, the $2007 merge with rendering
+    off, vblank, overflow, cycle stamps, FCEUmm's time base, the emphasis tint): tests/kat/oracle_framelog.cpp."""
+    exe = tmp_path / 'oracle_framelog'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_framelog.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all frame-log checks passed' in run.stdout
