@@ -65,3 +65,17 @@ def test_oracle_frame_log_follows_the_reference(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all frame-log checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_ppu_timing_follows_the_reference(tmp_path):
+    """The PPU's timing events (vblank flag, NMI, status clear, log freeze / capture, sprite-0 scheduling) and the
+    sprite-0 hit dot in the oracle against the patch's step code: tests/kat/oracle_ppu.cpp."""
+    exe = tmp_path / 'oracle_ppu'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_ppu.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all PPU timing checks passed' in run.stdout
