@@ -79,3 +79,18 @@ def test_oracle_ppu_timing_follows_the_reference(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all PPU timing checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_6502_follows_the_published_2a03(tmp_path):
+    """The oracle's 6502 core against the NES 2A03's published behaviour (binary-only ADC / SBC, flags, cycle counts
+    and penalties, stack, JMP ($xxFF), zero-page wraps, BRK / RTI, unofficial opcodes faulting): NeSLE's core is not
+    vendored, so this stands in for it. tests/kat/oracle_6502.cpp."""
+    exe = tmp_path / 'oracle_6502'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_6502.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all 6502 checks passed' in run.stdout
