@@ -94,3 +94,18 @@ def test_oracle_6502_follows_the_published_2a03(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
     assert 'all 6502 checks passed' in run.stdout
+
+
+@pytest.mark.skipif(shutil.which('g++') is None, reason='needs g++')
+def test_oracle_bus_follows_the_published_nes(tmp_path):
+    """The oracle's CPU bus against the NES's published register behaviour ($2002, the $2005 / $2006 toggle, the
+    $2007 read buffer and palette reads, v steps, palette mirrors, the controller port, OAM DMA timing, nametable
+    mirroring): NeSLE's base bus is not vendored, so this stands in for it. tests/kat/oracle_bus.cpp."""
+    exe = tmp_path / 'oracle_bus'
+    build = subprocess.run(['g++', '-std=c++17', '-O1', '-ffp-contract=off', '-I', str(ROOT / 'oracle'),
+                            str(ROOT / 'tests' / 'kat' / 'oracle_bus.cpp'), '-o', str(exe)],
+                           capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-1000:]
+    assert 'all bus checks passed' in run.stdout
