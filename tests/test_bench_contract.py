@@ -43,3 +43,16 @@ def test_workload_names_follow_the_env_count():
     assert b.nrom_workload(None).startswith('config 2: synthetic NROM, 8192 envs/GPU')
     assert b.nrom_workload(65536).startswith('config 4 (per GPU)')
     assert '2048 envs/GPU' in b.nrom_workload(2048)
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Under torchrun only rank 0 runs the reference arm and prints; the other ranks exit 0 without work."""
+    r = subprocess.run([sys.executable, '-m', 'torch.distributed.run', '--nnodes=1', '--nproc-per-node', '2',
+                        '--master-addr', '127.0.0.1', '--master-port', '29533', str(ROOT / 'bench.py'),
+                        '--impl', 'reference', '--gpus', '2', '--steps', '1', '--warmup', '1'],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith('{')]
+    assert len(lines) == 1, r.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d['impl'] == 'reference' and d['n_gpus'] == 2 and d['value'] > 0
