@@ -161,6 +161,7 @@ MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'cnrom': 3, 'mmc3': 4, 'mmc2': 9}
 # zero page / RAM map of the template (the synthetic reward reader reads these)
 ZP_BUTTONS, ZP_TMP, ZP_LFSR, ZP_FRAME = 0x00, 0x01, 0x02, 0x04
 ZP_PTR = 0x06
+ZP_DMC = 0x08   # the DMC variant keeps each frame's $4015 read here
 ZP_PROGRESS, ZP_LEVEL, ZP_LIVES, ZP_SCORE, ZP_MODE = 0x10, 0x12, 0x13, 0x14, 0x17
 OAM_BUF = 0x0200
 
@@ -174,8 +175,8 @@ class Cart:
     params: dict          # the seed-derived template constants
 
 
-def _template(a: Asm, p: dict, board: str, data_labels: dict):
-    """The reset/NMI/IRQ program (see the module docstring)."""
+def _template(a: Asm, p: dict, board: str, data_labels: dict, dmc: bool = False):
+    """The reset/NMI/IRQ program (see the module docstring); `dmc`: the NMI also plays a DMC sample."""
     i = a.i
     # ---------------------------------------------------------------- reset
     a.label('reset')
@@ -245,6 +246,16 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict):
     i('PHA'); i('TXA'); i('PHA'); i('TYA'); i('PHA')
     i('LDA', 'imm', 0); i('STA', 'abs', 0x2003); i('LDA', 'imm', OAM_BUF >> 8); i('STA', 'abs', 0x4014)
     i('BIT', 'abs', 0x2002)
+    if dmc:
+        # a 17-byte sample at rate 15, looped on odd frames, (re)started by $4015 bit 4 each frame; the status byte
+        # goes to RAM. Its fetches steal CPU cycles from the instructions that run while it plays.
+        i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 1)
+        for _ in range(6):
+            i('ASL', 'acc')
+        i('ORA', 'imm', 0x0F); i('STA', 'abs', 0x4010)
+        i('LDA', 'imm', 0x01); i('STA', 'abs', 0x4013)
+        i('LDA', 'imm', 0x1F); i('STA', 'abs', 0x4015)
+        i('LDA', 'abs', 0x4015); i('STA', 'zp', ZP_DMC)
     if board == 'mmc2':
         # latch 0 <- $FD / $FE by frame bit 0, latch 1 by frame bit 1: $2006 puts the address on the bus, a $2007 read
         # puts it there again (and its successor)
@@ -408,8 +419,9 @@ def template_params(seed: int, board: str) -> dict:
     return p
 
 
-def make_cart(seed: int, board: str = 'nrom') -> Cart:
-    """A seeded synthetic cartridge (iNES image + boot pads)."""
+def make_cart(seed: int, board: str = 'nrom', dmc: bool = False) -> Cart:
+    """A seeded synthetic cartridge (iNES image + boot pads); `dmc`: a variant whose NMI plays a DMC sample every
+    frame (the registered games never do; tests use it for the sample channel and its cycle steals)."""
     assert board in MAPPERS, board
     p = template_params(seed, board)
     r = np.random.default_rng([seed, 0xC0DE])
@@ -433,7 +445,7 @@ def make_cart(seed: int, board: str = 'nrom') -> Cart:
         data['chrtab'] = chr_bytes
     # program in the last 16 KB (fixed bank on every board), vectors at $FFFA
     a = Asm(0xC000)
-    _template(a, p, board, data)
+    _template(a, p, board, data, dmc)
     img = a.assemble()
     assert max(img) < 0xFFFA, 'program overflows into the vectors'
     prg = bytearray(r.integers(0, 256, prg_size, dtype=np.uint8).tobytes())

@@ -52,3 +52,33 @@ def test_save_load_exact_resume_latched_boards(gpu_lib_path):
         torch.cuda.synchronize()
         for k, v in rec[t].items():
             assert torch.equal(getattr(b, k), v), f'resumed step {t}: {k} differs'
+
+
+@pytest.mark.gpu
+def test_parity_dmc_sample_channel(oracle_path, gpu_lib_path):
+    """The DMC sample channel on the GPU against the oracle (patch:405-567; the oracle's DMC is pinned by the
+    reference's own known-answer tests): the NROM cart's DMC variant starts a sample every frame (looped on odd frames)
+    and keeps $4015 in RAM; every output each decision, and the machine dumps (CPU cycle counter, the DMC's state,
+    RAM) every 10 decisions, match."""
+    import torch
+    import synth
+    from rlenv import RlEnv
+    from actions import random_legal
+    from test_gpu_parity import _compare, _compare_dumps
+    rom = synth.make_cart(1000, 'nrom', dmc=True).rom
+    kw = dict(seed=6, sticky=True, idle_max=30, dropout=True, roms={'synth00': rom})
+    g = RlEnv({'synth00': 24}, device='cuda', lib_path=gpu_lib_path, **kw)
+    c = RlEnv({'synth00': 24}, device='cpu', lib_path=oracle_path, **kw)
+    g.start(); c.start()
+    gen = torch.Generator().manual_seed(6)
+    for t in range(61):
+        torch.cuda.synchronize()
+        _compare(g, c, t)
+        if t % 10 == 0:
+            _compare_dumps(g, c, [0, 11, 23], t)
+            assert c.dump(0)[64 + synth.ZP_DMC] & 0x10, 'the sample should be playing when $4015 is read'
+        if t == 60:
+            break
+        act = random_legal(c.masks, gen)
+        c.actions.copy_(act); g.actions.copy_(act.cuda())
+        c.step(); g.step()
