@@ -7,6 +7,10 @@
 //   * MMC3's counter, revision B (reload when zero or asked, else decrement; the IRQ line when zero and enabled;
 //     $E000 disables and acknowledges): patch:3148-3175, and when it is clocked: dot 266 of each visible line and 256
 //     of the pre-render line, while background or sprites are on, unless (ctrl & 0x38) == 0x18: patch:1861-1931.
+//   * UxROM (NeSLE's base, not vendored; the published board): the 16 KB bank at $8000 picked by a write, the last
+//     16 KB fixed at $C000,
+//   * the cold reset: PC from the reset vector, SP $FD, I set, 7 cycles (the published 6502 reset sequence), RAM $FF
+//     (rl/csrc/rlenv_build.hpp:86).
 // Built and run by tests/test_oracle_kats.py; prints one line per failed check and exits non-zero on any.
 #include <cstdio>
 #include <vector>
@@ -123,9 +127,42 @@ void mmc3_clock_timing() {
           dots_to_mmc3_clock(239 * kDots + 266) == 22 * kDots - 10);
 }
 
+void uxrom() {
+    Cart c;
+    c.board = kUxrom;
+    c.arrangement = 0;
+    c.prg.resize(128 * 1024);
+    for (std::size_t i = 0; i < c.prg.size(); ++i) c.prg[i] = static_cast<u8>(i >> 14);   // byte = its 16 KB bank
+    c.chr.assign(8192, 0);
+    c.bank_mask = 7;
+    c.fixed_base = 128 * 1024 - 16384;
+    Console m{};
+    cpu_write(c, m, 0x8000, 5);
+    CHECK(cpu_read(c, m, 0x8123) == 5 && cpu_read(c, m, 0xBFFF) == 5 && cpu_read(c, m, 0xC000) == 7);
+    cpu_write(c, m, 0xFFF0, 0x0B);                  // the bank number keeps the mask's bits
+    CHECK(cpu_read(c, m, 0x9000) == 3 && cpu_read(c, m, 0xFFFF) == 7);
+}
+
+void cold_reset_state() {
+    Cart c;
+    c.board = kNrom;
+    c.arrangement = 0;
+    c.prg.assign(32768, 0);
+    c.prg[0x7FFC] = 0x34; c.prg[0x7FFD] = 0x92;    // reset vector $9234
+    c.chr.assign(8192, 0);
+    Console m;
+    cold_reset(c, m);
+    CHECK(m.pc == 0x9234 && m.sp == 0xFD && (m.p & FI) && m.p == 0x24 && m.cycles == 7);
+    bool ram_ff = true;
+    for (u8 b : m.ram) ram_ff = ram_ff && b == 0xFF;
+    CHECK(ram_ff && m.frame_dot == 0);
+}
+
 }  // namespace
 
 int main() {
+    uxrom();
+    cold_reset_state();
     mmc1();
     cnrom();
     mmc3_counter();
