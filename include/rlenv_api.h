@@ -14,7 +14,7 @@ extern "C" {
 
 // ---------------------------------------------------------------- lifecycle (rl/csrc/rlenv_api.h:9-12, 43-46)
 
-// rl/csrc/rlenv_api.h:9-11. game_ids: rl10 game ids (0..11 the reference's commercial games, 12..23 the seeded
+// rl/csrc/rlenv_api.h:9-11. game_ids: rl10 game ids (0..11 the reference's commercial games, 12..25 the seeded
 // synthetic games of ghostrun-lab_b200/synth.py; a game needs its reward spec registered first, rl10_register_game).
 // roms: iNES images (mappers 0 NROM, 1 MMC1, 2 UxROM, 3 CNROM, 4 MMC3, 9 MMC2); boot_pads: pad byte of every frame from power-on to
 // the boot snapshot; n_envs: envs per game. sticky / dropout: 0/1; idle_max: 0..idle_max random idle frames at
