@@ -3,7 +3,7 @@
     python ghostrun-lab_b200/build.py [--force]
 
 The library lands next to this file (ghostrun-lab_b200/librlenv_b200.so) so it travels with the repository
-snapshot; it is rebuilt when a source under csrc/ is newer than it.
+snapshot; it is rebuilt when a source under csrc/ or a header under include/ is newer than it.
 """
 from __future__ import annotations
 
@@ -15,6 +15,7 @@ import sys
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
+INCLUDE = HERE.parent / 'include'   # the C-ABI header the definitions are compiled against
 OUT = HERE / 'librlenv_b200.so'
 BUILD = HERE / '_build'
 UNITS = ['rlenv_b200.cu', 'board_nrom.cu', 'board_uxrom.cu', 'board_mmc1.cu', 'board_mmc3.cu', 'board_cnrom.cu', 'board_mmc2.cu', 'stem.cu']
@@ -27,7 +28,7 @@ def stale() -> bool:
     if not OUT.exists():
         return True
     t = OUT.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in CSRC.iterdir())
+    return any(p.stat().st_mtime > t for p in [*CSRC.iterdir(), *INCLUDE.glob('*.h')])
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:

@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "host.cuh"
+#include "../../include/rlenv_api.h"   // the definitions below are compiled against the C-ABI declarations
 
 using namespace gr;
 
@@ -666,6 +667,8 @@ int rlenv_env_scalars(void* h, int ge, std::uint64_t* out, void* stream) {
 namespace {
 
 constexpr int kNoAllocMaxEnvs = 8;                 // RLENV_DUMP_NOALLOC_MAX_ENVS
+static_assert(kNoAllocMaxEnvs == RLENV_DUMP_NOALLOC_MAX_ENVS && kDumpBytes == RLENV_DUMP_BYTES,
+              "include/rlenv_api.h sizes");
 constexpr int kNoAllocMaxDevices = 64;
 // 8 x 23,040 B = 184,320 B. Every GPU that loads this library holds it until the process exits. Records start
 // 256-byte aligned (23,040 = 90 x 256).

@@ -27,6 +27,7 @@
 
 #include <cstdint>
 #include <string>
+#include "../../include/rlenv_api.h"   // rl_stem_* compiled against their C-ABI declarations
 
 namespace {
 
