@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "env.hpp"
+#include "../include/rlenv_api.h"   // the entry points below are compiled against the C-ABI declarations
 
 using namespace orc;
 
