@@ -115,10 +115,9 @@ def cpu_leg(args):
         steps = K
     else:
         steps = int(max(2, min(200, args.cpu_seconds / max(one, 1e-6))))
-    acts = [random_legal(env.masks, gen) for _ in range(4)]
     t0 = time.perf_counter()
-    for t in range(steps):
-        env.actions.copy_(acts[t % 4]); env.step()
+    for t in range(steps):   # every decision's moves drawn from its masks (the sampler's time is part of the step)
+        env.actions.copy_(random_legal(env.masks, gen)); env.step()
     dt = time.perf_counter() - t0
     cores = int(os.environ.get('OMP_NUM_THREADS', os.cpu_count()))
     print(json.dumps(dict(value=steps * E / dt, steps=steps, seconds=dt, cores=cores, envs=E)))
@@ -263,6 +262,21 @@ def render_traffic_per_env_frame():
     return None
 
 
+def random_words(shape, gen, dev):
+    """int32 random bits for RlEnv.legal_moves (one word per env and decision), drawn on `dev`."""
+    import torch
+    return torch.randint(-2 ** 31, 2 ** 31, shape, generator=gen, device=dev, dtype=torch.int64).to(torch.int32)
+
+
+def workload_config(args, world):
+    """The `config` both arms report for the NROM workloads (the driver compares the two arms' configs)."""
+    return dict(workload=nrom_workload(args.envs), envs_per_gpu=args.envs, frames_per_decision=4,
+                moves='each decision: every move part uniform among the choices the last masks allow '
+                      '(rl/actions.py random_legal)',
+                sticky=True, dropout=True, idle_max=30, pack6=True, parallelism=f'dp{world}',
+                inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)')
+
+
 def rank_seed_for_stem(seed):
     from shard import rank_seed
     return rank_seed(seed, 0)
@@ -320,7 +334,7 @@ def stem_arm(args):
     env.bind_obs_pack6(env_px)
     env.start()
     for _ in range(64):
-        env.actions.copy_(torch.randint(0, 81, (B,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        env.legal_moves(random_words((B,), g, dev))
         env.step()
     env_emph = env.emph.clone()
     del env
@@ -411,7 +425,7 @@ def config5_arm(args):
     env.start()
     g = torch.Generator(device=dev).manual_seed(args.seed + rank)
     for _ in range(args.age):   # spread the first episodes' ends to the steady-state restart rate
-        env.actions.copy_(torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16))
+        env.legal_moves(random_words((E,), g, dev))
         env.step()
     torch.manual_seed(args.seed)
     palette = torch.rand(512, 3, generator=torch.Generator().manual_seed(args.seed))   # a seeded stand-in colour table
@@ -490,12 +504,12 @@ def config5_arm(args):
     rollout(1, 0, True)   # warm the copy path
     ms_e2e = timed(lambda: rollout(K, 0, True))
 
-    # the two halves alone, same process: the env with random moves, the policy on all envs as one unit
-    acts = torch.randint(0, 81, (K, E), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+    # the two halves alone, same process: the env with random legal moves, the policy on all envs as one unit
+    words = random_words((K, E), g, dev)
 
     def env_only():
         for t in range(K):
-            env.actions.copy_(acts[t])
+            env.legal_moves(words[t])
             env.step()
 
     def policy_only():
@@ -575,10 +589,11 @@ def gpu_arm(args):
     packed = [torch.empty(E * PACKED_ROW, dtype=torch.uint8, device=dev) for _ in range(2)]
     env.bind_obs_pack6(packed[0])
     env.start()
-    # actions: uniform over the moves without Start/Select, drawn on the device up front (the env checks nothing)
+    # moves: each decision, every move part uniform among the choices the last masks allow (the reference sampler's
+    # distribution), drawn on the device by the library's sampler kernel from random words made up front
     g = torch.Generator(device=dev).manual_seed(args.seed + rank)
     K, W = args.steps, args.warmup
-    acts_dev = torch.randint(0, 81, (K + W, E), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
+    words_dev = random_words((K + W, E), g, dev)
     counters = EpisodeCounters(dev)
 
     def account():
@@ -586,14 +601,15 @@ def gpu_arm(args):
 
     stream = torch.cuda.current_stream(dev)
     # every env starts its first episode at once; aging spreads the episode ends to the steady-state restart rate
-    right = torch.full((E,), 3, dtype=torch.int16, device=dev)
+    right = torch.full((E,), 3, dtype=torch.int16, device=dev)   # d-pad choice 3 (Right), nothing else pressed
     for t in range(args.age):
-        a = torch.randint(0, 81, (E,), generator=g, device=dev, dtype=torch.int32).to(torch.int16)
-        if c3:   # level-entrance slots fill by play: every env holds Right first, half of them throughout
+        env.legal_moves(random_words((E,), g, dev))
+        if c3:   # level-entrance slots fill by play: every env holds Right first (where its mask allows), half of
+            # them throughout
             if t == 20:
                 env.set_level_prob(1.0)
-            a = torch.where((torch.arange(E, device=dev) % 2 == 0) | (t < args.age // 2), right, a)
-        env.actions.copy_(a)
+            hold = ((torch.arange(E, device=dev) % 2 == 0) | (t < args.age // 2)) & (env.masks[:, 3] != 0)
+            env.actions.copy_(torch.where(hold, right, env.actions))
         env.step()
     lv_info = None
     if c3:   # every new episode starts from a saved slot, Dirichlet(1) weights over each game's saved slots
@@ -609,7 +625,7 @@ def gpu_arm(args):
         lv_info = {gname: len(v) for gname, v in saved.items()}
     counters.attach(env)   # the finishing kernel adds the counters from here on (account() is then a no-op)
     for t in range(W):
-        env.actions.copy_(acts_dev[t]); env.step(); account()
+        env.legal_moves(words_dev[t]); env.step(); account()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -626,7 +642,7 @@ def gpu_arm(args):
     with clk:
         ev0.record(stream)
         for t in range(K):
-            env.actions.copy_(acts_dev[W + t])
+            env.legal_moves(words_dev[W + t])
             env.step()
             account()
             if (t + 1) % 128 == 0:
@@ -648,7 +664,7 @@ def gpu_arm(args):
     env.set_timing(True)
     env.timing(reset=True)
     for t in range(K):
-        env.actions.copy_(acts_dev[W + t])
+        env.legal_moves(words_dev[W + t])
         env.step()
         account()
         if (t + 1) % 128 == 0:
@@ -660,7 +676,8 @@ def gpu_arm(args):
 
     # ---- e2e: public API with host buffers (pinned), copies overlapped on a copy stream
     R = max(2, args.ring)
-    host_acts = torch.randint(0, 81, (K, E), dtype=torch.int16).pin_memory()
+    host_words = random_words((K, E), torch.Generator().manual_seed(args.seed + 7919 * rank), 'cpu').pin_memory()
+    words_buf = torch.empty(E, dtype=torch.int32, device=dev)
     ring = torch.empty((R, E * (PACKED_ROW + EMPH_ROW)), dtype=torch.uint8).pin_memory()
     small = torch.empty((R, E * (4 + 1 + 19)), dtype=torch.uint8).pin_memory()
     copy = torch.cuda.Stream(dev)
@@ -678,8 +695,9 @@ def gpu_arm(args):
         stream.wait_event(done_ev[b]) if t >= 2 else None   # the copy of this buffer two steps ago finished
         env.bind_obs_pack6(packed[b])
         env.bind_obs(env.obs, emph_buf[b].view(E, 4, 224))
-        env.actions.copy_(host_acts[t], non_blocking=True)
-        h2d += E * 2
+        words_buf.copy_(host_words[t], non_blocking=True)   # the decision's random bits, host -> device
+        h2d += E * 4
+        env.legal_moves(words_buf)
         env.step()
         account()
         if (t + 1) % 128 == 0:
@@ -733,15 +751,15 @@ def gpu_arm(args):
         result = dict(
             metric=METRIC, value=round(value, 1), unit=UNIT, n_gpus=world, steps=K, warmup=W,
             ms_per_step=round(ms_max / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
-            data='synthetic (seeded NROM cart synth00, random moves)' if not c3 else
-                 'synthetic (12 seeded games synth00-11 on NROM/UxROM/MMC1/MMC3, random moves, half holding Right)',
-            config=dict(workload=nrom_workload(E) if not c3 else
-                        f'config 3: 12 synthetic games on 4 boards, {E} envs/GPU, 16 level-start slots per game, '
-                        'P(level start)=1 with Dirichlet(1) weights, pack6 on',
-                        level_slots_saved=lv_info, envs_per_gpu=E,
-                        frames_per_decision=4, parallelism=f'dp{world} (env shards, NCCL all-reduce of counters)',
-                        aged_decisions=args.age,
+            data='synthetic (seeded NROM cart synth00, random legal moves)' if not c3 else
+                 'synthetic (12 seeded games synth00-11 on NROM/UxROM/MMC1/MMC3, random legal moves, half holding '
+                 'Right while aging)',
+            config=workload_config(args, world) if not c3 else
+                   dict(workload=f'config 3: 12 synthetic games on 4 boards, {E} envs/GPU, 16 level-start slots per '
+                                 'game, P(level start)=1 with Dirichlet(1) weights, pack6 on',
+                        level_slots_saved=lv_info, envs_per_gpu=E, frames_per_decision=4, parallelism=f'dp{world}',
                         inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)'),
+            aged_decisions=args.age, collective='NCCL all-reduce of the episode counters every 128 decisions',
             frames_per_s=round(4 * value, 1),
             e2e=dict(value=round(e2e_value, 1), unit=UNIT, h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=d2h // K,
                      pinned_ring_slots=R, host_link_gbs=round(link, 1) if link else None,
@@ -787,8 +805,7 @@ def main():
                     steps=r['steps'], warmup=args.warmup, ms_per_step=round(1e3 * r['seconds'] / r['steps'], 3),
                     higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
                     data='synthetic (seeded NROM cart synth00, random legal moves)',
-                    config=dict(workload=nrom_workload(args.envs),
-                                envs_per_gpu=args.envs, envs_timed=r['envs'], frames_per_decision=4),
+                    config=workload_config(args, world), envs_timed=r['envs'],
                     cpu_baseline=dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
                                       sample=sample, cpu=cpu_model()),
                     e2e=dict(value=round(r['value'], 1), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))

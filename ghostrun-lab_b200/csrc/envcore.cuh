@@ -295,6 +295,7 @@ struct EnvArgs {
     u32* fault;
     u8* resetting;
     u8* render_seq;     // [N, 4] frames left to the sequential renderer by the last render pass
+    unsigned long long* render_stats;   // [2] frames drawn by the sequential renderer, split lines drawn by the walk
     u8* tm_used;        // [N] 1: the env's restart was copied from a restart template (no restart frames to run)
     double* ep_acc;     // optional [4]: finished episodes, their deaths, their returns, level events (added here)
     // restart list
@@ -941,6 +942,7 @@ __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render_seq(const __gri
         if (!R.seqf[sl]) continue;
         u8* out = R.packed ? R.packed + sl * (kObsPixels / 4 * 3) : R.obs + sl * kObsPixels;
         rd.draw(ge, f, out, R.emph + sl * kObsH, R.packed != nullptr);
+        if (lane == 0) atomicAdd(R.stats, 1ull);
         __syncwarp();
     }
 }

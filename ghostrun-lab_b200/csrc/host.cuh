@@ -271,6 +271,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     R.emph = A.emph;
     R.packed = A.packed;
     R.seqf = A.render_seq;
+    R.stats = A.render_stats;
     R.e0 = g.e0;
     R.count = n;
     R.frames = kFramesPerDecision;

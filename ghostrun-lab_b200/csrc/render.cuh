@@ -68,6 +68,7 @@ struct RenderArgs {
     const u32* list_count;
     const u8* skip;      // envs to leave out (non-zero), nullptr = none
     u8* seqf;            // [N, 4]: 1 = the frame is left to the sequential renderer (k_render_seq)
+    unsigned long long* stats;   // [2]: frames drawn by k_render_seq, lines drawn exactly by the walk (split lines)
     u32 e0, count;       // global env range of this launch (game slice)
     u32 frames;          // frames per env to draw (4)
     u32 chrx_smem;       // 1: the cart's pattern table is staged in shared memory (8 KB CHR ROM boards)
@@ -852,6 +853,7 @@ struct Renderer {
                 wb.ev = reinterpret_cast<const u32*>(__shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(w.ev), 0));
                 __syncwarp();   // the leader's derive of this line's palette version is visible
                 split_line(F, wb, ls, obs_out, pack6);
+                if (lane == 0) atomicAdd(A.stats + 1, 1ull);
                 if (lane == 0) {
                     // the line's writes into the walk's copy-on-write tables; the exact registers replace the walk's
                     while (w.cursor < s.cursor && !w.seq) walk_apply(w, F, true);

@@ -124,6 +124,93 @@ __global__ void k_gather_rows(uint4* __restrict__ dst, const uint4* __restrict__
     for (std::size_t i = blockIdx.y * static_cast<std::size_t>(blockDim.x) + threadIdx.x; i < row_vecs; i += static_cast<std::size_t>(gridDim.y) * blockDim.x) d[i] = sr[i];
 }
 
+// One legal move per env from the masks of the last decision and 32 random bits per env: each part (d-pad 9, A 3,
+// B 3, Start 2, Select 2 choices; mask bytes 0-8, 9-11, 12-14, 15-16, 17-18) uniform among its allowed choices, the
+// distribution of the reference's sampler (rl/actions.py:18-20, torch.multinomial over each part's 0/1 mask), with
+// the draws made by splitmix64 (Vigna's published mixer) of the env's word and the part. Packed as
+// d + 9 a + 27 b + 81 start + 162 select.
+__global__ void __launch_bounds__(256) k_legal_moves(const u8* __restrict__ masks, const u32* __restrict__ words,
+                                                     std::int16_t* __restrict__ out, u32 n) {
+    const u32 e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    const u8* m = masks + static_cast<std::size_t>(e) * 19;
+    const u32 w = words[e];
+    constexpr u32 kLo[5] = {0, 9, 12, 15, 17}, kCnt[5] = {9, 3, 3, 2, 2}, kMul[5] = {1, 9, 27, 81, 162};
+    u32 move = 0;
+#pragma unroll
+    for (u32 p = 0; p < 5; ++p) {
+        u32 allowed = 0;
+        for (u32 c = 0; c < kCnt[p]; ++c) allowed |= (m[kLo[p] + c] ? 1u : 0u) << c;
+        u64 z = ((static_cast<u64>(w) << 32) | p) + 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        const u32 k = static_cast<u32>((static_cast<u64>(static_cast<u32>(z >> 32)) * __popc(allowed)) >> 32);
+        u32 pick = 0, a = allowed;   // the k-th allowed choice (0 when none is allowed)
+        for (u32 j = 0; j < k; ++j) a &= a - 1;
+        if (a) pick = __ffs(a) - 1;
+        move += pick * kMul[p];
+    }
+    out[e] = static_cast<std::int16_t>(move);
+}
+
+}  // namespace
+
+// ---- machine dump without any device allocation
+//
+// Who cannot allocate: a watchdog or debugger that inspects envs of a running rollout after the GPU's memory is
+// spent (env state, device picture buffers and the caching allocator's pools sized to fill HBM), where the
+// cudaMallocAsync staging of rlenv_dump_env fails exactly when a dump is wanted, and hosts whose memory policy fixes
+// all device memory at start-up and forbids later allocation. rlenv_dump_envs_noalloc stages through the file-scope
+// device array below instead and calls no cudaMalloc, cudaFree or allocating library routine.
+namespace {
+
+constexpr int kNoAllocMaxEnvs = 8;                 // RLENV_DUMP_NOALLOC_MAX_ENVS
+static_assert(kNoAllocMaxEnvs == RLENV_DUMP_NOALLOC_MAX_ENVS && kDumpBytes == RLENV_DUMP_BYTES,
+              "include/rlenv_api.h sizes");
+constexpr int kNoAllocMaxDevices = 64;
+// 8 x 23,040 B = 184,320 B. Every GPU that loads this library holds it until the process exits. Records start
+// 256-byte aligned (23,040 = 90 x 256).
+static __device__ __align__(256) u8 g_dump_scratch[kNoAllocMaxEnvs * kDumpBytes];
+static_assert(kDumpBytes % 256 == 0, "dump records keep the scratch alignment");
+
+std::mutex g_scratch_mu;
+u8* g_scratch_ptr[kNoAllocMaxDevices] = {};        // device address of g_dump_scratch, per device, after set-up
+
+// Set-up, once per device, with that device current: look up the array's device address and load k_dump's code
+// (cudaFuncGetAttributes; with lazy loading a kernel's code is otherwise loaded at its first launch). Both can need
+// device memory, so rlenv_create does this while memory is still free; a later dump then only launches and copies.
+u8* noalloc_scratch(int device) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (device < 0 || device >= kNoAllocMaxDevices) throw std::runtime_error("rlenv_dump_envs_noalloc: bad device");
+    if (g_scratch_ptr[device]) return g_scratch_ptr[device];
+    int prev = 0;
+    ck(cudaGetDevice(&prev), "rlenv_dump_envs_noalloc: cudaGetDevice");
+    ck(cudaSetDevice(device), "rlenv_dump_envs_noalloc: cudaSetDevice");
+    void* p = nullptr;
+    cudaError_t rc = cudaGetSymbolAddress(&p, g_dump_scratch);
+    cudaFuncAttributes fa{};
+    if (rc == cudaSuccess) rc = cudaFuncGetAttributes(&fa, k_dump);
+    const cudaError_t rc_back = cudaSetDevice(prev);
+    if (rc != cudaSuccess)
+        throw std::runtime_error(std::string("rlenv_dump_envs_noalloc: set-up (cudaGetSymbolAddress / cudaFuncGetAttributes) "
+                                             "failed: ") + cudaGetErrorString(rc));
+    if (rc_back != cudaSuccess) throw std::runtime_error("rlenv_dump_envs_noalloc: cudaSetDevice (restore) failed");
+    g_scratch_ptr[device] = static_cast<u8*>(p);
+    return g_scratch_ptr[device];
+}
+
+// The caller's current device for the length of a call that launches on env.device, restored on return.
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int device) {
+        ck(cudaGetDevice(&prev), "cudaGetDevice");
+        if (prev != device) ck(cudaSetDevice(device), "cudaSetDevice");
+        else prev = -1;
+    }
+    ~DeviceScope() { if (prev >= 0) cudaSetDevice(prev); }
+};
+
 }  // namespace
 
 extern "C" {
@@ -177,6 +264,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
         A.fault = M.allocn<u32>(N, true);
         A.resetting = M.allocn<u8>(N);
         A.render_seq = M.allocn<u8>(static_cast<std::size_t>(N) * kFramesPerDecision);   // transient: not saved
+        A.render_stats = M.allocn<unsigned long long>(2);   // transient: not saved
         A.tm_used = M.allocn<u8>(N);
         A.list = M.allocn<u32>(N);                                    // per game: its slice [game_e0, game_e0 + n)
         A.list_count = M.allocn<u32>(static_cast<std::size_t>(ngames) + 1 + N);   // per game, then per range start
@@ -276,6 +364,7 @@ void* rlenv_create(int ngames, const int* game_ids, const std::uint8_t* const* r
             env->gside_done.push_back(e);
         }
         env->timer = new KTimer();
+        noalloc_scratch(device);   // rlenv_dump_envs_noalloc's per-device set-up, while device memory is still free
         ck(cudaDeviceSynchronize(), "create");
         return env;
     } catch (const std::exception& ex) {
@@ -594,6 +683,20 @@ int rl_gather_envs(void* dst, const void* src, const std::int64_t* envs, int n, 
     return 0;
 }
 
+// One legal move per env (see k_legal_moves): masks u8[n,19] (the env's masks output), words u32[n] random bits,
+// actions i16[n]; device pointers, asynchronous on `stream`.
+int rl_legal_moves(const void* masks, const void* words, void* actions, int n, void* stream) {
+    try {
+        if (n < 0 || (n > 0 && (!masks || !words || !actions))) throw std::runtime_error("rl_legal_moves: bad arguments");
+        if (n == 0) return 0;
+        k_legal_moves<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const u8*>(masks), static_cast<const u32*>(words), static_cast<std::int16_t*>(actions),
+            static_cast<u32>(n));
+        check_launch("k_legal_moves");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
 // ---- measurement: per-kernel device time on the launching stream (CUDA events), launch counts
 void rlenv_set_timing(void* h, int on) {
     KTimer& T = *static_cast<Env*>(h)->timer;
@@ -625,6 +728,7 @@ int rlenv_dump_env(void* h, int ge, std::uint8_t* host_out, void* stream) {
     try {
         Env& env = *static_cast<Env*>(h);
         if (ge < 0 || ge >= env.total) throw std::runtime_error("dump: bad env index");
+        DeviceScope on(env.device);
         auto s = static_cast<cudaStream_t>(stream);
         u8* d = nullptr;
         ck(cudaMallocAsync(reinterpret_cast<void**>(&d), kDumpBytes, s), "dump alloc");
@@ -633,6 +737,22 @@ int rlenv_dump_env(void* h, int ge, std::uint8_t* host_out, void* stream) {
         ck(cudaMemcpyAsync(host_out, d, kDumpBytes, cudaMemcpyDeviceToHost, s), "dump copy");
         ck(cudaFreeAsync(d, s), "dump free");
         ck(cudaStreamSynchronize(s), "dump");
+        return 0;
+    } catch (const std::exception& ex) { return fail(ex); }
+}
+
+// How the pictures since the last reset were drawn: out[0] frames drawn by the sequential renderer (k_render_seq),
+// out[1] lines with a write inside their drawn part drawn exactly by the walk (host memory, synchronous).
+int rlenv_render_stats(void* h, std::uint64_t* out, int reset, void* stream) {
+    try {
+        Env& env = *static_cast<Env*>(h);
+        if (!out) throw std::runtime_error("rlenv_render_stats: null pointer");
+        auto s = static_cast<cudaStream_t>(stream);
+        unsigned long long v[2] = {0, 0};
+        ck(cudaMemcpyAsync(v, env.A.render_stats, sizeof v, cudaMemcpyDeviceToHost, s), "render stats");
+        if (reset) ck(cudaMemsetAsync(env.A.render_stats, 0, sizeof v, s), "render stats reset");
+        ck(cudaStreamSynchronize(s), "render stats");
+        out[0] = v[0]; out[1] = v[1];
         return 0;
     } catch (const std::exception& ex) { return fail(ex); }
 }
@@ -655,52 +775,6 @@ int rlenv_env_scalars(void* h, int ge, std::uint64_t* out, void* stream) {
     } catch (const std::exception& ex) { return fail(ex); }
 }
 
-}  // extern "C"
-
-// ---- machine dump without any device allocation
-//
-// Who cannot allocate: a watchdog or debugger that inspects envs of a running rollout after the GPU's memory is
-// spent (env state, device picture buffers and the caching allocator's pools sized to fill HBM), where the
-// cudaMallocAsync staging of rlenv_dump_env fails exactly when a dump is wanted, and hosts whose memory policy fixes
-// all device memory at start-up and forbids later allocation. rlenv_dump_envs_noalloc stages through the file-scope
-// device array below instead and calls no cudaMalloc, cudaFree or allocating library routine.
-namespace {
-
-constexpr int kNoAllocMaxEnvs = 8;                 // RLENV_DUMP_NOALLOC_MAX_ENVS
-static_assert(kNoAllocMaxEnvs == RLENV_DUMP_NOALLOC_MAX_ENVS && kDumpBytes == RLENV_DUMP_BYTES,
-              "include/rlenv_api.h sizes");
-constexpr int kNoAllocMaxDevices = 64;
-// 8 x 23,040 B = 184,320 B. Every GPU that loads this library holds it until the process exits. Records start
-// 256-byte aligned (23,040 = 90 x 256).
-static __device__ __align__(256) u8 g_dump_scratch[kNoAllocMaxEnvs * kDumpBytes];
-static_assert(kDumpBytes % 256 == 0, "dump records keep the scratch alignment");
-
-std::mutex g_scratch_mu;
-u8* g_scratch_ptr[kNoAllocMaxDevices] = {};        // device address of g_dump_scratch, per device, after set-up
-
-// Set-up, once per device, with that device current: look up the array's device address. The first call on a
-// device may load this library's device code there, which is why it must come before any stream capture.
-u8* noalloc_scratch(int device) {
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (device < 0 || device >= kNoAllocMaxDevices) throw std::runtime_error("rlenv_dump_envs_noalloc: bad device");
-    if (g_scratch_ptr[device]) return g_scratch_ptr[device];
-    int prev = 0;
-    ck(cudaGetDevice(&prev), "rlenv_dump_envs_noalloc: cudaGetDevice");
-    ck(cudaSetDevice(device), "rlenv_dump_envs_noalloc: cudaSetDevice");
-    void* p = nullptr;
-    const cudaError_t rc = cudaGetSymbolAddress(&p, g_dump_scratch);
-    const cudaError_t rc_back = cudaSetDevice(prev);
-    if (rc != cudaSuccess)
-        throw std::runtime_error(std::string("rlenv_dump_envs_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(rc));
-    if (rc_back != cudaSuccess) throw std::runtime_error("rlenv_dump_envs_noalloc: cudaSetDevice (restore) failed");
-    g_scratch_ptr[device] = static_cast<u8*>(p);
-    return g_scratch_ptr[device];
-}
-
-}  // namespace
-
-extern "C" {
-
 // rlenv_dump_env for envs[0..n) in one call, n <= 8, without allocating: n x 23,040 bytes into host_out, same
 // layout. k_dump zero-fills each record it writes before setting the fields, so nothing of an earlier call's
 // contents (the array keeps them) reaches the output. Every call and every handle on a device shares the one array:
@@ -716,7 +790,8 @@ int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, std::uint8_t* host_
         if (!envs || !host_out) throw std::runtime_error("rlenv_dump_envs_noalloc: null pointer");
         for (int i = 0; i < n; ++i)
             if (envs[i] < 0 || envs[i] >= env.total) throw std::runtime_error("rlenv_dump_envs_noalloc: bad env index");
-        u8* scratch = noalloc_scratch(env.device);
+        DeviceScope on(env.device);
+        u8* scratch = noalloc_scratch(env.device);   // looked up by rlenv_create already
         auto s = static_cast<cudaStream_t>(stream);
         for (int i = 0; i < n; ++i) {
             k_dump<<<1, 32, 0, s>>>(env.A.st, static_cast<u32>(envs[i]), env.chr_ram_any ? 1u : 0u,

@@ -90,6 +90,8 @@ def _load(path: Path):
     if hasattr(lib, 'rlenv_dump_env'):
         lib.rlenv_dump_env.argtypes = [P, I, P, P]
         lib.rlenv_env_scalars.argtypes = [P, I, P, P]
+    if hasattr(lib, 'rlenv_render_stats'):
+        lib.rlenv_render_stats.argtypes = [P, P, I, P]
     if hasattr(lib, 'rlenv_enable_places'):
         lib.rlenv_enable_level_starts.argtypes = [P, I]
         lib.rlenv_enable_places.argtypes = [P, I, I]
@@ -103,7 +105,8 @@ def _load(path: Path):
         lib.rlenv_level_layout.argtypes = [P, I, P]
     for name, args in (('rl_pack6', [P, P, SZ, P]), ('rl_unpack6', [P, P, SZ, P]), ('rl_memcpy_async', [P, P, SZ, P]),
                        ('rl_gather_rows', [P, P, P, I, SZ, P]), ('rl_gather_envs', [P, P, P, I, I, I, SZ, P]),
-                       ('rlenv_step_game', [P, I, P, P, P]), ('rlenv_step_range', [P, I, I, I, P, P, P])):
+                       ('rlenv_step_game', [P, I, P, P, P]), ('rlenv_step_range', [P, I, I, I, P, P, P]),
+                       ('rl_legal_moves', [P, P, P, I, P])):
         if hasattr(lib, name):
             getattr(lib, name).argtypes = args
     if hasattr(lib, 'rl_host_alloc'):
@@ -341,6 +344,24 @@ class RlEnv:
         names = ('frames', 'render', 'finish', 'restart_frames', 'restart_render', 'pack6')
         return dict(ms={k: float(out[i]) for i, k in enumerate(names)},
                     launches={k: int(out[6 + i]) for i, k in enumerate(names)}, total_launches=int(out[12]))
+
+    def legal_moves(self, words):
+        """env.actions <- one legal move per env under env.masks, each move part uniform among its allowed choices
+        (the distribution of actions.random_legal), drawn from `words` (int32 / uint32 random bits [N] on the env's
+        device) by the library's own kernel on the current stream. GPU library only."""
+        assert words.numel() == self.n and words.element_size() == 4 and words.is_contiguous()
+        self._check(self.lib.rl_legal_moves(ctypes.c_void_p(self.masks.data_ptr()), ctypes.c_void_p(words.data_ptr()),
+                                            ctypes.c_void_p(self.actions.data_ptr()), self.n, self._stream()),
+                    'rl_legal_moves')
+
+    def render_stats(self, reset=False) -> dict:
+        """How the pictures since the last reset were drawn: frames the sequential renderer drew (`seq_frames`) and
+        lines with a write inside their drawn part the two-phase renderer drew exactly (`split_lines`). GPU library
+        only (synchronous)."""
+        out = np.zeros(2, np.uint64)
+        self._check(self.lib.rlenv_render_stats(self.h, out.ctypes.data_as(ctypes.c_void_p), int(bool(reset)),
+                                                self._stream()), 'render_stats')
+        return dict(seq_frames=int(out[0]), split_lines=int(out[1]))
 
     def game_slices(self):
         out, a = [], 0

@@ -162,6 +162,7 @@ MAPPERS = {'nrom': 0, 'mmc1': 1, 'uxrom': 2, 'cnrom': 3, 'mmc3': 4, 'mmc2': 9}
 ZP_BUTTONS, ZP_TMP, ZP_LFSR, ZP_FRAME = 0x00, 0x01, 0x02, 0x04
 ZP_PTR = 0x06
 ZP_DMC = 0x08   # the DMC variant keeps each frame's $4015 read here
+ZP_COUNT = 0x0A   # loop counter of the mid-frame PPU variants
 ZP_PROGRESS, ZP_LEVEL, ZP_LIVES, ZP_SCORE, ZP_MODE = 0x10, 0x12, 0x13, 0x14, 0x17
 OAM_BUF = 0x0200
 
@@ -175,8 +176,9 @@ class Cart:
     params: dict          # the seed-derived template constants
 
 
-def _template(a: Asm, p: dict, board: str, data_labels: dict, dmc: bool = False):
-    """The reset/NMI/IRQ program (see the module docstring); `dmc`: the NMI also plays a DMC sample."""
+def _template(a: Asm, p: dict, board: str, data_labels: dict, dmc: bool = False, ppu: str | None = None):
+    """The reset/NMI/IRQ program (see the module docstring); `dmc`: the NMI also plays a DMC sample; `ppu`: the NMI
+    ends with one of the mid-frame PPU programs of `_ppu_variant`."""
     i = a.i
     # ---------------------------------------------------------------- reset
     a.label('reset')
@@ -344,6 +346,8 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict, dmc: bool = False)
     # player sprite (sprite 1) follows progress
     i('LDA', 'zp', ZP_PROGRESS); i('LSR', 'acc'); i('STA', 'abs', OAM_BUF + 7)
     a.label('nmi_out')
+    if ppu is not None:
+        _ppu_variant(a, p, ppu)
     if board == 'mmc2':
         # every 64th frame: wait ~2,400 cycles in 7-cycle instructions (into the picture, about line 10), then
         # rewrite the $FE bank of the $0000 half and put $1FD8 on the bus (the rest of the frame is drawn from there)
@@ -387,6 +391,67 @@ def _template(a: Asm, p: dict, board: str, data_labels: dict, dmc: bool = False)
         a.bytes(data)
 
 
+PPU_VARIANTS = ('split', 'raster', 'vread')
+
+
+def _delay(a: Asm, tag: str, outer: int, inner: int):
+    """About outer * (inner * 5 + 4) CPU cycles: nested DEX / DEY loops."""
+    a.i('LDY', 'imm', outer)
+    a.label(tag + '_o'); a.i('LDX', 'imm', inner & 0xFF)
+    a.label(tag + '_i'); a.i('DEX'); a.i('BNE', 'rel', tag + '_i')
+    a.i('DEY'); a.i('BNE', 'rel', tag + '_o')
+
+
+def _ppu_variant(a: Asm, p: dict, kind: str):
+    """Mid-frame PPU programs run at the end of the NMI, the ways real games drive the PPU while it draws:
+
+    split   SMB-style status bar: wait for the sprite-0 flag of the last frame to clear (pre-render line), poll
+            $2002 bit 6 until sprite 0 hits (bounded: ~25,000 cycles, then give up for this frame), then, in the
+            middle of that line, a $2006 pair (moves the VRAM address at once) and a $2005 pair (the scroll the next
+            line's horizontal copy takes).
+    raster  wait into the picture, then 6 times: rendering off, one palette entry rewritten through $2006 / $2007,
+            the VRAM address put back into the nametable, rendering (background + sprites) on again, a few lines
+            apart: more palette versions in one frame than the walk keeps, lines drawn with rendering off, and
+            rendering switched back on inside lines or their hblank.
+    vread   wait into the picture, then 3 $2007 reads a few lines apart with rendering on (the read buffer refill
+            moves the VRAM address as the PPU's own increments do).
+    """
+    i = a.i
+    assert kind in PPU_VARIANTS, kind
+    if kind == 'split':
+        a.label('s0_clear'); i('BIT', 'abs', 0x2002); i('BVS', 'rel', 's0_clear')
+        i('LDY', 'imm', 9)
+        a.label('s0_o'); i('LDX', 'imm', 0)
+        a.label('s0_i'); i('BIT', 'abs', 0x2002); i('BVS', 'rel', 's0_hit'); i('DEX'); i('BNE', 'rel', 's0_i')
+        i('DEY'); i('BNE', 'rel', 's0_o'); i('JMP', 'abs', 's0_end')
+        a.label('s0_hit')
+        i('LDA', 'imm', 0x21); i('STA', 'abs', 0x2006); i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 0xE0)
+        i('STA', 'abs', 0x2006)
+        i('LDA', 'zp', ZP_PROGRESS); i('STA', 'abs', 0x2005); i('LDA', 'zp', ZP_FRAME); i('AND', 'imm', 0x0F)
+        i('STA', 'abs', 0x2005)
+        a.label('s0_end')
+        return
+    _delay(a, kind + '_in', 3, 0)   # ~3,900 cycles: from the NMI's end past the pre-render line into the picture
+    if kind == 'raster':
+        i('LDA', 'imm', 6); i('STA', 'zp', ZP_COUNT)
+        a.label('ras')
+        i('LDX', 'imm', 120); a.label('ras_d'); i('DEX'); i('BNE', 'rel', 'ras_d')   # ~600 cycles, ~5 lines
+        i('LDA', 'imm', 0x00); i('STA', 'abs', 0x2001)
+        i('LDA', 'imm', 0x3F); i('STA', 'abs', 0x2006)
+        i('LDA', 'zp', ZP_COUNT); i('ASL', 'acc'); i('ASL', 'acc'); i('ASL', 'acc'); i('ORA', 'imm', 0x01)
+        i('AND', 'imm', 0x1F); i('STA', 'abs', 0x2006)
+        i('LDA', 'zp', ZP_FRAME); i('EOR', 'zp', ZP_COUNT); i('AND', 'imm', 0x3F); i('STA', 'abs', 0x2007)
+        i('LDA', 'imm', 0x20); i('STA', 'abs', 0x2006); i('LDA', 'zp', ZP_COUNT); i('STA', 'abs', 0x2006)
+        i('LDA', 'imm', p['mask']); i('STA', 'abs', 0x2001)
+        i('DEC', 'zp', ZP_COUNT); i('BNE', 'rel', 'ras')
+        return
+    i('LDA', 'imm', 3); i('STA', 'zp', ZP_COUNT)
+    a.label('vr')
+    i('LDX', 'zp', ZP_LFSR); a.label('vr_d'); i('DEX'); i('BNE', 'rel', 'vr_d')   # 5..1,280 cycles, by the LFSR
+    i('LDA', 'abs', 0x2007)
+    i('DEC', 'zp', ZP_COUNT); i('BNE', 'rel', 'vr')
+
+
 def _mmc1_write(a: Asm, addr: int, value: int, tag: str):
     """Serial MMC1 register write of a constant (reset bit first)."""
     a.i('LDA', 'imm', 0x80); a.i('STA', 'abs', 0x8000)
@@ -419,10 +484,14 @@ def template_params(seed: int, board: str) -> dict:
     return p
 
 
-def make_cart(seed: int, board: str = 'nrom', dmc: bool = False) -> Cart:
+def make_cart(seed: int, board: str = 'nrom', dmc: bool = False, ppu: str | None = None) -> Cart:
     """A seeded synthetic cartridge (iNES image + boot pads); `dmc`: a variant whose NMI plays a DMC sample every
-    frame (the registered games never do; tests use it for the sample channel and its cycle steals)."""
+    frame (the registered games never do; tests use it for the sample channel and its cycle steals); `ppu`: a variant
+    whose NMI ends with a mid-frame PPU program (`PPU_VARIANTS`, see `_ppu_variant`; not on MMC2, whose NMI has its own
+    mid-frame writes), for the sequential renderer and the CPU-visible sprite-0 flag."""
     assert board in MAPPERS, board
+    assert ppu is None or board != 'mmc2', 'the MMC2 cart has its own mid-frame program'
+
     p = template_params(seed, board)
     r = np.random.default_rng([seed, 0xC0DE])
     chr_bytes = r.integers(0, 256, 8192, dtype=np.uint8).tobytes()
@@ -445,7 +514,7 @@ def make_cart(seed: int, board: str = 'nrom', dmc: bool = False) -> Cart:
         data['chrtab'] = chr_bytes
     # program in the last 16 KB (fixed bank on every board), vectors at $FFFA
     a = Asm(0xC000)
-    _template(a, p, board, data, dmc)
+    _template(a, p, board, data, dmc, ppu)
     img = a.assemble()
     assert max(img) < 0xFFFA, 'program overflows into the vectors'
     prg = bytearray(r.integers(0, 256, prg_size, dtype=np.uint8).tobytes())
@@ -454,12 +523,10 @@ def make_cart(seed: int, board: str = 'nrom', dmc: bool = False) -> Cart:
         prg[base + addr - 0xC000] = b
     vec = struct.pack('<HHH', a.labels['nmi'], a.labels['reset'], a.labels['irq'])
     prg[prg_size - 6:] = vec
-    if board == 'nrom':   # 32 KB: the image at $8000-$FFFF, program in its top half
-        pass
     mapper = MAPPERS[board]
-    chr_rom = b'' if board == 'mmc1' else (chr_bytes if board != 'mmc3' else
-                                             r.integers(0, 256, 131072, dtype=np.uint8).tobytes()[:0] + chr_bytes * 16)
+    chr_rom = b'' if board == 'mmc1' else chr_bytes   # MMC1: CHR-RAM, filled by the reset code from CHRTAB
     if board == 'mmc3':
+        r.integers(0, 256, 131072, dtype=np.uint8)   # skipped: the cart's bytes stay those every earlier build drew
         chr_rom = bytes(chr_bytes) + r.integers(0, 256, 131072 - 8192, dtype=np.uint8).tobytes()
     if board == 'cnrom':   # 4 CHR banks of 8 KB
         chr_rom = bytes(chr_bytes) + r.integers(0, 256, 32768 - 8192, dtype=np.uint8).tobytes()

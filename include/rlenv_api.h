@@ -89,6 +89,11 @@ int rl_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);    
 int rl_gather_rows(void* dst, const void* src, const int64_t* rows, int nrows, size_t row_bytes, void* stream);  // rl/csrc/rlenv.cu:400-409
 int rl_gather_envs(void* dst, const void* src, const int64_t* envs, int n, int T, int N, size_t row_bytes,
                    void* stream);                                         // rl/csrc/rlenv.cu:411-421
+// The reference's random legal moves (rl/actions.py:18-20 random_legal: each move part uniform among the choices its
+// mask allows) on the device: masks u8[n,19] (the last decision's masks output), words u32[n] random bits (one draw
+// per env; the parts' draws are mixed from it), actions i16[n] packed move ids. The distribution is the reference
+// sampler's; the random stream is not torch's. Device pointers, asynchronous on `stream`.
+int rl_legal_moves(const void* masks, const void* words, void* actions, int n, void* stream);
 
 // ---------------------------------------------------------------- extensions (no reference counterpart)
 
@@ -105,14 +110,20 @@ size_t rlenv_dump_bytes(void);
 int rlenv_dump_env(void* h, int ge, uint8_t* host_out, void* stream);
 // target, ep_frame, episode, fault, sticky counter of env ge into host memory (synchronous).
 int rlenv_env_scalars(void* h, int ge, uint64_t* host_out, void* stream);
+// How the pictures since the last reset were drawn (synchronous on `stream`; reset != 0 clears the counts
+// afterwards): out[0] = frames the sequential renderer drew (more than 4 palette or CHR-page versions, a write inside
+// a line's drawn part on the boards without split-line drawing, sprites switched on in the hblank of a line drawn with
+// rendering off, every MMC2 frame), out[1] = lines with a write inside their drawn part that the two-phase renderer
+// drew exactly itself (MMC3).
+int rlenv_render_stats(void* h, uint64_t* host_out, int reset, void* stream);
 // No counterpart in the reference. rlenv_dump_env without any device allocation, for callers that cannot allocate
 // device memory: a watchdog or debugger inspecting a rollout that has spent the GPU's memory (where the staging
 // allocation of rlenv_dump_env would fail), or a host whose policy fixes device memory at start-up. Dumps
 // envs[0..n) (host array, 1 <= n <= RLENV_DUMP_NOALLOC_MAX_ENVS; more is rejected with a message) into host_out,
 // n x RLENV_DUMP_BYTES in the rlenv_dump_env layout, synchronous on `stream`. It stages through one file-scope
 // device array of 8 x RLENV_DUMP_BYTES = 184,320 bytes, which every GPU that loads the library holds until exit.
-// The first call on a device looks the array up (cudaGetSymbolAddress, which may load the library's device code):
-// make that first call before any stream capture. All calls and handles on a device share the array; calls whose
+// rlenv_create does the per-device set-up while device memory is still free (the array's address by
+// cudaGetSymbolAddress, and the dump kernel's code loaded), so the call itself only launches that kernel and copies. All calls and handles on a device share the array; calls whose
 // work overlaps on the GPU (two threads, two streams) race.
 #define RLENV_DUMP_NOALLOC_MAX_ENVS 8
 int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, uint8_t* host_out, void* stream);

@@ -36,6 +36,9 @@ def test_reference_arm_prints_the_contract_line():
     assert cb['kind'] == 'port' and cb['cores'] >= 1 and cb['value'] == d['value'] and cb['sample']
     assert d['e2e'] == {'value': d['value'], 'unit': 'decisions/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}
     assert d['config']['workload'].startswith('config 2')
+    # the GPU arm reports the same config (bench.workload_config), so the driver sees one workload in both arms
+    import types
+    assert d['config'] == json.loads(json.dumps(_bench_module().workload_config(types.SimpleNamespace(envs=8192), 1)))
 
 
 def test_workload_names_follow_the_env_count():

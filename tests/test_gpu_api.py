@@ -189,3 +189,59 @@ def test_episode_counters_in_finishing_kernel(gpu_lib_path):
     for k in ('finished', 'deaths', 'level_events'):
         assert va[k] == vb[k], (k, va[k], vb[k])
     assert abs(va['return_sum'] - vb['return_sum']) <= 1e-4 * max(1.0, abs(vb['return_sum']))
+
+
+def _legal_moves_numpy(masks: np.ndarray, words: np.ndarray) -> np.ndarray:
+    """The sampler of rl_legal_moves restated: per part, splitmix64 of (word << 32 | part), the high 32 bits scaled
+    to the number of allowed choices, the k-th allowed choice."""
+    M = (1 << 64) - 1
+    lo, cnt, mul = (0, 9, 12, 15, 17), (9, 3, 3, 2, 2), (1, 9, 27, 81, 162)
+    out = np.zeros(len(words), np.int16)
+    for e, w in enumerate(words.astype(np.uint32).tolist()):
+        move = 0
+        for p in range(5):
+            allowed = [c for c in range(cnt[p]) if masks[e, lo[p] + c]]
+            z = (((w << 32) | p) + 0x9E3779B97F4A7C15) & M
+            z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+            z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+            z ^= z >> 31
+            k = ((z >> 32) * len(allowed)) >> 32
+            move += (allowed[k] if allowed else 0) * mul[p]
+        out[e] = move
+    return out
+
+
+@pytest.mark.gpu
+def test_legal_moves_sampler(gpu_lib_path):
+    """rl_legal_moves (the benchmark's device sampler): every move legal under the masks, equal to the restated draw
+    bit for bit, and each part uniform over its allowed choices (the distribution of rl/actions.py random_legal)."""
+    from actions import unpack, PARTS
+    e = _env(gpu_lib_path, seed=4)
+    gen = torch.Generator(device='cuda').manual_seed(3)
+    for t in range(12):   # masks with dropout in effect somewhere
+        e.legal_moves(torch.randint(-2 ** 31, 2 ** 31, (e.n,), generator=gen, device='cuda', dtype=torch.int64).to(torch.int32))
+        e.step()
+    # legality and the restated draw on the env's masks
+    words = torch.randint(-2 ** 31, 2 ** 31, (e.n,), generator=gen, device='cuda', dtype=torch.int64).to(torch.int32)
+    e.legal_moves(words)
+    torch.cuda.synchronize()
+    masks = e.masks.cpu().numpy()
+    got = e.actions.cpu().numpy()
+    assert np.array_equal(got, _legal_moves_numpy(masks, words.cpu().numpy()))
+    parts = unpack(e.actions.cpu())
+    for (a, b), pt in zip(PARTS, parts):
+        assert bool(torch.from_numpy(masks[:, a:b]).gather(1, pt.view(-1, 1)).all()), 'an illegal part'
+    # uniformity: 40 envs x 2,000 draws on fixed masks, every allowed choice of every part near 1 / count
+    words = torch.randint(-2 ** 31, 2 ** 31, (2000, e.n), generator=gen, device='cuda', dtype=torch.int64).to(torch.int32)
+    draws = []
+    for r in range(2000):
+        e.legal_moves(words[r])
+        draws.append(e.actions.clone())
+    d = torch.stack(draws).cpu()
+    for p, (a, b) in enumerate(PARTS):
+        choice = unpack(d)[p]                      # [2000, n]
+        for env in range(e.n):
+            allowed = np.flatnonzero(masks[env, a:b])
+            freq = np.bincount(choice[:, env].numpy(), minlength=b - a)[allowed] / 2000
+            assert np.all(np.abs(freq - 1 / len(allowed)) < 0.06), (p, env, freq)
+            assert freq.sum() == 1.0

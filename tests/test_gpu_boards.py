@@ -17,8 +17,15 @@ def test_parity_paged_board(game, oracle_path, gpu_lib_path):
 
 @pytest.mark.gpu
 def test_parity_mixed_boards(oracle_path, gpu_lib_path):
+    """All six boards in one env; the NROM slice runs the sprite-0 status-bar split variant of its cart (mid-line
+    $2006 / $2005 writes after a $2002 poll), so its frames take the sequential renderer beside the other boards'."""
+    import synth
+    from rlenv import CART_SEED
     counts = {'synth00': 8, 'synth01': 8, 'synth02': 8, 'synth03': 8, 'synth12': 8, 'synth13': 8}
-    run_parity(counts, oracle_path, gpu_lib_path, steps=200, dump_every=40)
+    roms = {'synth00': synth.make_cart(CART_SEED, 'nrom', ppu='split').rom}
+    envs = []
+    run_parity(counts, oracle_path, gpu_lib_path, steps=200, dump_every=40, roms=roms, envs_out=envs)
+    assert envs[0].render_stats()['seq_frames'] > 0
 
 
 @pytest.mark.gpu

@@ -43,8 +43,13 @@ def _compare_dumps(g, c, envs, t):
         assert np.array_equal(g.scalars(e), c.scalars(e)), f'step {t} env {e}: scalars differ'
 
 
-def run_parity(counts, oracle_path, gpu_lib_path, steps, seed=11, dump_every=25):
-    g, c = _pair(counts, oracle_path, gpu_lib_path, seed)
+def run_parity(counts, oracle_path, gpu_lib_path, steps, seed=11, dump_every=25, roms=None, envs_out=None):
+    """Steps a GPU env and an oracle env with the same seeded legal moves and compares them (every output every
+    decision, machine dumps every `dump_every`); returns the finished episodes. roms: slug -> iNES image in place of
+    the registered cart; envs_out: a list that receives (gpu env, oracle env)."""
+    g, c = _pair(counts, oracle_path, gpu_lib_path, seed, roms=roms)
+    if envs_out is not None:
+        envs_out.extend([g, c])
     g.start()
     c.start()
     torch.cuda.synchronize()
@@ -96,7 +101,7 @@ def test_parity_config2_subset(oracle_path, gpu_lib_path):
     g.start()
     c.start()
     gen = torch.Generator().manual_seed(5)
-    gen_rest = torch.Generator(device='cuda').manual_seed(6)
+    gen_rest = torch.Generator(device='cuda').manual_seed(6)   # the other envs: the bench's device sampler
     stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
     dones = 0
     for t in range(151):
@@ -112,9 +117,10 @@ def test_parity_config2_subset(oracle_path, gpu_lib_path):
         if t == 150:
             break
         act = random_legal(c.masks, gen)
-        rest = torch.randint(0, 81, (N - S,), generator=gen_rest, device='cuda', dtype=torch.int32).to(torch.int16)
+        words = torch.randint(-2 ** 31, 2 ** 31, (N,), generator=gen_rest, device='cuda', dtype=torch.int64)
+        g.legal_moves(words.to(torch.int32))
         c.actions.copy_(act)
-        g.actions.copy_(torch.cat([act.cuda(), rest]))
+        g.actions[:S].copy_(act.cuda())
         c.step()
         g.step()
     for e in (0, 101, 255):

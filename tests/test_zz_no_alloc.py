@@ -18,6 +18,28 @@ MAX_ENVS = 8          # RLENV_DUMP_NOALLOC_MAX_ENVS
 DUMP = 23040          # RLENV_DUMP_BYTES
 
 
+class _DefaultPool:
+    """The device's default memory pool through the driver API (libcuda): its used-memory high-water mark, reset
+    before a call and read after it, shows whether the call allocated from it (rlenv_dump_env's staging does)."""
+    USED_MEM_HIGH = 8   # CU_MEMPOOL_ATTR_USED_MEM_HIGH
+
+    def __init__(self, device):
+        self.cu = ctypes.CDLL('libcuda.so.1')
+        dev = ctypes.c_int()
+        assert self.cu.cuDeviceGet(ctypes.byref(dev), device) == 0
+        self.pool = ctypes.c_void_p()
+        assert self.cu.cuDeviceGetDefaultMemPool(ctypes.byref(self.pool), dev) == 0
+
+    def reset_high(self):
+        zero = ctypes.c_uint64(0)
+        assert self.cu.cuMemPoolSetAttribute(self.pool, self.USED_MEM_HIGH, ctypes.byref(zero)) == 0
+
+    def high(self):
+        v = ctypes.c_uint64()
+        assert self.cu.cuMemPoolGetAttribute(self.pool, self.USED_MEM_HIGH, ctypes.byref(v)) == 0
+        return v.value
+
+
 def _noalloc(env, envs):
     fn = env.lib.rlenv_dump_envs_noalloc
     fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
@@ -43,6 +65,16 @@ def test_dump_noalloc_matches_dump_env(gpu_lib_path):
         for i, e in enumerate(envs):
             want = env.dump(e)
             assert np.array_equal(got[i], want), f'env {e}: bytes {np.flatnonzero(got[i] != want)[:12].tolist()}'
+
+    # allocates nothing: the default pool's high-water mark moves for the allocating dump and stays 0 for this one
+    torch.cuda.synchronize()
+    pool = _DefaultPool(torch.cuda.current_device())
+    pool.reset_high()
+    env.dump(3)
+    assert pool.high() > 0, 'the check should see rlenv_dump_env\'s staging allocation'
+    pool.reset_high()
+    rc, _ = _noalloc(env, [3, 4])
+    assert rc == 0 and pool.high() == 0, 'rlenv_dump_envs_noalloc allocated from the device pool'
 
     rc, _ = _noalloc(env, list(range(MAX_ENVS + 1)))
     assert rc != 0 and b'1..8 envs' in env.lib.rlenv_error()
