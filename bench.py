@@ -63,10 +63,11 @@ def parse():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--envs', type=int, default=None, help='envs per GPU (default 8192; 32768 for --workload config3)')
-    ap.add_argument('--workload', default='config2', choices=['config2', 'config3', 'config5', 'stem'],
+    ap.add_argument('--workload', default='config2', choices=['config2', 'config3', 'config5', 'stem', 'learner'],
                     help='config2: synthetic NROM (the headline); config3: 12 synthetic games on 4 boards with level '
                          'starts; config5: config 2 with the reference policy network choosing the moves; stem: the '
-                         'policy input stem (colour lookup + 2x2 conv, tcgen05) on packed pictures')
+                         'policy input stem (colour lookup + 2x2 conv, tcgen05) on packed pictures; learner: '
+                         'minibatches of rollout rows gathered from a pinned host region and unpacked')
     ap.add_argument('--units', type=int, default=4, help='config5: parts of the envs, each on its own stream')
     ap.add_argument('--seed', type=int, default=1)
     ap.add_argument('--age', type=int, default=1024,
@@ -120,7 +121,25 @@ def cpu_leg(args):
         env.actions.copy_(random_legal(env.masks, gen)); env.step()
     dt = time.perf_counter() - t0
     cores = int(os.environ.get('OMP_NUM_THREADS', os.cpu_count()))
-    print(json.dumps(dict(value=steps * E / dt, steps=steps, seconds=dt, cores=cores, envs=E)))
+    print(json.dumps(dict(value=steps * E / dt, steps=steps, seconds=dt, cores=cores, envs=E, split=cpu_split())))
+
+
+def cpu_split(frames=600):
+    """One thread, one console of the workload's cart: microseconds per frame spent emulating and drawing (the
+    reference's rl/bench/split_cpu.cpp method, through the oracle's oracle_split_frames)."""
+    import ctypes
+    import numpy as np
+    from rlenv import synth_cart
+    lib = ctypes.CDLL(str(ROOT / 'oracle' / 'liboracle_rlenv.so'))
+    cart = synth_cart(GAME)
+    rom, boot = np.frombuffer(cart.rom, np.uint8), np.frombuffer(cart.boot_pads, np.uint8)
+    out = np.zeros(2)
+    rc = lib.oracle_split_frames(rom.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(len(rom)),
+                                 boot.ctypes.data_as(ctypes.c_void_p), len(boot), frames, out.ctypes.data_as(ctypes.c_void_p))
+    if rc != 0:
+        return None
+    return dict(emulate_us_per_frame=round(float(out[0]), 2), draw_us_per_frame=round(float(out[1]), 2),
+                frames=frames, threads=1, method='rl/bench/split_cpu.cpp (emulate = step_until, draw = render_obs)')
 
 
 def run_cpu_leg(args, seconds, steps=0):
@@ -250,6 +269,23 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d['hbm_gbs']), 'measured'
     return 6650.0, 'fallback'
+
+
+def profile_instructions(kernel):
+    """(warp instructions of one main-pass launch, envs of that capture) from the committed ncu summary of `kernel`
+    on the synthetic NROM workload, or None."""
+    p = ROOT / 'profiles' / f'{kernel}_synth00.md'
+    if p.exists():
+        t = p.read_text()
+        m, e = re.search(r'warp_instructions_per_launch:\s*([0-9]+)', t), re.search(r'profile_envs:\s*([0-9]+)', t)
+        if m and e:
+            return int(m.group(1)), int(e.group(1))
+    return None
+
+
+# Output bytes of one env and decision with packed pictures: packed rows + emphasis + masks + timeline + pads + reward +
+# done + events + info + parts (rl/csrc/rlenv_api.h:15-19 shapes)
+OUTPUT_BYTES_PACK6 = PACKED_ROW + EMPH_ROW + 19 + 360 + 4 + 4 + 1 + 4 + 32 + 28
 
 
 def render_traffic_per_env_frame():
@@ -386,6 +422,106 @@ def stem_arm(args):
                               kernel='k_stem_bwd<packed> + k_stem_bwd_reduce'),
                 gpu_launches=K, clocks=clk.summary(), cpu_baseline=None,
                 checksum=[round(float(x), 5) for x in m[:4]])
+
+
+def learner_arm(args):
+    """The learner half of the packed picture format (rl/train.py:262-295 HostObs._fetch): T decisions of packed rows
+    and emphasis of --envs envs (at most 2,048: the pinned region is T x envs x 162,176 bytes) written by the env into
+    a pinned host region, then K minibatches of 256 random envs gathered back to the device, one copy-engine 2-D copy
+    per env (rl_gather_envs), and unpacked to colour numbers (rl_unpack6). value: env-decisions of rollout rows
+    gathered per second; GB/s against a plain pinned host->device copy of the same bytes."""
+    import ctypes
+    import numpy as np
+    import torch
+    from rlenv import RlEnv
+    dev = torch.device('cuda', 0)
+    E, T, B, K, W = min(args.envs, 2048), 16, 256, args.steps, args.warmup
+    row, erow = PACKED_ROW, EMPH_ROW
+    env = RlEnv({GAME: E}, device=dev, seed=args.seed * 7919, sticky=True, idle_max=30, dropout=True)
+    packed = torch.empty(E, 4, 224, 180, dtype=torch.uint8, device=dev)
+    env.bind_obs_pack6(packed)
+    env.start()
+    lib = env.lib
+    s = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    host, host_e = lib.rl_host_alloc(T * E * row), lib.rl_host_alloc(T * E * erow)
+    if not host or not host_e:
+        raise RuntimeError('rl_host_alloc failed')
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    try:
+        for t in range(T):   # the rollout: every decision's rows into slot t of the host region
+            env.legal_moves(random_words((E,), g, dev))
+            env.step()
+            lib.rl_memcpy_async(ctypes.c_void_p(host + t * E * row), ctypes.c_void_p(packed.data_ptr()), E * row, s)
+            lib.rl_memcpy_async(ctypes.c_void_p(host_e + t * E * erow), ctypes.c_void_p(env.emph.data_ptr()), E * erow, s)
+        torch.cuda.synchronize(dev)
+        rng = np.random.default_rng(args.seed)
+        picks = [np.ascontiguousarray(rng.permutation(E)[:B].astype(np.int64)) for _ in range(K + W)]
+        dst = torch.empty(T, B, row, dtype=torch.uint8, device=dev)
+        dst_e = torch.empty(T, B, erow, dtype=torch.uint8, device=dev)
+        obs = torch.empty(T, B, 4, 224, 240, dtype=torch.uint8, device=dev)
+
+        def batch(k):
+            envs = picks[k]
+            lib.rl_gather_envs(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(host), envs.ctypes.data_as(ctypes.c_void_p),
+                               B, T, E, row, s)
+            lib.rl_gather_envs(ctypes.c_void_p(dst_e.data_ptr()), ctypes.c_void_p(host_e),
+                               envs.ctypes.data_as(ctypes.c_void_p), B, T, E, erow, s)
+            lib.rl_unpack6(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(obs.data_ptr()), obs.numel(), s)
+
+        for k in range(W):
+            batch(k)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(0)
+        with clk:
+            e0.record()
+            for k in range(K):
+                batch(W + k)
+            e1.record()
+            torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / K
+        moved = T * B * (row + erow)
+        # the link: one plain pinned host->device copy of the same bytes
+        flat = torch.empty(moved, dtype=torch.uint8, device=dev)
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        lib.rl_memcpy_async(ctypes.c_void_p(flat.data_ptr()), ctypes.c_void_p(host), moved, s)
+        l0.record()
+        for _ in range(3):
+            lib.rl_memcpy_async(ctypes.c_void_p(flat.data_ptr()), ctypes.c_void_p(host), moved, s)
+        l1.record()
+        torch.cuda.synchronize(dev)
+        link = 3 * moved / (l0.elapsed_time(l1) / 1e3) / 1e9
+        # the unpack alone (device side of the minibatch)
+        u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        u0.record()
+        for _ in range(K):
+            lib.rl_unpack6(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(obs.data_ptr()), obs.numel(), s)
+        u1.record()
+        torch.cuda.synchronize(dev)
+        ums = u0.elapsed_time(u1) / K
+        peak, kind = measured_peaks()
+        unpack_gbs = (dst.numel() + obs.numel()) / (ums / 1e3) / 1e9
+    finally:
+        torch.cuda.synchronize(dev)
+        lib.rl_host_free(ctypes.c_void_p(host))
+        lib.rl_host_free(ctypes.c_void_p(host_e))
+    gbs = moved / (ms / 1e3) / 1e9
+    return dict(metric='rollout rows gathered (env-decisions/s: pinned host -> device + unpack)',
+                value=round(T * B / (ms / 1e3), 1), unit='env-decisions/s', n_gpus=1, steps=K, warmup=W,
+                ms_per_step=round(ms, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
+                data='synthetic (seeded NROM cart synth00, random legal moves)',
+                config=dict(workload=f'learner minibatch: {B} of {E} envs x {T} decisions of packed rows from pinned '
+                                     'host memory, gathered and unpacked', envs=E, decisions=T, minibatch=B,
+                            inputs_exceed_l2=True),
+                e2e=dict(value=round(T * B / (ms / 1e3), 1), unit='env-decisions/s', h2d_bytes_per_step=moved,
+                         d2h_bytes_per_step=0, note='the whole step is the host -> device gather'),
+                link=dict(achieved_gbs=round(gbs, 1), plain_copy_gbs=round(link, 1), frac=round(gbs / link, 3)),
+                roofline=dict(bound='host link', achieved=round(gbs, 1), peak=round(link, 1), unit='GB/s',
+                              frac=round(gbs / link, 3), traffic=None, kernel='rl_gather_envs (copy engine)',
+                              peak_source='measured here: one pinned host->device copy of the same bytes'),
+                unpack=dict(ms=round(ums, 4), achieved_gbs=round(unpack_gbs, 1), frac=round(unpack_gbs / peak, 4),
+                            peak=peak, kernel='k_unpack6'),
+                gpu_launches=K, clocks=clk.summary(), cpu_baseline=None)
 
 
 def config5_arm(args):
@@ -656,7 +792,11 @@ def gpu_arm(args):
     tm = env.timing(reset=True)
     env.set_timing(False)
     ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
+    per_rank = [ms]
+    if world > 1:   # every rank's device time (the same collective on every rank), then the max
+        gathered = [torch.zeros_like(ms_t) for _ in range(world)]
+        dist.all_gather(gathered, ms_t)
+        per_rank = [float(x.item()) for x in gathered]
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
     value = K * E * world / (ms_max / 1e3)
@@ -748,6 +888,22 @@ def gpu_arm(args):
         alg_bytes = env_frames * (PACKED_ROW // 4 + 224 + 2048 + 256 + 64)   # per decision: packed out, emph, NT, OAM, log header
         achieved = alg_bytes / (render_ms / 1e3) / 1e9
         tr = render_traffic_per_env_frame()
+        # the whole step against HBM: outputs + the env state read and written once (S_env = the saved state per env,
+        # rlenv_state_bytes / envs)
+        s_env = env.lib.rlenv_state_bytes(env.h) / E
+        step_bytes = OUTPUT_BYTES_PACK6 + 2 * s_env
+        step_gbs = value / world * step_bytes / 1e9
+        # issue-slot use of the two hot kernels: warp instructions of a main-pass launch (committed ncu capture,
+        # scaled to these envs) / (device time per decision x 148 SMs x 4 schedulers x median SM clock)
+        sm_mhz = clk.summary().get('sm_mhz') or 1965.0
+        issue = {}
+        for kern, kind in (('k_frames', 'frames'), ('k_render', 'render')):
+            pi = profile_instructions(kern)
+            kms = tm_all['ms'][kind] / K
+            if pi and kms > 0:
+                inst = pi[0] * E / pi[1]
+                issue[kern] = dict(warp_instructions_per_decision=round(inst), ms_per_decision=round(kms, 4),
+                                   issue_frac=round(inst / (kms * 1e-3 * 148 * 4 * sm_mhz * 1e6), 4))
         result = dict(
             metric=METRIC, value=round(value, 1), unit=UNIT, n_gpus=world, steps=K, warmup=W,
             ms_per_step=round(ms_max / K, 4), higher_is_better=True, scaling='weak', vs_baseline=None, dtype='u8',
@@ -760,6 +916,7 @@ def gpu_arm(args):
                         level_slots_saved=lv_info, envs_per_gpu=E, frames_per_decision=4, parallelism=f'dp{world}',
                         inputs_exceed_l2=True, l2_note='per-step state + outputs > 1.5 GB (L2 is 126 MB)'),
             aged_decisions=args.age, collective='NCCL all-reduce of the episode counters every 128 decisions',
+            per_rank_ms_per_step=[round(x / K, 4) for x in per_rank],
             frames_per_s=round(4 * value, 1),
             e2e=dict(value=round(e2e_value, 1), unit=UNIT, h2d_bytes_per_step=h2d // K, d2h_bytes_per_step=d2h // K,
                      pinned_ring_slots=R, host_link_gbs=round(link, 1) if link else None,
@@ -770,7 +927,13 @@ def gpu_arm(args):
                           traffic=round(tr * env_frames) if tr else None, kernel='k_render',
                           peak_source=f'{peak_kind} (MEASURED_PEAKS.json hbm_gbs)' if peak_kind == 'measured' else 'fallback',
                           algorithmic_bytes_per_decision=alg_bytes, render_ms_per_decision=round(render_ms, 4),
-                          render_launches_per_decision=round(tm['launches']['render'] / K, 2)),
+                          render_launches_per_decision=round(tm['launches']['render'] / K, 2),
+                          traffic_note='ncu DRAM bytes of a main render launch per env-frame drawn, x env-frames',
+                          issue=issue,
+                          step=dict(state_bytes_per_env=round(s_env, 1), output_bytes_per_decision=OUTPUT_BYTES_PACK6,
+                                    bytes_per_decision=round(step_bytes), achieved_gbs_per_gpu=round(step_gbs, 1),
+                                    frac=round(step_gbs / peak, 4),
+                                    note='outputs + 2 x S_env per decision (the whole step as one HBM pass)')),
             kernel_ms_per_step={k: round(v / K, 4) for k, v in tm_all['ms'].items()},
             kernel_ms_note='every launch timed in a second pass of the same K decisions (events around every launch '
                            'slow the step ~5%; the timed pass times the render launches only)',
@@ -807,12 +970,17 @@ def main():
                     data='synthetic (seeded NROM cart synth00, random legal moves)',
                     config=workload_config(args, world), envs_timed=r['envs'],
                     cpu_baseline=dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
-                                      sample=sample, cpu=cpu_model()),
+                                      sample=sample, cpu=cpu_model(),
+                                      core_us_per_env_frame=round(r['cores'] * 1e6 / (4 * r['value']), 1),
+                                      split_one_thread=r['split']),
                     e2e=dict(value=round(r['value'], 1), unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
         print(json.dumps(line), flush=True)
         return
     if args.workload == 'stem':
         print(json.dumps(stem_arm(args)), flush=True)
+        return
+    if args.workload == 'learner':
+        print(json.dumps(learner_arm(args)), flush=True)
         return
     if args.workload == 'config5':
         res = config5_arm(args)
@@ -824,7 +992,8 @@ def main():
         try:
             r = run_cpu_leg(args, seconds=args.cpu_seconds)
             cpu = dict(value=round(r['value'], 1), unit=UNIT, cores=r['cores'], kind='port',
-                       sample=f"{r['steps']} decisions x {args.envs} envs (config 2 workload)", cpu=cpu_model())
+                       sample=f"{r['steps']} decisions x {args.envs} envs (config 2 workload)", cpu=cpu_model(),
+                       core_us_per_env_frame=round(r['cores'] * 1e6 / (4 * r['value']), 1), split_one_thread=r['split'])
         except Exception as ex:   # reported, never silent
             cpu = dict(value=None, unit=UNIT, cores=os.cpu_count(), kind='port', sample=f'failed: {ex}'[:200])
     res = gpu_arm(args)

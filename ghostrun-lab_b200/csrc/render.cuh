@@ -122,6 +122,7 @@ struct RState {
     u32 sh0, sh1, at;    // tile shift registers (low 16 bits) and attribute latch
     u32 blurp, spork, hit, sphitx, sphitmask, hit_x;
     u32 fb;              // which of the two sprite buffers is `fetched`
+    u32 fsame;           // 1: `fetched` holds what `drawn` holds (no fetch since the last copy), W.spr[fb ^ 1]
     u32 spal[4];         // sprite palette taken at RefreshSprites (& 0x3F)
     u32 lazy, lz_v, lz_ctrl, lz_mir;   // shift registers not yet materialised: fetches 32 / 33 of the line at lz_v
     u32 lz_saved;        // W.lzchr holds the lazy line's CHR pages (saved at the first CHR write after that line)
@@ -466,6 +467,7 @@ struct Renderer {
         const int start = l * 341 - 16;
         s.sphitx = 0x100u;
         if (s.mask & 0x18u) {
+            s.fsame = 0;
             RSprites& f = W.spr[s.fb];
             const u32 c = s.ctrl;
             const u32 hgt = (c & 0x20u) ? 16u : 8u;
@@ -534,12 +536,18 @@ struct Renderer {
         while (s.next_t < start + 341) next_event(true);
         if (s.mask & 0x10u) {
             s.spork = 0;
-            const RSprites& f = W.spr[s.fb];
-            if (s.nf != 0) {
-                s.fb ^= 1u;    // drawn = fetched (the other buffer becomes the next fetch target)
-                const u32 t = s.nd;
-                s.nd = s.nf;
-                s.nf = t;
+            // FCEUmm keeps one fetch buffer and copies it to the drawn one: without a fetch on this line (rendering
+            // off at its end) the copy repeats the last fetch, which the drawn buffer already holds
+            const bool same = s.fsame != 0;
+            const RSprites& f = W.spr[same ? s.fb ^ 1u : s.fb];
+            if ((same ? s.nd : s.nf) != 0) {
+                if (!same) {
+                    s.fb ^= 1u;    // drawn = fetched (the other buffer becomes the next fetch target)
+                    const u32 t = s.nd;
+                    s.nd = s.nf;
+                    s.nf = t;
+                    s.fsame = 1;
+                }
                 for (int q = 0; q < 4; ++q) s.spal[q] = W.pal[4 + q] & 0x3F3F3F3Fu;
                 if (s.blurp && !s.hit && f.opq0) {
                     s.sphitx = f.meta[0] >> 8;
@@ -694,7 +702,7 @@ struct Renderer {
             s.lz_saved = 1;
         }
         // the sprites drawn on line l: fetched at the end of line l - 1 and refreshed there
-        s.fb = 0; s.nd = 0; s.nf = 0; s.spork = 0;
+        s.fb = 0; s.nd = 0; s.nf = 0; s.spork = 0; s.fsame = 0;
         if (l >= 1) {
             const uint2 re = F.rec[l - 1];
             if ((re.y & 0x18u) && (re.y & (1u << 16))) {
@@ -1147,7 +1155,7 @@ struct Renderer {
         s.mirroring = h[5] & 0xFFu;
         s.sh0 = s.sh1 = s.at = 0;
         s.blurp = 0; s.spork = 0; s.hit = 0; s.sphitx = 0x100u; s.sphitmask = 0; s.hit_x = 0;
-        s.fb = 0;
+        s.fb = 0; s.fsame = 0;
         s.spal[0] = s.spal[1] = s.spal[2] = s.spal[3] = 0;
         s.lazy = 0; s.lz_v = 0; s.lz_ctrl = 0; s.lz_mir = 0; s.lz_saved = 0;
         s.nf = 0; s.nd = 0;

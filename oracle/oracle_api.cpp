@@ -2,6 +2,7 @@
 // (rl/csrc/rlenv_api.h:8-47, implemented by rl/csrc/rlenv_cpu.cpp:1-192 in the reference). Envs run under OpenMP
 // `parallel for schedule(dynamic, 1)` as in rl/csrc/rlenv_cpu.cpp:35-45. Only tests/, __graft_entry__.smoke() and
 // bench.py's cpu_baseline leg load this library; the product never does.
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -310,6 +311,45 @@ int oracle_run_frames(const std::uint8_t* rom, std::size_t rom_size, const std::
                                     emph_out + static_cast<std::size_t>(f) * kObsH);
             if (dump_out) dump_console(c, m, dump_out + static_cast<std::size_t>(f) * kDumpBytes);
         }
+        return 0;
+    } catch (const std::exception& ex) {
+        g_error = ex.what();
+        return 1;
+    }
+}
+
+// Per-frame cost split on one thread, the reference's method (rl/bench/split_cpu.cpp:1-30): the boot frames, then
+// `frames` frames with LCG pads (x = x * 1103515245 + 12345, pad = (x >> 16) & 0xF3), each timed as emulating the
+// frame (step_until) and drawing it (render_obs). out[0] = emulate us / frame, out[1] = draw us / frame.
+int oracle_split_frames(const std::uint8_t* rom, std::size_t rom_size, const std::uint8_t* boot, int boot_n, int frames,
+                        double* out) {
+    try {
+        const Cart c = parse_ines(rom, rom_size);
+        Console m;
+        cold_reset(c, m);
+        u64 target = kVblankDot;
+        for (int f = 0; f < boot_n; ++f) {
+            m.pad = boot[f];
+            step_until(c, m, target);
+            target += kFrameDots;
+        }
+        std::vector<std::uint8_t> pix(kObsPixels), em(kObsH);
+        double te = 0, tr = 0;
+        unsigned x = 1;
+        for (int i = 0; i < frames; ++i) {
+            x = x * 1103515245u + 12345u;
+            m.pad = static_cast<u8>((x >> 16) & 0xF3);
+            const auto t0 = std::chrono::steady_clock::now();
+            step_until(c, m, target);
+            target += kFrameDots;
+            const auto t1 = std::chrono::steady_clock::now();
+            render_obs(c, m, pix.data(), em.data());
+            const auto t2 = std::chrono::steady_clock::now();
+            te += std::chrono::duration<double>(t1 - t0).count();
+            tr += std::chrono::duration<double>(t2 - t1).count();
+        }
+        out[0] = 1e6 * te / frames;
+        out[1] = 1e6 * tr / frames;
         return 0;
     } catch (const std::exception& ex) {
         g_error = ex.what();

@@ -27,12 +27,21 @@ def oracle_lib() -> Path:
     return lib
 
 
+def reference_tree():
+    """The reference source tree (read only, test infrastructure): the environment variable REF, else a `reference`
+    directory beside the repository; None when neither holds the reference's rl/csrc/host_api.cpp."""
+    import os
+    ref = Path(os.environ.get('REF') or ROOT.parent / 'reference')
+    return ref if (ref / 'rl' / 'csrc' / 'host_api.cpp').exists() else None
+
+
 def reference_host_lib():
     """The reference's own controller / reward10 host library (oracle/_ref, compiled from the reference tree when it is
     present), or None."""
     lib = ORACLE / '_ref' / 'librl_host.so'
-    if not lib.exists() and Path('/root/reference/rl/csrc/host_api.cpp').exists():
-        subprocess.run(['make', '-C', str(ORACLE), 'ref'], check=True, capture_output=True)
+    ref = reference_tree()
+    if not lib.exists() and ref is not None:
+        subprocess.run(['make', '-C', str(ORACLE), 'ref', f'REF={ref}'], check=True, capture_output=True)
     return lib if lib.exists() else None
 
 

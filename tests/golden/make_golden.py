@@ -13,6 +13,7 @@
 from __future__ import annotations
 
 import argparse
+import os
 import ctypes
 import sys
 from pathlib import Path
@@ -182,7 +183,8 @@ def rewards(ref):
 
 if __name__ == '__main__':
     ap = argparse.ArgumentParser()
-    ap.add_argument('--ref', default='/root/reference')
+    ap.add_argument('--ref', default=os.environ.get('REF') or str(ROOT.parent / 'reference'),
+                    help='the reference source tree (default: $REF, else a `reference` directory beside the repository)')
     a = ap.parse_args()
     import subprocess
     subprocess.run(['make', '-C', str(ROOT / 'oracle'), 'ref', f'REF={a.ref}'], check=True)

@@ -242,6 +242,59 @@ def test_legal_moves_sampler(gpu_lib_path):
         choice = unpack(d)[p]                      # [2000, n]
         for env in range(e.n):
             allowed = np.flatnonzero(masks[env, a:b])
-            freq = np.bincount(choice[:, env].numpy(), minlength=b - a)[allowed] / 2000
+            counts = np.bincount(choice[:, env].numpy(), minlength=b - a)
+            assert counts[allowed].sum() == 2000, (p, env, counts)   # nothing outside the allowed choices
+            freq = counts[allowed] / 2000
             assert np.all(np.abs(freq - 1 / len(allowed)) < 0.06), (p, env, freq)
-            assert freq.sum() == 1.0
+
+
+@pytest.mark.gpu
+def test_learner_gather_from_pinned_host(gpu_lib_path):
+    """The learner half of the 6-bit picture format (rl/train.py:262-295 HostObs, rl/csrc/rlenv.cu:369-421): every
+    decision's packed pictures and emphasis go into a pinned host region [T, N, row] (rl_host_alloc,
+    rl_memcpy_async); a minibatch of envs is gathered back to the device from that host region, one copy-engine 2-D
+    copy per env (rl_gather_envs), and unpacked (rl_unpack6). The result equals the pictures and emphasis an
+    identical env (same seed and moves) wrote unpacked, decision by decision."""
+    N, T = 48, 16
+    row, erow = 4 * 224 * 180, 4 * 224
+    kw = dict(lib_path=gpu_lib_path, seed=21, sticky=True, idle_max=30, dropout=True)
+    a = RlEnv({'synth00': 24, 'synth02': 24}, device='cuda', **kw)   # NROM and MMC1 (CHR-RAM) rows
+    b = RlEnv({'synth00': 24, 'synth02': 24}, device='cuda', **kw)
+    packed = torch.zeros(N, 4, 224, 180, dtype=torch.uint8, device='cuda')
+    a.bind_obs_pack6(packed)
+    lib = a.lib
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    host = lib.rl_host_alloc(T * N * row)
+    host_e = lib.rl_host_alloc(T * N * erow)
+    assert host and host_e
+    try:
+        a.start(); b.start()
+        gen = torch.Generator().manual_seed(21)
+        want_obs, want_emph = [], []
+        for t in range(T):
+            act = random_legal(b.masks.cpu(), gen).cuda()
+            a.actions.copy_(act); b.actions.copy_(act)
+            a.step(); b.step()
+            assert lib.rl_memcpy_async(ctypes.c_void_p(host + t * N * row), ctypes.c_void_p(packed.data_ptr()), N * row, s) == 0
+            assert lib.rl_memcpy_async(ctypes.c_void_p(host_e + t * N * erow), ctypes.c_void_p(a.emph.data_ptr()), N * erow, s) == 0
+            want_obs.append(b.obs.clone()); want_emph.append(b.emph.clone())
+        torch.cuda.synchronize()
+        want_obs, want_emph = torch.stack(want_obs), torch.stack(want_emph)   # [T, N, ...]
+        for envs in (np.array([3, 47, 0, 30, 24, 23], np.int64), np.arange(N, dtype=np.int64)[::-1].copy()):
+            n = len(envs)
+            dst = torch.zeros(T, n, row, dtype=torch.uint8, device='cuda')
+            dst_e = torch.zeros(T, n, erow, dtype=torch.uint8, device='cuda')
+            assert lib.rl_gather_envs(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(host),
+                                      envs.ctypes.data_as(ctypes.c_void_p), n, T, N, row, s) == 0
+            assert lib.rl_gather_envs(ctypes.c_void_p(dst_e.data_ptr()), ctypes.c_void_p(host_e),
+                                      envs.ctypes.data_as(ctypes.c_void_p), n, T, N, erow, s) == 0
+            obs = torch.zeros(T, n, 4, 224, 240, dtype=torch.uint8, device='cuda')
+            assert lib.rl_unpack6(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(obs.data_ptr()), obs.numel(), s) == 0
+            torch.cuda.synchronize()
+            idx = torch.from_numpy(envs).cuda()
+            assert torch.equal(obs, want_obs[:, idx]), 'gathered pictures differ from the env\'s own'
+            assert torch.equal(dst_e.view(T, n, 4, 224), want_emph[:, idx]), 'gathered emphasis differs'
+    finally:
+        torch.cuda.synchronize()
+        lib.rl_host_free(ctypes.c_void_p(host))
+        lib.rl_host_free(ctypes.c_void_p(host_e))
