@@ -123,8 +123,9 @@ int rlenv_render_stats(void* h, uint64_t* host_out, int reset, void* stream);
 // n x RLENV_DUMP_BYTES in the rlenv_dump_env layout, synchronous on `stream`. It stages through one file-scope
 // device array of 8 x RLENV_DUMP_BYTES = 184,320 bytes, which every GPU that loads the library holds until exit.
 // rlenv_create does the per-device set-up while device memory is still free (the array's address by
-// cudaGetSymbolAddress, and the dump kernel's code loaded), so the call itself only launches that kernel and copies. All calls and handles on a device share the array; calls whose
-// work overlaps on the GPU (two threads, two streams) race.
+// cudaGetSymbolAddress, and the dump kernel's code loaded), so the call itself only launches that kernel and
+// copies. All calls and handles on a device share the array; calls whose work overlaps on the GPU (two threads,
+// two streams) race.
 #define RLENV_DUMP_NOALLOC_MAX_ENVS 8
 int rlenv_dump_envs_noalloc(void* h, const int* envs, int n, uint8_t* host_out, void* stream);
 
