@@ -20,8 +20,12 @@
 
 namespace gr {
 
+enum : u32 { FC = 1, FZ = 2, FI = 4, FD = 8, FB = 0x10, FU = 0x20, FV = 0x40, FN = 0x80 };
+
 // ------------------------------------------------------------------------------------------------ decode table
-// entry: mode (4 bits) | op << 4 (6 bits) | cycles << 10 (4 bits) | page-cross penalty << 14
+// entry: mode (4 bits) | op << 4 (6 bits) | cycles << 10 (4 bits) | page-cross penalty << 14, and the addressing
+// mode's effective-address recipe for a branch-free computation: length - 1 << 15 (2 bits), index X (bit 17) or Y
+// (bit 18), zero-page wrap (bit 19), 16-bit operand (bit 20), indirect (bit 21: (zp,X), (zp),Y, JMP (ind))
 enum Mode : u32 { M_IMP = 0, M_ACC, M_IMM, M_ZP, M_ZPX, M_ZPY, M_ABS, M_ABSX, M_ABSY, M_IND, M_INDX, M_INDY, M_REL };
 enum Op : u32 {
     O_ILL = 0, O_LDA, O_LDX, O_LDY, O_STA, O_STX, O_STY, O_ADC, O_SBC, O_AND, O_ORA, O_EOR, O_CMP, O_CPX, O_CPY,
@@ -30,7 +34,25 @@ enum Op : u32 {
     O_RTI, O_BRK, O_BPL, O_BMI, O_BVC, O_BVS, O_BCC, O_BCS, O_BNE, O_BEQ
 };
 
-constexpr u32 dec(u32 mode, u32 op, u32 cyc, u32 px = 0) { return mode | (op << 4) | (cyc << 10) | (px << 14); }
+enum : u32 { kDLen = 15, kDX = 1u << 17, kDY = 1u << 18, kDZp = 1u << 19, kDAbs = 1u << 20, kDInd = 1u << 21 };
+constexpr u32 mode_bits(u32 mode) {
+    switch (mode) {
+        case M_IMP: case M_ACC: return 0u << kDLen;
+        case M_IMM: case M_REL: return 1u << kDLen;
+        case M_ZP: return (1u << kDLen) | kDZp;
+        case M_ZPX: return (1u << kDLen) | kDZp | kDX;
+        case M_ZPY: return (1u << kDLen) | kDZp | kDY;
+        case M_ABS: return (2u << kDLen) | kDAbs;
+        case M_ABSX: return (2u << kDLen) | kDAbs | kDX;
+        case M_ABSY: return (2u << kDLen) | kDAbs | kDY;
+        case M_IND: return (2u << kDLen) | kDAbs | kDInd;
+        case M_INDX: return (1u << kDLen) | kDInd | kDX;
+        default: return (1u << kDLen) | kDInd | kDY;   // M_INDY
+    }
+}
+constexpr u32 dec(u32 mode, u32 op, u32 cyc, u32 px = 0) {
+    return mode | (op << 4) | (cyc << 10) | (px << 14) | mode_bits(mode);
+}
 
 struct DecodeTable {
     u32 t[256];
@@ -86,8 +108,6 @@ struct DecodeTable {
     }
 };
 static __constant__ DecodeTable kDecode = DecodeTable();
-
-enum : u32 { FC = 1, FZ = 2, FI = 4, FD = 8, FB = 0x10, FU = 0x20, FV = 0x40, FN = 0x80 };
 
 // ------------------------------------------------------------------------------------------------ small helpers
 
@@ -198,6 +218,7 @@ struct Emu {
     u32 log_n, log_ctl;
     u32 now;
     u32 pend;     // PPU dots run since frame_dot (not yet settled) during step_until
+    u64 dmc_at;   // the DMC's next event cycle (register words R_DMC_EV), kept here for the per-instruction check
     u32 resched;  // MMC3: a store changed what the scanline counter does; the next event is recomputed
     u32 dma;
     u32 slot;     // presentation slot of the frame being emulated
@@ -250,6 +271,7 @@ struct Emu {
         log_ctl = (p2 >> 8) & 0xFF;
         prg_bank = (p2 >> 16) & 0xFF;
         log_n = rw(R_LOGN) & 0xFFFF;
+        dmc_at = rw(R_DMC_EV) | (static_cast<u64>(rw(R_DMC_EV + 1)) << 32);
         dma = 0;
         now = 0;
         pend = 0;
@@ -895,6 +917,7 @@ struct Emu {
             else if (bytes_left == 0) bytes_left = length * 16u + 1u;
             ww(R_DMC_A, bytes_left | (control << 16) | (length << 24));
             ww(R_DMC_EV, 0); ww(R_DMC_EV + 1, 0);
+            dmc_at = 0;
             return;
         }
         if (addr < 0x6000u) return;
@@ -945,11 +968,10 @@ struct Emu {
         ww(R_DMC_B, rate | (full << 8));
         const u64 ev = full ? be : kDmcIdle;
         ww(R_DMC_EV, static_cast<u32>(ev)); ww(R_DMC_EV + 1, static_cast<u32>(ev >> 32));
+        dmc_at = ev;
         return stolen;
     }
-    __device__ __forceinline__ u64 dmc_event() const {
-        return rw(R_DMC_EV) | (static_cast<u64>(rw(R_DMC_EV + 1)) << 32);
-    }
+    __device__ __forceinline__ u64 dmc_event() const { return dmc_at; }
 
     // -------- 6502
     __device__ __forceinline__ void push(u32 v) { ram_wr(0x100u | sp, v); sp = (sp - 1) & 0xFFu; }
@@ -985,40 +1007,21 @@ struct Emu {
             if (mode >= M_IMM) b1 = fetch((pc0 + 1) & 0xFFFFu);
             if (mode >= M_ABS && mode <= M_IND) b2 = fetch((pc0 + 2) & 0xFFFFu);
         }
-        // ---- operand / effective address
-        u32 ea = 0, val = 0;
-        bool cross = false;
-        switch (mode) {
-            case M_IMP: case M_ACC: pc = pc0 + 1; break;
-            case M_IMM: pc = pc0 + 2; break;
-            case M_REL: pc = pc0 + 2; break;
-            case M_ZP: ea = b1; pc = pc0 + 2; break;
-            case M_ZPX: ea = (b1 + x) & 0xFFu; pc = pc0 + 2; break;
-            case M_ZPY: ea = (b1 + y) & 0xFFu; pc = pc0 + 2; break;
-            case M_INDX: {
-                const u32 z = (b1 + x) & 0xFFu;
-                ea = ram_rd(z) | (ram_rd((z + 1) & 0xFFu) << 8);
-                pc = pc0 + 2;
-                break;
-            }
-            case M_INDY: {
-                const u32 base = ram_rd(b1) | (ram_rd((b1 + 1) & 0xFFu) << 8);
-                ea = (base + y) & 0xFFFFu;
-                cross = ((base ^ ea) & 0xFF00u) != 0;
-                pc = pc0 + 2;
-                break;
-            }
-            default: {   // ABS, ABSX, ABSY, IND
-                const u32 base = b1 | (b2 << 8);
-                const u32 idx = mode == M_ABSX ? x : mode == M_ABSY ? y : 0u;
-                ea = (base + idx) & 0xFFFFu;
-                cross = ((base ^ ea) & 0xFF00u) != 0;
-                pc = pc0 + 3;
-                break;
+        // ---- operand / effective address: selects from the decode entry's recipe (no branch but the rare
+        // indirect modes), the operand bytes fetched speculatively above
+        u32 val = 0;
+        pc = (pc0 + 1u + ((d >> kDLen) & 3u)) & 0xFFFFu;
+        const u32 idx = (d & kDX) ? x : ((d & kDY) ? y : 0u);
+        u32 base = (d & kDAbs) ? (b1 | (b2 << 8)) : b1;
+        if (d & kDInd) {   // (zp,X): pointer at zp b1 + X; (zp),Y: pointer at zp b1, + Y; JMP (ind): the operand
+            if (mode != M_IND) {
+                const u32 z = (d & kDX) ? ((b1 + x) & 0xFFu) : b1;
+                base = ram_rd(z) | (ram_rd((z + 1) & 0xFFu) << 8);
             }
         }
+        u32 ea = (base + ((d & kDInd) && (d & kDX) ? 0u : idx)) & ((d & kDZp) ? 0xFFu : 0xFFFFu);
+        const bool cross = ((base ^ ea) & 0xFF00u) != 0;
         if ((d >> 14) & cross) ++cyc;
-        pc &= 0xFFFFu;
         // operand value for the reading operations
         const bool reads = (opn >= O_LDA && opn <= O_LDY) || (opn >= O_ADC && opn <= O_DEC);
         if (reads) val = mode == M_IMM ? b1 : mode == M_ACC ? a : rd(ea);
@@ -1153,13 +1156,16 @@ struct Emu {
         const u32 logged = log_n;
         const Step s = step6502();
         if (s.illegal) { ppu_cycles = 0; return s; }
-        if (log_n != logged) {
-            u32* bank = writing_bank();
-            const u32 c = (s.cycles > 15u ? 15u : s.cycles) << 17;
-            for (u32 i = logged; i < log_n && i < kLogEv; ++i) bank[kLogHdr + 2 * i] |= c;
+        // the rare work after an instruction (frame-log cycle stamps, OAM DMA, a DMC fetch) behind one branch
+        if ((log_n != logged) | (dma != 0u) | (cycles >= dmc_event())) {
+            if (log_n != logged) {
+                u32* bank = writing_bank();
+                const u32 c = (s.cycles > 15u ? 15u : s.cycles) << 17;
+                for (u32 i = logged; i < log_n && i < kLogEv; ++i) bank[kLogHdr + 2 * i] |= c;
+            }
+            if (dma) { dma = 0; cycles += 513u + static_cast<u32>(cycles & 1u); }
+            if (cycles >= dmc_event()) cycles += dmc_service(cycles, true);
         }
-        if (dma) { dma = 0; cycles += 513u + static_cast<u32>(cycles & 1u); }
-        if (cycles >= dmc_event()) cycles += dmc_service(cycles, true);
         ppu_cycles = static_cast<u32>(cycles - before) * 3u;
         return s;
     }

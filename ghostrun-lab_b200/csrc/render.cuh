@@ -832,7 +832,19 @@ struct Renderer {
                     // after the stretch: a line with a write inside its drawn part is drawn here, exactly (MMC3,
                     // whose IRQ handlers split the screen; the other boards leave such frames to k_render_seq)
                     const int ls = l + run;
-                    if constexpr (kSplitLines) split = (ls < kLines && w.next_t < ls * 341 - 16 + 272) ? 1u : 0u;
+                    if constexpr (kSplitLines) {
+                        split = (ls < kLines && w.next_t < ls * 341 - 16 + 272) ? 1u : 0u;
+                        // FCEUmm draws one tile more before a mid-line write while sprite 0 is on the line and has
+                        // not hit yet (replay_update's sphitx rule, patch:1593-1596), so where the write lands
+                        // depends on the frame's sprite-0 state, which only the sequential renderer follows: a
+                        // split line that sprite 0 may reach (fetched at the end of the line above, 8x16 at most;
+                        // lane 0 holds OAM entry 0) sends the frame there
+                        if (split && static_cast<u32>(ls - 1 - static_cast<int>(spA & 0xFFu)) < 16u) {
+                            w.seq = 1;
+                            split = 0;
+                            run = 0;
+                        }
+                    }
                 }
             }
             run = __shfl_sync(0xFFFFFFFFu, run, 0);

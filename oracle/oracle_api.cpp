@@ -288,6 +288,19 @@ int oracle_dump_env(void* h, int ge, std::uint8_t* out) {
 }
 
 // Per-env RL scalars: target, ep_frame, episode, fault, sticky_ctr.
+// Both frame-log banks of global env ge (2 x 528 words: the shown one first, then the other, which after a decision
+// still holds the frame before the shown one; nothing runs between a frame's vblank stop and the next decision).
+int oracle_log_banks(void* h, int ge, std::uint32_t* out) {
+    World& w = static_cast<Handle*>(h)->w;
+    if (ge < 0 || ge >= w.total) { g_error = "log banks: bad env"; return 1; }
+    std::size_t gi = 0;
+    while (ge >= w.games[gi].offset + w.games[gi].n) ++gi;
+    const Console& m = w.games[gi].con[ge - w.games[gi].offset];
+    std::memcpy(out, log_bank_ptr(m, m.log_bank & 1u), 4 * kLogBank);
+    std::memcpy(out + kLogBank, log_bank_ptr(m, (m.log_bank & 1u) ^ 1u), 4 * kLogBank);
+    return 0;
+}
+
 int oracle_env_scalars(void* h, int ge, std::uint64_t* out) {
     World& w = static_cast<Handle*>(h)->w;
     const PerEnv& pe = w.env[ge];

@@ -27,7 +27,12 @@ def _compare(g, c, t):
         a, b = getattr(g, k).cpu(), getattr(c, k)
         if not torch.equal(a, b):
             bad = (a != b).reshape(len(a), -1).any(1).nonzero().flatten().tolist()
-            raise AssertionError(f'step {t}: output {k} differs in envs {bad[:8]} ({len(bad)} envs)')
+            where = ''
+            if k == 'obs':   # the first differing env's frames and picture rows
+                d = (a[bad[0]] != b[bad[0]])
+                where = '; env %d: ' % bad[0] + ', '.join(
+                    f'frame {f} rows {d[f].any(1).nonzero().flatten().tolist()[:8]}' for f in range(d.shape[0]) if d[f].any())
+            raise AssertionError(f'step {t}: output {k} differs in envs {bad[:8]} ({len(bad)} envs){where}')
     d = c.done.bool()
     if t and d.any():
         assert torch.equal(g.info.cpu()[d], c.info[d]), f'step {t}: info differs'
