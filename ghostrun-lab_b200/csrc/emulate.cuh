@@ -1170,9 +1170,34 @@ struct Emu {
         return s;
     }
 
+    // Dots from frame_dot to the next scanline-counter clock (the reference's batch_ppu_dots_until_scanline_clock,
+    // patch:1881-1902 and its short-frame use, patch:2061-2064).
+    __device__ __forceinline__ u32 dots_to_counter_clock() const {
+        const u32 cur = frame_dot, line = cur / kDots, dot = cur % kDots;
+        u32 d;
+        if (line < 240u) {
+            d = dot < kMmc3VisibleClock ? kMmc3VisibleClock - dot
+              : line + 1u < 240u ? kDots - dot + kMmc3VisibleClock : (261u - line) * kDots + kMmc3PreClock - dot;
+        } else if (line < 261u) {
+            d = (261u - line) * kDots + kMmc3PreClock - dot;
+        } else {
+            d = dot < kMmc3PreClock ? kMmc3PreClock - dot : kDots - dot + kMmc3VisibleClock;
+        }
+        if ((log_ctl & kLcShort) && cur + d >= kFrameDots) d -= 1u;
+        return d;
+    }
+
     __device__ __forceinline__ void fast_forward() {
         if (nmi) return;
-        const u32 jumps = (dots_to_event() + 8u) / 9u;
+        u32 to = dots_to_event();
+        if constexpr (BOARD == kMmc3) {
+            // The reference schedules every counter clock as an event, so a skip ends at the next clock. Only the clock
+            // that raises the IRQ is an event here; that is the same wherever no IRQ can be taken, but an IRQ the
+            // settle before this skip raised (the jump crossed its clock) is taken after the next clock, not after the
+            // next other event.
+            if ((rw(R_IO) >> 24) && !(p & FI)) to = min(to, dots_to_counter_clock());
+        }
+        const u32 jumps = (to + 8u) / 9u;
         if (jumps == 0) return;
         const u32 cc = jumps * 3u;
         cycles += cc;

@@ -1067,7 +1067,7 @@ struct Renderer {
                 for (int q = 0; q < 8; ++q) px[q] = bdw;
             }
             // ---- sprites over this lane's 32 pixels (CopySprites, patch:1615-1640: the first in OAM order wins)
-            const u32 nmax = __reduce_max_sync(0xFFFFFFFFu, nsp);
+            const u32 nmax = any ? __reduce_max_sync(0xFFFFFFFFu, nsp) : 0u;   // `any` is warp-uniform
             if (nmax) {
                 u32 n0 = 0, n1 = 0, n2 = 0, n3 = 0, a0 = 0, a1 = 0, a2 = 0, a3 = 0, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
                 const int x0 = 8 + 32 * static_cast<int>(j);
