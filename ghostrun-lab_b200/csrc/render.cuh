@@ -51,7 +51,7 @@ struct FrameWalk {   // per frame, shared memory
     //             palette version at the line end << 20
     uint2 rec[kObsY0 + kObsH];
     u32 pal[kWalkVers][8];       // palette RAM per version
-    uint4 bgp[kWalkVers];        // background sub-palettes as drawn: colour 0 = backdrop | 0x40, & 0x3F
+    uint4 bgp[kWalkVers];        // background sub-palettes as drawn: colour 0 = backdrop, & 0x3F (no marker bit)
     uint4 spal[kWalkVers];       // sprite sub-palettes & 0x3F
     u32 chr[kWalkVers][8];       // CHR pages per version
     u32 seq;                     // 1: the frame takes the sequential path (Renderer::draw)
@@ -102,8 +102,25 @@ __device__ __forceinline__ u32 pal_lookup4(u32 sel16, u32 p0, u32 p1, u32 p2, u3
     return (r1 & ~m) | (r2 & m);
 }
 
+// prmt.b32 in its default mode (PTX ISA, prmt): a selector nibble with bit 3 set gives the sign bit of the byte its
+// low 3 bits select, replicated over the target byte, so such a byte below 0x80 reads 0.
+__device__ __forceinline__ u32 prmt_signed(u32 a, u32 b, u32 s) {
+    u32 r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(s));
+    return r;
+}
+
+// The same lookup for palette bytes below 0x80 in two permutes: (p0, p1) serve the nibbles whose attribute bit 1 is
+// clear and read 0 where it is set; (p2, p3) take the nibbles with bit 3 flipped (sx = s ^ 0x8888), the other half.
+__device__ __forceinline__ u32 pal_lookup4s(u32 s, u32 sx, u32 p0, u32 p1, u32 p2, u32 p3) {
+    return prmt_signed(p0, p1, s) | prmt_signed(p2, p3, sx);
+}
+
 // nibble mask (4 nibbles, each 0 or 0xF, low 16 bits) -> byte mask
 __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0xFFFFFFFFu, nm16 & 0x4444u); }
+
+// 4 pixel nibbles (colour | attribute << 2, low 16 bits) -> 0xFF where the colour is not 0 (opaque background)
+__device__ __forceinline__ u32 nib_opaque_bytes(u32 s16) { return nib_to_bytes((s16 | (s16 >> 1)) << 2); }
 
 // 4 colour numbers (bytes <= 0x3F) -> their 24-bit 6-bit group in bits 0-23 (rl/csrc/rlenv.cu:126-134 layout) with
 // leftovers in bits 24-25, which the joins of groups into words mask off: two shift + merge steps.
@@ -573,7 +590,7 @@ struct Renderer {
     }
     __device__ static void derive(FrameWalk& F, u32 pv) {
         const u32* p = F.pal[pv];
-        const u32 bd = (p[0] & 0x3Fu) | 0x40u;
+        const u32 bd = p[0] & 0x3Fu;
         F.bgp[pv] = make_uint4((p[0] & 0x3F3F3F00u) | bd, (p[1] & 0x3F3F3F00u) | bd, (p[2] & 0x3F3F3F00u) | bd,
                                (p[3] & 0x3F3F3F00u) | bd);
         F.spal[pv] = make_uint4(p[4] & 0x3F3F3F3Fu, p[5] & 0x3F3F3F3Fu, p[6] & 0x3F3F3F3Fu, p[7] & 0x3F3F3F3Fu);
@@ -935,7 +952,7 @@ struct Renderer {
         } else {
             sel = chr_sel(pages, (t << 4) + f.vrow);
         }
-        return sel | (attr * 0x44444444u);
+        return sel + attr * 0x44444444u;   // disjoint bits: one multiply-add
     }
 
     // ---- phase 2 (the whole warp): draw frame f of env ge from its walk, 4 lines at a time: lane group g = lane / 8
@@ -951,11 +968,12 @@ struct Renderer {
         sb = beh ? (sb | om) : (sb & ~om);
         (void)m;
     }
-    __device__ __forceinline__ static u32 sprite_mix(u32 bg, u32 sn16, u32 sa16, u32 sb16, const uint4& sp) {
-        const u32 c = pal_lookup4(sn16, sp.x, sp.y, sp.z, sp.w);
+    // bgs16: the 4 background pixels' nibbles (0 where the background is off); a sprite behind the background shows
+    // where the background colour is 0
+    __device__ __forceinline__ static u32 sprite_mix(u32 bg, u32 bgs16, u32 sn16, u32 sa16, u32 sb16, const uint4& sp) {
+        const u32 c = pal_lookup4s(sn16, sn16 ^ 0x8888u, sp.x, sp.y, sp.z, sp.w);
         const u32 any = nib_to_bytes(sa16), beh = nib_to_bytes(sb16);
-        const u32 tr = ((bg & 0x40404040u) >> 6) * 0xFFu;
-        const u32 use = any & (~beh | tr);
+        const u32 use = any & ~(beh & nib_opaque_bytes(bgs16));
         return (bg & ~use) | (c & use);
     }
     __device__ void draw_fast(u32 ge, u32 f, const FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
@@ -1056,12 +1074,13 @@ struct Renderer {
                 s0 = __funnelshift_r(c0, c1, x4); s1 = __funnelshift_r(c1, c2, x4);
                 s2 = __funnelshift_r(c2, c3, x4); s3 = __funnelshift_r(c3, c4, x4);
             }
-            u32 px[8];   // colour bytes (0x40 = background colour 0), 4 pixels per word
+            u32 px[8];   // colour bytes (<= 0x3F), 4 pixels per word
             if (bg) {
-                px[0] = pal_lookup4(s0, P.x, P.y, P.z, P.w); px[1] = pal_lookup4(s0 >> 16, P.x, P.y, P.z, P.w);
-                px[2] = pal_lookup4(s1, P.x, P.y, P.z, P.w); px[3] = pal_lookup4(s1 >> 16, P.x, P.y, P.z, P.w);
-                px[4] = pal_lookup4(s2, P.x, P.y, P.z, P.w); px[5] = pal_lookup4(s2 >> 16, P.x, P.y, P.z, P.w);
-                px[6] = pal_lookup4(s3, P.x, P.y, P.z, P.w); px[7] = pal_lookup4(s3 >> 16, P.x, P.y, P.z, P.w);
+                const u32 x0 = s0 ^ 0x88888888u, x1 = s1 ^ 0x88888888u, x2 = s2 ^ 0x88888888u, x3 = s3 ^ 0x88888888u;
+                px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w); px[1] = pal_lookup4s(s0 >> 16, x0 >> 16, P.x, P.y, P.z, P.w);
+                px[2] = pal_lookup4s(s1, x1, P.x, P.y, P.z, P.w); px[3] = pal_lookup4s(s1 >> 16, x1 >> 16, P.x, P.y, P.z, P.w);
+                px[4] = pal_lookup4s(s2, x2, P.x, P.y, P.z, P.w); px[5] = pal_lookup4s(s2 >> 16, x2 >> 16, P.x, P.y, P.z, P.w);
+                px[6] = pal_lookup4s(s3, x3, P.x, P.y, P.z, P.w); px[7] = pal_lookup4s(s3 >> 16, x3 >> 16, P.x, P.y, P.z, P.w);
             } else {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) px[q] = bdw;
@@ -1095,15 +1114,16 @@ struct Renderer {
                 }
                 if (a0 | a1 | a2 | a3) {
                     const uint4 sp = F.spal[(F.rec[l - 1].y >> 20) & 3u];
-                    if (a0) { px[0] = sprite_mix(px[0], n0, a0, b0, sp); px[1] = sprite_mix(px[1], n0 >> 16, a0 >> 16, b0 >> 16, sp); }
-                    if (a1) { px[2] = sprite_mix(px[2], n1, a1, b1, sp); px[3] = sprite_mix(px[3], n1 >> 16, a1 >> 16, b1 >> 16, sp); }
-                    if (a2) { px[4] = sprite_mix(px[4], n2, a2, b2, sp); px[5] = sprite_mix(px[5], n2 >> 16, a2 >> 16, b2 >> 16, sp); }
-                    if (a3) { px[6] = sprite_mix(px[6], n3, a3, b3, sp); px[7] = sprite_mix(px[7], n3 >> 16, a3 >> 16, b3 >> 16, sp); }
+                    if (a0) { px[0] = sprite_mix(px[0], s0, n0, a0, b0, sp); px[1] = sprite_mix(px[1], s0 >> 16, n0 >> 16, a0 >> 16, b0 >> 16, sp); }
+                    if (a1) { px[2] = sprite_mix(px[2], s1, n1, a1, b1, sp); px[3] = sprite_mix(px[3], s1 >> 16, n1 >> 16, a1 >> 16, b1 >> 16, sp); }
+                    if (a2) { px[4] = sprite_mix(px[4], s2, n2, a2, b2, sp); px[5] = sprite_mix(px[5], s2 >> 16, n2 >> 16, a2 >> 16, b2 >> 16, sp); }
+                    if (a3) { px[6] = sprite_mix(px[6], s3, n3, a3, b3, sp); px[7] = sprite_mix(px[7], s3 >> 16, n3 >> 16, a3 >> 16, b3 >> 16, sp); }
                 }
             }
-            const u32 keep = ((mask & 1u) && (mask & 0x18u)) ? 0x30303030u : 0x3F3F3F3Fu;
+            if ((mask & 1u) && (mask & 0x18u)) {   // greyscale
 #pragma unroll
-            for (int q = 0; q < 8; ++q) px[q] &= keep;
+                for (int q = 0; q < 8; ++q) px[q] &= 0x30303030u;
+            }
             const int y = l - kObsY0;
             bool exact = false;
             if constexpr (kSplitLines) exact = ((F.split[l >> 5] >> (l & 31)) & 1u) != 0u;   // drawn by the walk
@@ -1115,15 +1135,16 @@ struct Renderer {
             } else {
                 u32 gq[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);   // px bytes are <= 0x3F (keep mask)
+                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);   // px bytes are <= 0x3F
+                // the 3-byte groups joined into words: one byte permute per word (bytes 3 of the groups left out)
                 u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3) + 24u * j);
-                row[0] = (gq[0] & 0xFFFFFFu) | (gq[1] << 24);
-                row[1] = ((gq[1] >> 8) & 0xFFFFu) | (gq[2] << 16);
-                row[2] = ((gq[2] >> 16) & 0xFFu) | (gq[3] << 8);
+                row[0] = __byte_perm(gq[0], gq[1], 0x4210);
+                row[1] = __byte_perm(gq[1], gq[2], 0x5421);
+                row[2] = __byte_perm(gq[2], gq[3], 0x6542);
                 if (j < 7) {
-                    row[3] = (gq[4] & 0xFFFFFFu) | (gq[5] << 24);
-                    row[4] = ((gq[5] >> 8) & 0xFFFFu) | (gq[6] << 16);
-                    row[5] = ((gq[6] >> 16) & 0xFFu) | (gq[7] << 8);
+                    row[3] = __byte_perm(gq[4], gq[5], 0x4210);
+                    row[4] = __byte_perm(gq[5], gq[6], 0x5421);
+                    row[5] = __byte_perm(gq[6], gq[7], 0x6542);
                 }
             }
             __syncwarp();   // sbuf is rewritten by the next iteration
