@@ -51,11 +51,12 @@ struct FrameWalk {   // per frame, shared memory
     //             palette version at the line end << 20
     uint2 rec[kObsY0 + kObsH];
     u32 pal[kWalkVers][8];       // palette RAM per version
-    uint4 bgp[kWalkVers];        // background sub-palettes as drawn: colour 0 = backdrop, & 0x3F (no marker bit)
+    uint4 bgp[kWalkVers];        // background sub-palettes as drawn: colour 0 = backdrop, colours 1-3 | 0x40
     uint4 spal[kWalkVers];       // sprite sub-palettes & 0x3F
     u32 chr[kWalkVers][8];       // CHR pages per version
     u32 seq;                     // 1: the frame takes the sequential path (Renderer::draw)
     u32 split[8];                // bit l: line l was drawn exactly by the walk (a write inside its drawn part)
+    alignas(16) u8 rows[4][256]; // draw_fast: the 4 lines of an iteration with sprites, byte x - 8 = screen x
 };
 
 struct RenderArgs {
@@ -119,8 +120,6 @@ __device__ __forceinline__ u32 pal_lookup4s(u32 s, u32 sx, u32 p0, u32 p1, u32 p
 // nibble mask (4 nibbles, each 0 or 0xF, low 16 bits) -> byte mask
 __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0xFFFFFFFFu, nm16 & 0x4444u); }
 
-// 4 pixel nibbles (colour | attribute << 2, low 16 bits) -> 0xFF where the colour is not 0 (opaque background)
-__device__ __forceinline__ u32 nib_opaque_bytes(u32 s16) { return nib_to_bytes((s16 | (s16 >> 1)) << 2); }
 
 // 4 colour numbers (bytes <= 0x3F) -> their 24-bit 6-bit group in bits 0-23 (rl/csrc/rlenv.cu:126-134 layout) with
 // leftovers in bits 24-25, which the joins of groups into words mask off: two shift + merge steps.
@@ -590,9 +589,9 @@ struct Renderer {
     }
     __device__ static void derive(FrameWalk& F, u32 pv) {
         const u32* p = F.pal[pv];
-        const u32 bd = p[0] & 0x3Fu;
-        F.bgp[pv] = make_uint4((p[0] & 0x3F3F3F00u) | bd, (p[1] & 0x3F3F3F00u) | bd, (p[2] & 0x3F3F3F00u) | bd,
-                               (p[3] & 0x3F3F3F00u) | bd);
+        const u32 bd = p[0] & 0x3Fu;   // colours 1-3 carry bit 6 (opaque background, for sprite priority)
+        F.bgp[pv] = make_uint4((p[0] & 0x3F3F3F00u) | 0x40404000u | bd, (p[1] & 0x3F3F3F00u) | 0x40404000u | bd,
+                               (p[2] & 0x3F3F3F00u) | 0x40404000u | bd, (p[3] & 0x3F3F3F00u) | 0x40404000u | bd);
         F.spal[pv] = make_uint4(p[4] & 0x3F3F3F3Fu, p[5] & 0x3F3F3F3Fu, p[6] & 0x3F3F3F3Fu, p[7] & 0x3F3F3F3Fu);
     }
     __device__ void walk_apply(Walk& w, FrameWalk& F, bool drawing) const {
@@ -938,13 +937,19 @@ struct Renderer {
         f.vrow = ((ctrl & 0x10u) << 8) | fy;
         return f;
     }
-    __device__ __forceinline__ u32 line_tile_p(const LineFetch& f, u32 c, const u32* pages) const {
+    // Fetch c of a line in two parts: the nametable's tile and attribute (the same for the 8 lines of a tile row) as
+    // tile | attr << 8, then the pattern row of this line as colour nibbles with the attribute in bits 2-3.
+    __device__ __forceinline__ u32 line_tile_ta(const LineFetch& f, u32 c) const {
         const u32 cc = f.cx0 + c;
         const u32 col = cc & 31u;
         const u32 base = ((cc >> 5) & 1u) ? f.base_b : f.base_a;
         const u32 t = W.nt[base | f.row | col];
         const u32 ab = W.nt[base | f.arow | (col >> 2)];
         const u32 attr = (ab >> (f.ashift | (col & 2u))) & 3u;
+        return t | (attr << 8);
+    }
+    __device__ __forceinline__ u32 line_tile_sel(const LineFetch& f, u32 ta, const u32* pages) const {
+        const u32 t = ta & 0xFFu;
         u32 sel;
         if constexpr (BOARD == kNrom || BOARD == kUxrom) {
             if (A.chrx_smem) sel = chrx[f.rowsel + t];
@@ -952,7 +957,8 @@ struct Renderer {
         } else {
             sel = chr_sel(pages, (t << 4) + f.vrow);
         }
-        return sel + attr * 0x44444444u;   // disjoint bits: one multiply-add
+        // the attribute in bits 2-3 of every nibble (disjoint from the colour bits): one multiply-add
+        return sel + (ta >> 8) * 0x44444444u;
     }
 
     // ---- phase 2 (the whole warp): draw frame f of env ge from its walk, 4 lines at a time: lane group g = lane / 8
@@ -961,31 +967,14 @@ struct Renderer {
     // l - 1 (FetchSpriteData with line l - 1's control, CHR pages and OAM) when line l - 1 fetched (rendering on)
     // and the refresh at its end had sprites on (which is line l's mask); the walk sends the one case where an older
     // fetch would show to the sequential path. Crop x starts at 8, so the left-column clips never show.
-    __device__ __forceinline__ static void put_sprite(u32 win, u32 m, u32 pw, bool beh, u32& sn, u32& sa, u32& sb) {
-        const u32 om = ((win | (win >> 1)) & 0x11111111u) * 0xFu;
-        sn = (sn & ~om) | ((win | pw) & om);
-        sa |= om;
-        sb = beh ? (sb | om) : (sb & ~om);
-        (void)m;
-    }
-    // bgs16: the 4 background pixels' nibbles (0 where the background is off); a sprite behind the background shows
-    // where the background colour is 0
-    __device__ __forceinline__ static u32 sprite_mix(u32 bg, u32 bgs16, u32 sn16, u32 sa16, u32 sb16, const uint4& sp) {
-        const u32 c = pal_lookup4s(sn16, sn16 ^ 0x8888u, sp.x, sp.y, sp.z, sp.w);
-        const u32 any = nib_to_bytes(sa16), beh = nib_to_bytes(sb16);
-        const u32 use = any & ~(beh & nib_opaque_bytes(bgs16));
-        return (bg & ~use) | (c & use);
-    }
-    __device__ void draw_fast(u32 ge, u32 f, const FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
+    __device__ void draw_fast(u32 ge, u32 f, FrameWalk& F, u8* obs_out, u8* emph_out, bool pack6) {
         if constexpr (!kSplitLines) load_frame(ge, f);   // (boards with exact lines staged it in walk_frame)
         const u32 g = lane >> 3, j = lane & 7u;
         const u32 lt = (1u << lane) - 1u;
-        uint2* sbuf = reinterpret_cast<uint2*>(W.px);   // [4 lines][8 sprites] (colour nibbles, meta)
         // Lines that can show a sprite: one at y is found by the evaluation at the end of lines y..y+h-1 (height h) and
         // drawn on lines y+1..y+h. A superset; iterations whose 4 lines have none skip the sprite work.
         u32* may = reinterpret_cast<u32*>(W.emph);   // 8 words: bit l of the 256-line mask
         u8* vis = W.emph + 32;                       // OAM indices of the sprites that can show, in OAM order
-        u32* ov = reinterpret_cast<u32*>(W.emph + 96);   // per lane: bit r = sprite rank r of its line reaches its pixels
         u32 nv;
         {
             // 8x16 sprites on any line of the frame (control bit 5 in the records): 16 lines per sprite, else 8
@@ -1012,48 +1001,9 @@ struct Renderer {
             nv = __popc(ba) + __popc(bb);
             __syncwarp();
         }
+        u32 key_prev = 0xFFFFFFFFu, ta0 = 0, ta1 = 0, ta2 = 0, ta3 = 0;   // this lane's cached tile row
         for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
-            // ---- sprites of lines l0..l0+3: lane group g evaluates the end of line l0 + g - 1 (the fetch its line
-            // draws) over the visible sprites in OAM order, 8 candidates per round; the first 8 in range are fetched
-            u32 nsp = 0;   // this lane group's sprite count
-            const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;
-            if (any) {
-                ov[lane] = 0u;
-                __syncwarp();
-                const int e = l0 + static_cast<int>(g) - 1;
-                const uint2 re = F.rec[e];
-                const u32 ctrl = ((re.x >> 18) & 7u) << 3;
-                const bool on = (re.y & 0x18u) && (re.y & (1u << 16));
-                const u32 hgt = (ctrl & 0x20u) ? 16u : 8u;
-                const u32* pages = F.chr[(re.y >> 12) & 3u];
-                const u32 vofs = ((ctrl & 0x08u) && !(ctrl & 0x20u)) ? 0x1000u : 0u;
-                for (u32 c0 = 0; c0 < nv; c0 += 8) {   // warp-uniform trip count
-                    const u32 c = c0 + j;
-                    const u32 si = c < nv ? vis[c] : 0u;
-                    const u32 wa = __shfl_sync(0xFFFFFFFFu, spA, si & 31u), wb = __shfl_sync(0xFFFFFFFFu, spB, si & 31u);
-                    const u32 spw = si >= 32u ? wb : wa;
-                    const u32 t = static_cast<u32>(e - static_cast<int>(spw & 0xFFu));
-                    const bool in = on && c < nv && t < hgt;
-                    const u32 gb = (__ballot_sync(0xFFFFFFFFu, in) >> (8u * g)) & 0xFFu;
-                    const u32 rk = nsp + __popc(gb & ((1u << j) - 1u));
-                    if (in && rk < 8) {
-                        const u32 tile = (spw >> 8) & 0xFFu, attr = (spw >> 16) & 0xFFu, xx = spw >> 24;
-                        u32 vadr = hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs;
-                        if (attr & 0x80u) { vadr += 7u; vadr -= t; vadr += (ctrl & 0x20u) >> 1; vadr -= t & 8u; }
-                        else { vadr += t; vadr += t & 8u; }
-                        u32 cw = chr_sel(pages, vadr & 0x1FFFu);
-                        if (attr & 0x40u) cw = nib_reverse(cw);
-                        sbuf[g * 8 + rk] = make_uint2(cw, (attr & 3u) | ((attr & 0x20u) ? 4u : 0u) | (xx << 8));
-                        // the lanes whose 32 pixels (screen x 8 + 32j ..) the sprite's x .. x + 7 reach
-                        const int wlo = (static_cast<int>(xx) - 8) >> 5, whi = (static_cast<int>(xx) - 1) >> 5;
-                        if (wlo >= 0) atomicOr(&ov[g * 8 + static_cast<u32>(wlo)], 1u << rk);
-                        if (whi != wlo && whi >= 0 && whi < 8) atomicOr(&ov[g * 8 + static_cast<u32>(whi)], 1u << rk);
-                    }
-                    nsp += __popc(gb);
-                }
-                nsp = min(nsp, 8u);
-            }
-            __syncwarp();
+            const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;   // warp-uniform
             // ---- background of line l (this lane group's), 32 pixels per lane
             const int l = l0 + static_cast<int>(g);
             const uint2 r = F.rec[l];
@@ -1062,19 +1012,33 @@ struct Renderer {
             const u32 bdw = (P.x & 0xFFu) * 0x01010101u;
             u32 s0 = 0, s1 = 0, s2 = 0, s3 = 0;   // pixel nibbles (colour | attribute << 2), 8 per word
             const bool bg = (mask & 0x08u) != 0;
+            // the tile row of the line (coarse x / y, nametable, page map): unchanged on every lane since the
+            // iteration before (lines without background keep theirs) -> this lane's tiles and attributes are cached
+            const u32 key = bg ? (r.x & 0x0FFFu) | (((r.x >> 21) & 0xFu) << 12) : key_prev;
+            const bool fresh = __any_sync(0xFFFFFFFFu, key != key_prev);
+            key_prev = key;
+            u32 c0 = 0, c1 = 0, c2 = 0, c3 = 0;   // this lane's 4 fetches (0 where the background is off)
             if (bg) {
                 const u32 ctrl = ((r.x >> 18) & 7u) << 3;
                 const u32* pages = F.chr[(r.y >> 12) & 3u];
                 const LineFetch lf = line_fetch_at(r.x & 0x7FFFu, ctrl, (r.x >> 21) & 0xFu);
+                if (fresh) {
+                    ta0 = line_tile_ta(lf, 4 * j + 1); ta1 = line_tile_ta(lf, 4 * j + 2);
+                    ta2 = line_tile_ta(lf, 4 * j + 3); ta3 = line_tile_ta(lf, 4 * j + 4);
+                }
+                c0 = line_tile_sel(lf, ta0, pages); c1 = line_tile_sel(lf, ta1, pages);
+                c2 = line_tile_sel(lf, ta2, pages); c3 = line_tile_sel(lf, ta3, pages);
+            }
+            // fetch 4j + 5 is the next lane's first (a full-warp shuffle, outside the per-line branch); lane 7's last
+            // 16 pixels (screen x 248-263) are not drawn
+            const u32 c4 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
+            if (bg) {
                 const u32 x4 = 4u * ((r.x >> 15) & 7u);
-                const u32 c0 = line_tile_p(lf, 4 * j + 1, pages), c1 = line_tile_p(lf, 4 * j + 2, pages);
-                const u32 c2 = line_tile_p(lf, 4 * j + 3, pages), c3 = line_tile_p(lf, 4 * j + 4, pages);
-                // fetch 4j + 5 is the next lane's first; lane 7's last 16 pixels (screen x 248-263) are not drawn
-                const u32 c4 = __shfl_down_sync(0xFFFFFFFFu, c0, 1);
                 s0 = __funnelshift_r(c0, c1, x4); s1 = __funnelshift_r(c1, c2, x4);
                 s2 = __funnelshift_r(c2, c3, x4); s3 = __funnelshift_r(c3, c4, x4);
             }
-            u32 px[8];   // colour bytes (<= 0x3F), 4 pixels per word
+            // colour bytes, 4 pixels per word: bits 0-5 the colour, bit 6 set where the background colour is not 0
+            u32 px[8];
             if (bg) {
                 const u32 x0 = s0 ^ 0x88888888u, x1 = s1 ^ 0x88888888u, x2 = s2 ^ 0x88888888u, x3 = s3 ^ 0x88888888u;
                 px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w); px[1] = pal_lookup4s(s0 >> 16, x0 >> 16, P.x, P.y, P.z, P.w);
@@ -1085,40 +1049,98 @@ struct Renderer {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) px[q] = bdw;
             }
-            // ---- sprites over this lane's 32 pixels (CopySprites, patch:1615-1640: the first in OAM order wins)
-            const u32 nmax = any ? __reduce_max_sync(0xFFFFFFFFu, nsp) : 0u;   // `any` is warp-uniform
-            if (nmax) {
-                u32 n0 = 0, n1 = 0, n2 = 0, n3 = 0, a0 = 0, a1 = 0, a2 = 0, a3 = 0, b0 = 0, b1 = 0, b2 = 0, b3 = 0;
-                const int x0 = 8 + 32 * static_cast<int>(j);
-                // the sprites that reach this lane's pixels, last in OAM order first (the first one wins)
-                for (u32 m = ov[lane]; m != 0u;) {
-                    const u32 i = 31u - static_cast<u32>(__clz(m));
-                    m &= ~(1u << i);
-                    const uint2 sd = sbuf[g * 8 + i];
-                    const int rel = static_cast<int>(sd.y >> 8) - x0;
-                    const int w = rel >> 3;                  // -1..3: word of the sprite's first pixel
-                    const u32 o = static_cast<u32>(rel) & 7u;
-                    const u32 lo = sd.x << (4 * o), hi = o ? (sd.x >> (32 - 4 * o)) : 0u;
-                    const u32 pw = (sd.y & 3u) * 0x44444444u;
-                    const bool beh = (sd.y & 4u) != 0;
-                    if (w == 0) put_sprite(lo, 0, pw, beh, n0, a0, b0);
-                    if (w == 1) put_sprite(lo, 1, pw, beh, n1, a1, b1);
-                    if (w == 2) put_sprite(lo, 2, pw, beh, n2, a2, b2);
-                    if (w == 3) put_sprite(lo, 3, pw, beh, n3, a3, b3);
-                    if (hi) {
-                        if (w == -1) put_sprite(hi, 0, pw, beh, n0, a0, b0);
-                        if (w == 0) put_sprite(hi, 1, pw, beh, n1, a1, b1);
-                        if (w == 1) put_sprite(hi, 2, pw, beh, n2, a2, b2);
-                        if (w == 2) put_sprite(hi, 3, pw, beh, n3, a3, b3);
+            // ---- sprites of lines l0..l0+3 (CopySprites, patch:1615-1640: the first opaque pixel in OAM order wins,
+            // and shows the background instead where it is behind an opaque background pixel). The lines' pixels go
+            // to shared memory; lane group g evaluates the end of line l - 1 (the fetch line l draws) over the
+            // visible sprites in OAM order, 8 candidates per round, and each lane holding one of the first 8 in range
+            // writes that sprite's pixels as bytes (bit 7: taken by a sprite); within a round the pixels an earlier
+            // sprite of the round covers are found from the other lanes' opaque masks, across rounds from bit 7.
+            if (any) {
+                u8* rowb = F.rows[g];
+                uint4* rw = reinterpret_cast<uint4*>(rowb + 32u * j);
+                rw[0] = make_uint4(px[0], px[1], px[2], px[3]);
+                rw[1] = make_uint4(px[4], px[5], px[6], px[7]);
+                __syncwarp();
+                const int e = l - 1;
+                const uint2 re = F.rec[e];
+                const u32 ctrl = ((re.x >> 18) & 7u) << 3;
+                const bool on = (re.y & 0x18u) && (re.y & (1u << 16));
+                const u32 hgt = (ctrl & 0x20u) ? 16u : 8u;
+                const u32* pages = F.chr[(re.y >> 12) & 3u];
+                const u32 vofs = ((ctrl & 0x08u) && !(ctrl & 0x20u)) ? 0x1000u : 0u;
+                const u32* spal = reinterpret_cast<const u32*>(&F.spal[(re.y >> 20) & 3u]);   // at the end of line e
+                u32 nsp = 0;   // this lane group's sprites so far
+                for (u32 c0 = 0; c0 < nv; c0 += 8) {   // warp-uniform trip count
+                    const u32 c = c0 + j;
+                    const u32 si = c < nv ? vis[c] : 0u;
+                    const u32 wa = __shfl_sync(0xFFFFFFFFu, spA, si & 31u), wb = __shfl_sync(0xFFFFFFFFu, spB, si & 31u);
+                    const u32 spw = si >= 32u ? wb : wa;
+                    const u32 t = static_cast<u32>(e - static_cast<int>(spw & 0xFFu));
+                    const bool in = on && c < nv && t < hgt;
+                    const u32 gb = (__ballot_sync(0xFFFFFFFFu, in) >> (8u * g)) & 0xFFu;
+                    const bool mine = in && nsp + __popc(gb & ((1u << j) - 1u)) < 8u;
+                    const u32 attr = (spw >> 16) & 0xFFu, xx = spw >> 24;
+                    // the sprite's row (every lane, no branches: the address stays inside the pattern tables):
+                    // row tf of the sprite, vertical flip tf = h - 1 - t; rows 8-15 of an 8x16 sprite in its second tile
+                    const u32 tile = (spw >> 8) & 0xFFu;
+                    const u32 tf = (attr & 0x80u) ? hgt - 1u - t : t;
+                    const u32 vadr = (hgt == 16u ? ((tile & 1u) << 12) + ((tile & 0xFEu) << 4) : (tile << 4) + vofs) + tf + (tf & 8u);
+                    const u32 cwr = chr_sel(pages, vadr & 0x1FFFu);
+                    const u32 cw = mine ? ((attr & 0x40u) ? nib_reverse(cwr) : cwr) : 0u;
+                    const u32 om = nib_opaque8(cw);   // bit p: pixel p (screen x xx + p) is opaque; 0 unless mine
+                    // pixels of this sprite that a sprite of the round before it covers: the lanes of the group below
+                    // this one that hold a drawn sprite, one per trip (the trip count is the warp's largest number of
+                    // such lanes, mostly 0 or 1)
+                    const u32 info = (xx << 8) | om;
+                    u32 cov = 0;
+                    const u32 drawn = __ballot_sync(0xFFFFFFFFu, om != 0u);   // every lane (a full-warp vote)
+                    u32 below = om ? (drawn >> (8u * g)) & ((1u << j) - 1u) : 0u;
+                    const u32 kmax = __reduce_max_sync(0xFFFFFFFFu, __popc(below));
+                    for (u32 k = 0; k < kmax; ++k) {
+                        const u32 src = below ? static_cast<u32>(__ffs(below)) - 1u : j;
+                        below &= below - 1u;
+                        const u32 o = __shfl_sync(0xFFFFFFFFu, info, 8u * g + src);
+                        const int d = static_cast<int>(o >> 8) - static_cast<int>(xx);   // other sprite's pixel q = my q + d
+                        const u32 oq = src != j ? o & 0xFFu : 0u;
+                        if (d > -8 && d < 8) cov |= d >= 0 ? oq << d : oq >> -d;
                     }
+                    u32 wm = om & ~cov;
+                    if (xx < 8u) wm &= 0xFFu << (8u - xx);   // screen x < 8 is cropped
+                    if (wm) {
+                        const u32 sw = spal[attr & 3u];
+                        const u32 clo = __byte_perm(sw, 0u, cw) | 0x80808080u, chi = __byte_perm(sw, 0u, cw >> 16) | 0x80808080u;
+                        // byte masks of the visible pixels 0-3 and 4-7
+                        const u32 mlo = (((wm & 0xFu) * 0x00204081u) & 0x01010101u) * 0xFFu;
+                        const u32 mhi = ((((wm >> 4) & 0xFu) * 0x00204081u) & 0x01010101u) * 0xFFu;
+                        const u32 behm = (attr & 0x20u) ? 0xFFFFFFFFu : 0u;   // behind the background
+                        // the 8 pixels (bytes x8 .. x8 + 7 of the row) as the 3 row words w0 .. w0 + 2 they touch
+                        const int x8 = static_cast<int>(xx) - 8;
+                        const int w0 = x8 >> 2;   // -2 .. 61; words before the row hold only cropped pixels (mask 0)
+                        const u32 sh = 8u * (static_cast<u32>(x8) & 3u);
+                        const u32 cwd[3] = {clo << sh, __funnelshift_l(clo, chi, sh), __funnelshift_l(chi, 0u, sh)};
+                        const u32 mwd[3] = {mlo << sh, __funnelshift_l(mlo, mhi, sh), __funnelshift_l(mhi, 0u, sh)};
+                        u32* roww = reinterpret_cast<u32*>(rowb);
+#pragma unroll
+                        for (int k = 0; k < 3; ++k) {
+                            const int wi = w0 + k;
+                            if (mwd[k] != 0u && wi >= 0) {
+                                // bytes of this word no other lane of the round writes (claims are disjoint): read,
+                                // then change only them, by an xor, while other lanes may change the rest
+                                const u32 old = roww[wi];
+                                const u32 taken = prmt_signed(old, 0u, 0xBA98u);         // bit 7: an earlier round's
+                                const u32 bgop = prmt_signed(old << 1, 0u, 0xBA98u);     // bit 6: opaque background
+                                const u32 m = mwd[k] & ~taken;
+                                const u32 keep = m & bgop & behm;
+                                const u32 val = (cwd[k] & ~keep) | ((old | 0x80808080u) & keep);
+                                atomicXor(&roww[wi], (old ^ val) & m);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    nsp += __popc(gb);
                 }
-                if (a0 | a1 | a2 | a3) {
-                    const uint4 sp = F.spal[(F.rec[l - 1].y >> 20) & 3u];
-                    if (a0) { px[0] = sprite_mix(px[0], s0, n0, a0, b0, sp); px[1] = sprite_mix(px[1], s0 >> 16, n0 >> 16, a0 >> 16, b0 >> 16, sp); }
-                    if (a1) { px[2] = sprite_mix(px[2], s1, n1, a1, b1, sp); px[3] = sprite_mix(px[3], s1 >> 16, n1 >> 16, a1 >> 16, b1 >> 16, sp); }
-                    if (a2) { px[4] = sprite_mix(px[4], s2, n2, a2, b2, sp); px[5] = sprite_mix(px[5], s2 >> 16, n2 >> 16, a2 >> 16, b2 >> 16, sp); }
-                    if (a3) { px[6] = sprite_mix(px[6], s3, n3, a3, b3, sp); px[7] = sprite_mix(px[7], s3 >> 16, n3 >> 16, a3 >> 16, b3 >> 16, sp); }
-                }
+                px[0] = rw[0].x; px[1] = rw[0].y; px[2] = rw[0].z; px[3] = rw[0].w;
+                px[4] = rw[1].x; px[5] = rw[1].y; px[6] = rw[1].z; px[7] = rw[1].w;
             }
             if ((mask & 1u) && (mask & 0x18u)) {   // greyscale
 #pragma unroll
@@ -1130,13 +1152,13 @@ struct Renderer {
             if (exact) {
             } else if (!pack6) {
                 uint4* row = reinterpret_cast<uint4*>(obs_out + static_cast<u64>(y) * kObsW + 32u * j);
-                row[0] = make_uint4(px[0], px[1], px[2], px[3]);
-                if (j < 7) row[1] = make_uint4(px[4], px[5], px[6], px[7]);
+                row[0] = make_uint4(px[0] & 0x3F3F3F3Fu, px[1] & 0x3F3F3F3Fu, px[2] & 0x3F3F3F3Fu, px[3] & 0x3F3F3F3Fu);
+                if (j < 7) row[1] = make_uint4(px[4] & 0x3F3F3F3Fu, px[5] & 0x3F3F3F3Fu, px[6] & 0x3F3F3F3Fu, px[7] & 0x3F3F3F3Fu);
             } else {
+                // 6-bit groups (bits 6-7 of each byte are dropped by the packing), joined into words by byte permutes
                 u32 gq[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);   // px bytes are <= 0x3F
-                // the 3-byte groups joined into words: one byte permute per word (bytes 3 of the groups left out)
+                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);
                 u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3) + 24u * j);
                 row[0] = __byte_perm(gq[0], gq[1], 0x4210);
                 row[1] = __byte_perm(gq[1], gq[2], 0x5421);
@@ -1147,7 +1169,7 @@ struct Renderer {
                     row[5] = __byte_perm(gq[6], gq[7], 0x6542);
                 }
             }
-            __syncwarp();   // sbuf is rewritten by the next iteration
+            __syncwarp();   // the staging rows are rewritten by the next iteration
         }
         for (int i = lane; i < kObsH / 4; i += 32) {   // emphasis bits of the 224 drawn lines
             u32 e4 = 0;
