@@ -276,6 +276,7 @@ void launch_game(const Env& env, const Game& gm, bool start, cudaStream_t s, con
     R.count = n;
     R.frames = kFramesPerDecision;
     R.chrx_smem = gm.chrx_smem ? 1u : 0u;
+    R.one = 1u;
     const std::size_t smem = render_smem(gm.chrx_smem), seq_smem = render_seq_smem(gm.chrx_smem);
     KTimer& T = *env.timer;
     if (phases & kPhFrames) {

@@ -73,6 +73,7 @@ struct RenderArgs {
     u32 e0, count;       // global env range of this launch (game slice)
     u32 frames;          // frames per env to draw (4)
     u32 chrx_smem;       // 1: the cart's pattern table is staged in shared memory (8 KB CHR ROM boards)
+    u32 one;             // 1 (a run-time value: the kernels add disjoint bit fields as x * one + y, multiply-adds)
 };
 
 __device__ __forceinline__ u32 spread8(u32 b) {   // bit (7-k) of b -> bit 4k
@@ -113,8 +114,10 @@ __device__ __forceinline__ u32 prmt_signed(u32 a, u32 b, u32 s) {
 
 // The same lookup for palette bytes below 0x80 in two permutes: (p0, p1) serve the nibbles whose attribute bit 1 is
 // clear and read 0 where it is set; (p2, p3) take the nibbles with bit 3 flipped (sx = s ^ 0x8888), the other half.
-__device__ __forceinline__ u32 pal_lookup4s(u32 s, u32 sx, u32 p0, u32 p1, u32 p2, u32 p3) {
-    return prmt_signed(p0, p1, s) | prmt_signed(p2, p3, sx);
+// The halves have no bit in common, so they are joined by a multiply-add with `one` = 1 (a run-time value, so the
+// compiler keeps the multiply): the integer multiply-add pipe has twice the integer logic pipe's rate and is idle here.
+__device__ __forceinline__ u32 pal_lookup4s(u32 s, u32 sx, u32 p0, u32 p1, u32 p2, u32 p3, u32 one) {
+    return prmt_signed(p2, p3, sx) * one + prmt_signed(p0, p1, s);
 }
 
 // nibble mask (4 nibbles, each 0 or 0xF, low 16 bits) -> byte mask
@@ -948,14 +951,14 @@ struct Renderer {
         const u32 attr = (ab >> (f.ashift | (col & 2u))) & 3u;
         return t | (attr << 8);
     }
-    __device__ __forceinline__ u32 line_tile_sel(const LineFetch& f, u32 ta, const u32* pages) const {
+    __device__ __forceinline__ u32 line_tile_sel(u32 rowsel, u32 vrow, u32 ta, const u32* pages) const {
         const u32 t = ta & 0xFFu;
         u32 sel;
         if constexpr (BOARD == kNrom || BOARD == kUxrom) {
-            if (A.chrx_smem) sel = chrx[f.rowsel + t];
-            else sel = chr_sel(pages, (t << 4) + f.vrow);
+            if (A.chrx_smem) sel = chrx[rowsel + t];
+            else sel = chr_sel(pages, (t << 4) + vrow);
         } else {
-            sel = chr_sel(pages, (t << 4) + f.vrow);
+            sel = chr_sel(pages, (t << 4) + vrow);
         }
         // the attribute in bits 2-3 of every nibble (disjoint from the colour bits): one multiply-add
         return sel + (ta >> 8) * 0x44444444u;
@@ -1002,6 +1005,7 @@ struct Renderer {
             __syncwarp();
         }
         u32 key_prev = 0xFFFFFFFFu, ta0 = 0, ta1 = 0, ta2 = 0, ta3 = 0;   // this lane's cached tile row
+        const u32 one = A.one;
         for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
             const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;   // warp-uniform
             // ---- background of line l (this lane group's), 32 pixels per lane
@@ -1021,13 +1025,16 @@ struct Renderer {
             if (bg) {
                 const u32 ctrl = ((r.x >> 18) & 7u) << 3;
                 const u32* pages = F.chr[(r.y >> 12) & 3u];
-                const LineFetch lf = line_fetch_at(r.x & 0x7FFFu, ctrl, (r.x >> 21) & 0xFu);
-                if (fresh) {
+                if (fresh) {   // the tile row's nametable and attribute bytes
+                    const LineFetch lf = line_fetch_at(r.x & 0x7FFFu, ctrl, (r.x >> 21) & 0xFu);
                     ta0 = line_tile_ta(lf, 4 * j + 1); ta1 = line_tile_ta(lf, 4 * j + 2);
                     ta2 = line_tile_ta(lf, 4 * j + 3); ta3 = line_tile_ta(lf, 4 * j + 4);
                 }
-                c0 = line_tile_sel(lf, ta0, pages); c1 = line_tile_sel(lf, ta1, pages);
-                c2 = line_tile_sel(lf, ta2, pages); c3 = line_tile_sel(lf, ta3, pages);
+                // this line's pattern row: fine y and the background pattern table
+                const u32 fy = (r.x >> 12) & 7u;
+                const u32 rowsel = fy * 512u + ((ctrl & 0x10u) << 4), vrow = ((ctrl & 0x10u) << 8) | fy;
+                c0 = line_tile_sel(rowsel, vrow, ta0, pages); c1 = line_tile_sel(rowsel, vrow, ta1, pages);
+                c2 = line_tile_sel(rowsel, vrow, ta2, pages); c3 = line_tile_sel(rowsel, vrow, ta3, pages);
             }
             // fetch 4j + 5 is the next lane's first (a full-warp shuffle, outside the per-line branch); lane 7's last
             // 16 pixels (screen x 248-263) are not drawn
@@ -1041,10 +1048,10 @@ struct Renderer {
             u32 px[8];
             if (bg) {
                 const u32 x0 = s0 ^ 0x88888888u, x1 = s1 ^ 0x88888888u, x2 = s2 ^ 0x88888888u, x3 = s3 ^ 0x88888888u;
-                px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w); px[1] = pal_lookup4s(s0 >> 16, x0 >> 16, P.x, P.y, P.z, P.w);
-                px[2] = pal_lookup4s(s1, x1, P.x, P.y, P.z, P.w); px[3] = pal_lookup4s(s1 >> 16, x1 >> 16, P.x, P.y, P.z, P.w);
-                px[4] = pal_lookup4s(s2, x2, P.x, P.y, P.z, P.w); px[5] = pal_lookup4s(s2 >> 16, x2 >> 16, P.x, P.y, P.z, P.w);
-                px[6] = pal_lookup4s(s3, x3, P.x, P.y, P.z, P.w); px[7] = pal_lookup4s(s3 >> 16, x3 >> 16, P.x, P.y, P.z, P.w);
+                px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w, one); px[1] = pal_lookup4s(s0 >> 16, x0 >> 16, P.x, P.y, P.z, P.w, one);
+                px[2] = pal_lookup4s(s1, x1, P.x, P.y, P.z, P.w, one); px[3] = pal_lookup4s(s1 >> 16, x1 >> 16, P.x, P.y, P.z, P.w, one);
+                px[4] = pal_lookup4s(s2, x2, P.x, P.y, P.z, P.w, one); px[5] = pal_lookup4s(s2 >> 16, x2 >> 16, P.x, P.y, P.z, P.w, one);
+                px[6] = pal_lookup4s(s3, x3, P.x, P.y, P.z, P.w, one); px[7] = pal_lookup4s(s3 >> 16, x3 >> 16, P.x, P.y, P.z, P.w, one);
             } else {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) px[q] = bdw;
