@@ -866,6 +866,9 @@ struct RenderWarp {
     FrameWalk fw;
 };
 constexpr u32 kRenderWarps = 8;
+// Render blocks per SM the register budget is fitted to: 3 for the CHR-ROM boards whose draw path is lightest
+// (NROM, UxROM: <= 85 registers), 2 for the others (up to 128 registers)
+template <u32 BOARD> constexpr int render_min_blocks() { return (BOARD == kNrom || BOARD == kUxrom) ? 3 : 2; }
 inline std::size_t render_smem(bool chrx_smem) {
     return 1024 + (chrx_smem ? 16384 : 0) + kRenderWarps * sizeof(RenderWarp);
 }
@@ -893,7 +896,7 @@ __device__ __forceinline__ void render_setup(const RenderArgs& R, u8* smem, u32*
 }
 
 template <u32 BOARD>
-__global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render(const __grid_constant__ RenderArgs R) {
+__global__ void __launch_bounds__(32 * kRenderWarps, render_min_blocks<BOARD>()) k_render(const __grid_constant__ RenderArgs R) {
     extern __shared__ __align__(16) u8 smem[];
     u32 *spread, *chrx;
     render_setup<BOARD>(R, smem, spread, chrx);

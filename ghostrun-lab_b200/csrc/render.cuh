@@ -124,11 +124,14 @@ __device__ __forceinline__ u32 pal_lookup4s(u32 s, u32 sx, u32 p0, u32 p1, u32 p
 __device__ __forceinline__ u32 nib_to_bytes(u32 nm16) { return __byte_perm(0u, 0xFFFFFFFFu, nm16 & 0x4444u); }
 
 
-// 4 colour numbers (bytes <= 0x3F) -> their 24-bit 6-bit group in bits 0-23 (rl/csrc/rlenv.cu:126-134 layout) with
-// leftovers in bits 24-25, which the joins of groups into words mask off: two shift + merge steps.
-__device__ __forceinline__ u32 pack_group6_loose(u32 w) {
-    const u32 u = w ^ ((w ^ (w >> 2)) & 0x0FC00FC0u);   // c0 | c1 << 6 in bits 0-11, c2 | c3 << 6 in bits 16-27
-    return u ^ ((u ^ (u >> 4)) & 0xFFFFF000u);           // bits 16-27 down to 12-23
+// 4 colour numbers (bits 0-5 of each byte; bits 6-7 are ignored) -> their 24-bit 6-bit group in bits 0-23
+// (rl/csrc/rlenv.cu:126-134 layout) with leftovers in bits 24-31, which the joins of groups into words leave out: two
+// shift + merge steps. The right shifts are high halves of multiplies by m30 = 1 << 30 and m28 = 1 << 28 (run-time
+// values, so the compiler keeps the multiplies): x >> k = (x * 2^(32-k)) >> 32 runs on the integer multiply-add pipe,
+// which the renderer leaves mostly idle, instead of the integer logic pipe that bounds it.
+__device__ __forceinline__ u32 pack_group6_loose(u32 w, u32 m30, u32 m28) {
+    const u32 u = w ^ ((w ^ __umulhi(w, m30)) & 0x0FC00FC0u);   // c0 | c1 << 6 in bits 0-11, c2 | c3 << 6 in 16-27
+    return u ^ ((u ^ __umulhi(u, m28)) & 0xFFFFF000u);           // bits 16-27 down to 12-23
 }
 
 // 4 colour numbers (bytes) -> one 24-bit 6-bit group (rl/csrc/rlenv.cu:126-134 layout)
@@ -940,19 +943,18 @@ struct Renderer {
         f.vrow = ((ctrl & 0x10u) << 8) | fy;
         return f;
     }
-    // Fetch c of a line in two parts: the nametable's tile and attribute (the same for the 8 lines of a tile row) as
-    // tile | attr << 8, then the pattern row of this line as colour nibbles with the attribute in bits 2-3.
-    __device__ __forceinline__ u32 line_tile_ta(const LineFetch& f, u32 c) const {
+    // Fetch c of a line in two parts: the nametable's tile t and attribute (the same for the 8 lines of a tile row; the
+    // attribute as aw = attr * 0x44444444, its bits 2-3 in every nibble), then the pattern row of this line as colour
+    // nibbles with the attribute added (disjoint bits: one multiply-add with `one` = 1).
+    __device__ __forceinline__ void line_tile_ta(const LineFetch& f, u32 c, u32& t, u32& aw) const {
         const u32 cc = f.cx0 + c;
         const u32 col = cc & 31u;
         const u32 base = ((cc >> 5) & 1u) ? f.base_b : f.base_a;
-        const u32 t = W.nt[base | f.row | col];
+        t = W.nt[base | f.row | col];
         const u32 ab = W.nt[base | f.arow | (col >> 2)];
-        const u32 attr = (ab >> (f.ashift | (col & 2u))) & 3u;
-        return t | (attr << 8);
+        aw = ((ab >> (f.ashift | (col & 2u))) & 3u) * 0x44444444u;
     }
-    __device__ __forceinline__ u32 line_tile_sel(u32 rowsel, u32 vrow, u32 ta, const u32* pages) const {
-        const u32 t = ta & 0xFFu;
+    __device__ __forceinline__ u32 line_tile_sel(u32 rowsel, u32 vrow, u32 t, u32 aw, const u32* pages, u32 one) const {
         u32 sel;
         if constexpr (BOARD == kNrom || BOARD == kUxrom) {
             if (A.chrx_smem) sel = chrx[rowsel + t];
@@ -960,8 +962,7 @@ struct Renderer {
         } else {
             sel = chr_sel(pages, (t << 4) + vrow);
         }
-        // the attribute in bits 2-3 of every nibble (disjoint from the colour bits): one multiply-add
-        return sel + (ta >> 8) * 0x44444444u;
+        return sel * one + aw;
     }
 
     // ---- phase 2 (the whole warp): draw frame f of env ge from its walk, 4 lines at a time: lane group g = lane / 8
@@ -1004,8 +1005,9 @@ struct Renderer {
             nv = __popc(ba) + __popc(bb);
             __syncwarp();
         }
-        u32 key_prev = 0xFFFFFFFFu, ta0 = 0, ta1 = 0, ta2 = 0, ta3 = 0;   // this lane's cached tile row
-        const u32 one = A.one;
+        u32 key_prev = 0xFFFFFFFFu;   // this lane's cached tile row: tiles t0-t3, attributes aw0-aw3
+        u32 t0 = 0, t1 = 0, t2 = 0, t3 = 0, aw0 = 0, aw1 = 0, aw2 = 0, aw3 = 0;
+        const u32 one = A.one, m16 = one << 16, m28 = one << 28, m30 = one << 30;   // see pack_group6_loose
         for (int l0 = kObsY0; l0 < kObsY0 + kObsH; l0 += 4) {
             const bool any = ((may[l0 >> 5] >> (l0 & 31)) & 0xFu) != 0;   // warp-uniform
             // ---- background of line l (this lane group's), 32 pixels per lane
@@ -1027,14 +1029,14 @@ struct Renderer {
                 const u32* pages = F.chr[(r.y >> 12) & 3u];
                 if (fresh) {   // the tile row's nametable and attribute bytes
                     const LineFetch lf = line_fetch_at(r.x & 0x7FFFu, ctrl, (r.x >> 21) & 0xFu);
-                    ta0 = line_tile_ta(lf, 4 * j + 1); ta1 = line_tile_ta(lf, 4 * j + 2);
-                    ta2 = line_tile_ta(lf, 4 * j + 3); ta3 = line_tile_ta(lf, 4 * j + 4);
+                    line_tile_ta(lf, 4 * j + 1, t0, aw0); line_tile_ta(lf, 4 * j + 2, t1, aw1);
+                    line_tile_ta(lf, 4 * j + 3, t2, aw2); line_tile_ta(lf, 4 * j + 4, t3, aw3);
                 }
                 // this line's pattern row: fine y and the background pattern table
                 const u32 fy = (r.x >> 12) & 7u;
                 const u32 rowsel = fy * 512u + ((ctrl & 0x10u) << 4), vrow = ((ctrl & 0x10u) << 8) | fy;
-                c0 = line_tile_sel(rowsel, vrow, ta0, pages); c1 = line_tile_sel(rowsel, vrow, ta1, pages);
-                c2 = line_tile_sel(rowsel, vrow, ta2, pages); c3 = line_tile_sel(rowsel, vrow, ta3, pages);
+                c0 = line_tile_sel(rowsel, vrow, t0, aw0, pages, one); c1 = line_tile_sel(rowsel, vrow, t1, aw1, pages, one);
+                c2 = line_tile_sel(rowsel, vrow, t2, aw2, pages, one); c3 = line_tile_sel(rowsel, vrow, t3, aw3, pages, one);
             }
             // fetch 4j + 5 is the next lane's first (a full-warp shuffle, outside the per-line branch); lane 7's last
             // 16 pixels (screen x 248-263) are not drawn
@@ -1048,10 +1050,10 @@ struct Renderer {
             u32 px[8];
             if (bg) {
                 const u32 x0 = s0 ^ 0x88888888u, x1 = s1 ^ 0x88888888u, x2 = s2 ^ 0x88888888u, x3 = s3 ^ 0x88888888u;
-                px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w, one); px[1] = pal_lookup4s(s0 >> 16, x0 >> 16, P.x, P.y, P.z, P.w, one);
-                px[2] = pal_lookup4s(s1, x1, P.x, P.y, P.z, P.w, one); px[3] = pal_lookup4s(s1 >> 16, x1 >> 16, P.x, P.y, P.z, P.w, one);
-                px[4] = pal_lookup4s(s2, x2, P.x, P.y, P.z, P.w, one); px[5] = pal_lookup4s(s2 >> 16, x2 >> 16, P.x, P.y, P.z, P.w, one);
-                px[6] = pal_lookup4s(s3, x3, P.x, P.y, P.z, P.w, one); px[7] = pal_lookup4s(s3 >> 16, x3 >> 16, P.x, P.y, P.z, P.w, one);
+                px[0] = pal_lookup4s(s0, x0, P.x, P.y, P.z, P.w, one); px[1] = pal_lookup4s(__umulhi(s0, m16), __umulhi(x0, m16), P.x, P.y, P.z, P.w, one);
+                px[2] = pal_lookup4s(s1, x1, P.x, P.y, P.z, P.w, one); px[3] = pal_lookup4s(__umulhi(s1, m16), __umulhi(x1, m16), P.x, P.y, P.z, P.w, one);
+                px[4] = pal_lookup4s(s2, x2, P.x, P.y, P.z, P.w, one); px[5] = pal_lookup4s(__umulhi(s2, m16), __umulhi(x2, m16), P.x, P.y, P.z, P.w, one);
+                px[6] = pal_lookup4s(s3, x3, P.x, P.y, P.z, P.w, one); px[7] = pal_lookup4s(__umulhi(s3, m16), __umulhi(x3, m16), P.x, P.y, P.z, P.w, one);
             } else {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) px[q] = bdw;
@@ -1165,7 +1167,7 @@ struct Renderer {
                 // 6-bit groups (bits 6-7 of each byte are dropped by the packing), joined into words by byte permutes
                 u32 gq[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q]);
+                for (int q = 0; q < 8; ++q) gq[q] = pack_group6_loose(px[q], m30, m28);
                 u32* row = reinterpret_cast<u32*>(obs_out + static_cast<u64>(y) * (kObsW / 4 * 3) + 24u * j);
                 row[0] = __byte_perm(gq[0], gq[1], 0x4210);
                 row[1] = __byte_perm(gq[1], gq[2], 0x5421);
