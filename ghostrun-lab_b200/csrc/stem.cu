@@ -119,10 +119,12 @@ __device__ __forceinline__ void rows_store(const RowLoad<PACKED>& L, uint32_t* r
 }
 
 // Half of a pixel's A row (picture rows q0..q0+3: 8 input pixels, 16 words) from the staged rows: two palette
-// lookups per picture row, each (R | G << 16, B | 1.0 << 16).
+// lookups per picture row, each (R | G << 16, B | 1.0 << 16) from two 4-byte tables. A picture row has one emphasis
+// for the whole block, so its lookups fall in one 64-entry slice: as 4-byte words that slice puts at most 2 colours
+// on a shared-memory bank (as 8-byte entries, 4 colours shared a bank pair).
 template <bool PACKED>
-__device__ __forceinline__ void build_half(const uint32_t* rb, const uint32_t* eb, const uint2* pal, int q0,
-                                           uint32_t wi, uint32_t sh, uint32_t* x) {
+__device__ __forceinline__ void build_half(const uint32_t* rb, const uint32_t* eb, const uint32_t* pal_rg,
+                                           const uint32_t* pal_b1, int q0, uint32_t wi, uint32_t sh, uint32_t* x) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int q = q0 + j;
@@ -137,11 +139,11 @@ __device__ __forceinline__ void build_half(const uint32_t* rb, const uint32_t* e
             c1 = (v >> 8) & 63u;
         }
         const uint32_t e = eb[q];
-        const uint2 p0 = pal[c0 | e], p1 = pal[c1 | e];
-        x[4 * j] = p0.x;
-        x[4 * j + 1] = p0.y;
-        x[4 * j + 2] = p1.x;
-        x[4 * j + 3] = p1.y;
+        const uint32_t i0 = c0 | e, i1 = c1 | e;
+        x[4 * j] = pal_rg[i0];
+        x[4 * j + 1] = pal_b1[i0];
+        x[4 * j + 2] = pal_rg[i1];
+        x[4 * j + 3] = pal_b1[i1];
     }
 }
 
@@ -168,7 +170,8 @@ __device__ __forceinline__ uint32_t mbar_wait(uint32_t addr, uint32_t parity) {
 template <bool PACKED>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stem_fwd(const __grid_constant__ StemArgs a) {
     __shared__ __align__(128) uint8_t sB[kN * kKp * 2];   // 2 KB: permuted weights + bias
-    __shared__ __align__(16) uint2 sPal[512];             // 4 KB
+    __shared__ __align__(16) uint32_t sPalRG[512];       // 2 KB: R | G << 16
+    __shared__ __align__(16) uint32_t sPalB1[512];       // 2 KB: B | 1.0 << 16
     __shared__ __align__(16) uint32_t sRow[2][8 * 64];    // 2 x 2 KB: a tile's 8 picture rows
     __shared__ __align__(16) uint32_t sEmph[2][8];
     __shared__ __align__(8) uint64_t mbar;
@@ -177,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stem_fwd(const __grid_
 
     for (int i = tid; i < 512; i += kThreads) {
         const uint2 v = reinterpret_cast<const uint2*>(a.pal)[i];
-        sPal[i] = make_uint2(v.x, (v.y & 0xFFFFu) | (kOneBf16 << 16));   // R | G << 16, B | 1.0 << 16
+        sPalRG[i] = v.x;                                   // R | G << 16
+        sPalB1[i] = (v.y & 0xFFFFu) | (kOneBf16 << 16);    // B | 1.0 << 16
     }
     for (int i = tid; i < kN * kKp; i += kThreads) {   // permuted weights into the core-matrix layout (row n = channel)
         const int n = i / kKp, kp = i % kKp, pos = kp >> 2, c = kp & 3;
@@ -226,9 +230,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) k_stem_fwd(const __grid_
         if (it > 0) ok = mbar_wait(bar, phase);   // tile i-1's MMAs (they read A and wrote the accumulator)
         if (have && ok) {
             uint32_t x[16];
-            build_half<PACKED>(sRow[buf], sEmph[buf], sPal, 0, wi, sh, x);
+            build_half<PACKED>(sRow[buf], sEmph[buf], sPalRG, sPalB1, 0, wi, sh, x);
             tmem_st16(lane_a, x);
-            build_half<PACKED>(sRow[buf], sEmph[buf], sPal, 4, wi, sh, x);
+            build_half<PACKED>(sRow[buf], sEmph[buf], sPalRG, sPalB1, 4, wi, sh, x);
             tmem_st16(lane_a + 16, x);
         }
         if (it > 0) {
@@ -324,7 +328,8 @@ __global__ void __launch_bounds__(kThreads) k_stem_bwd(const __grid_constant__ S
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* sA = smem;                                                    // [2][kBwdA]
     uint8_t* sB = smem + 2 * kBwdA;                                        // [2][kBwdB]
-    uint2* sPal = reinterpret_cast<uint2*>(sB + 2 * kBwdB);                // [512]
+    uint32_t* sPalRG = reinterpret_cast<uint32_t*>(sB + 2 * kBwdB);        // [512] R | G << 16
+    uint32_t* sPalB1 = sPalRG + 512;                                       // [512] B | 1.0 << 16
     uint32_t* sRow = reinterpret_cast<uint32_t*>(sB + 2 * kBwdB + 4096);   // [2][8 * 64]
     uint32_t* sEmph = sRow + 2 * 8 * 64;                                   // [2][8]
     __shared__ __align__(8) uint64_t mbar[2];
@@ -333,7 +338,8 @@ __global__ void __launch_bounds__(kThreads) k_stem_bwd(const __grid_constant__ S
 
     for (int i = tid; i < 512; i += kThreads) {
         const uint2 v = reinterpret_cast<const uint2*>(a.pal)[i];
-        sPal[i] = make_uint2(v.x, (v.y & 0xFFFFu) | (kOneBf16 << 16));
+        sPalRG[i] = v.x;
+        sPalB1[i] = (v.y & 0xFFFFu) | (kOneBf16 << 16);
     }
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(&mbar[0])));
@@ -386,11 +392,11 @@ __global__ void __launch_bounds__(kThreads) k_stem_bwd(const __grid_constant__ S
         if (ok) {
             uint8_t* A = sA + buf * kBwdA;
             uint32_t x[16];
-            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPal, 0, wi, sh, x);
+            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPalRG, sPalB1, 0, wi, sh, x);
 #pragma unroll
             for (int c = 0; c < 4; ++c)
                 *reinterpret_cast<uint4*>(A + c * kBwdChunk + cm) = make_uint4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
-            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPal, 4, wi, sh, x);
+            build_half<PACKED>(sRow + buf * 8 * 64, sEmph + buf * 8, sPalRG, sPalB1, 4, wi, sh, x);
 #pragma unroll
             for (int c = 0; c < 4; ++c)
                 *reinterpret_cast<uint4*>(A + (4 + c) * kBwdChunk + cm) = make_uint4(x[4 * c], x[4 * c + 1], x[4 * c + 2], x[4 * c + 3]);
