@@ -866,6 +866,7 @@ struct RenderWarp {
     FrameWalk fw;
 };
 constexpr u32 kRenderWarps = 8;
+static_assert((kRenderWarps & (kRenderWarps - 1u)) == 0u, "k_render_seq's item scan takes kRenderWarps as a power of two");
 // Render blocks per SM the register budget is fitted to: 3 for the CHR-ROM boards whose draw path is lightest
 // (NROM, UxROM: <= 85 registers), 2 for the others (up to 128 registers)
 template <u32 BOARD> constexpr int render_min_blocks() { return (BOARD == kNrom || BOARD == kUxrom) ? 3 : 2; }
@@ -932,6 +933,18 @@ __global__ void __launch_bounds__(32 * kRenderWarps, render_min_blocks<BOARD>())
 template <u32 BOARD>
 __global__ void __launch_bounds__(32 * kRenderWarps, 2) k_render_seq(const __grid_constant__ RenderArgs R) {
     extern __shared__ __align__(16) u8 smem[];
+    {   // most launches find no flagged frame: the block's items are scanned by all its threads first, and a block
+        // with none returns before staging its tables (the same items as the warp loop below, 32 per warp at once)
+        const u32 items = (R.list ? *R.list_count : R.count) * R.frames;
+        const u32 step = gridDim.x * kRenderWarps;
+        bool found = false;
+        for (u32 k = blockIdx.x * kRenderWarps + (threadIdx.x & (kRenderWarps - 1u)) + (threadIdx.x / kRenderWarps) * step;
+             k < items; k += 32u * step) {
+            u32 ge, f;
+            if (render_item(R, k, ge, f) && R.seqf[static_cast<u64>(ge) * 4 + f]) found = true;
+        }
+        if (!__syncthreads_or(found)) return;
+    }
     u32 *spread, *chrx;
     render_setup<BOARD>(R, smem, spread, chrx);
     RWarp* warps = reinterpret_cast<RWarp*>(smem + 1024 + (R.chrx_smem ? 16384 : 0));
